@@ -1,0 +1,473 @@
+"""Benchmark of the B200 quantized-weight path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Workloads (seeded synthetic inputs with the configs' shapes and value distributions):
+  sweep    (default) configs[1]: GGUF Q4_K -> bf16 dequantisation of a Cosmos-Predict2-14B checkpoint, sharded by
+           tensor with no communication. Weak scaling: at N GPUs the tensor table is N x 36 blocks, bin-packed by
+           bytes over the ranks, so every rank sweeps 36 blocks (14.16 G values, 7.96 GB in, 28.31 GB out) per
+           step through one batched launch (wf_dequant_gguf_batch). Inputs are larger than L2, so no flush.
+  q8       configs[0]: Q8_0 5120x5120 -> bf16 (one launch per step; L2 flushed between steps).
+  q4k      configs[1]'s single FFN weight, Q4_K 5120x13824 -> bf16 (one launch per step; L2 flushed).
+Metric: GGUF dequant output GB/s (bf16 bytes written per second, all ranks). `e2e` is the same metric through the
+reference-facing entry point (gguf_dequant.dequantize) with pinned host buffers: every step copies the packed
+bytes host -> device, dequantises and copies the bf16 weight device -> host, for one block's 16 tensors.
+--impl reference times the reference's algorithm on the host cores instead (the C restatement in oracle/, all
+threads; there is no other CPU implementation of the path), on a bounded sample of the same workload.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from the ncu captures summarised in
+# profiles/ (None until captured). Keyed by workload; scaled to the bench's launch as described in the profile.
+NCU_TRAFFIC = {"sweep": None, "q8": None, "q4k": None}
+
+Q4K_TS, Q8_TS = 144, 34
+
+
+def _pkg(mod):
+    import importlib
+    return importlib.import_module("comfyui-weightferry_b200." + mod)
+
+
+# ----------------------------------------------------------------------------------------------------- workloads
+def cosmos14b_block_shapes():
+    """The 2-D weights of one Cosmos-Predict2-14B block (hidden 5120, 40 heads x 128, MLP 20480, cross-attention
+    context 1024, adaLN-LoRA 256): 16 tensors, 393,216,000 values."""
+    h, mlp, ctx, lora = 5120, 20480, 1024, 256
+    shapes = [(h, h)] * 4                       # self-attention q, k, v, o
+    shapes += [(h, h), (h, h), (h, ctx), (h, ctx)]  # cross-attention q, o, k, v
+    shapes += [(mlp, h), (h, mlp)]              # MLP layer1, layer2
+    for _ in range(3):                          # adaLN modulation (self-attn, cross-attn, MLP): LoRA down + up
+        shapes += [(lora, h), (3 * h, lora)]
+    return shapes
+
+
+def bin_pack(sizes, n_bins):
+    """Greedy largest-first assignment of items to the least-loaded bin; returns the item indices per bin."""
+    order = sorted(range(len(sizes)), key=lambda i: -sizes[i])
+    loads = [0] * n_bins
+    bins = [[] for _ in range(n_bins)]
+    for i in order:
+        b = min(range(n_bins), key=lambda j: loads[j])
+        bins[b].append(i)
+        loads[b] += sizes[i]
+    return bins
+
+
+def fill_q4k(torch, n_blocks, device, gen):
+    """Packed Q4_K super-blocks as BASELINE configs[1]: random bytes, d and dmin float16 U(0, 0.01)."""
+    raw = torch.randint(0, 256, (n_blocks, Q4K_TS), dtype=torch.uint8, device=device, generator=gen)
+    dd = (torch.rand((n_blocks, 2), device=device, generator=gen) * 0.01).half()
+    raw[:, 0:4] = dd.view(torch.uint8)
+    return raw.reshape(-1)
+
+
+def fill_q8(torch, n_blocks, device, gen):
+    """Packed Q8_0 blocks as BASELINE configs[0]: int8 quants uniform in [-127, 127], d = fp16(|N(0,1)| * 0.002)."""
+    q = torch.randint(-127, 128, (n_blocks, 32), dtype=torch.int16, device=device, generator=gen).to(torch.int8)
+    d = (torch.randn((n_blocks, 1), device=device, generator=gen).abs() * 0.002).half()
+    return torch.cat([d.view(torch.uint8), q.view(torch.uint8)], dim=1).reshape(-1)
+
+
+# ----------------------------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------------------------------- helpers
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def setup_dist(torch):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local, dist
+
+
+def max_over_ranks(torch, dist, value):
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(torch, dist, value):
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(torch, dist):
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ----------------------------------------------------------------------------------------------------- CPU baseline
+def cpu_baseline_sweep(seconds=10.0):
+    """The oracle port (oracle/wf_oracle.c, OpenMP, all host threads) on one BASELINE configs[1] weight, Q4_K
+    5120x13824 -> bf16 (mid float16), repeated for about `seconds`. Returns (out GB/s, threads, sample text)."""
+    from oracle import oracle
+    rng = np.random.default_rng(20261201 + 1)
+    n = 5120 * 13824
+    nb = n // 256
+    raw = rng.integers(0, 256, size=(nb, Q4K_TS), dtype=np.uint8)
+    raw[:, 0:4] = (rng.uniform(0, 0.01, (nb, 2)).astype(np.float16)).view(np.uint8)
+    threads = oracle.max_threads()
+    oracle.dequant_gguf(raw, n, 12, 0, 1)  # warm-up (page faults, thread pool)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.dequant_gguf(raw, n, 12, 0, 1)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    gbs = reps * n * 2 / el / 1e9
+    return gbs, threads, f"Q4_K 5120x13824 -> bf16 (mid f16), {reps} reps in {el:.1f} s"
+
+
+# ----------------------------------------------------------------------------------------------------- our arm
+def run_sweep(torch, args, world, rank, dist):
+    gd = _pkg("enhancers.gguf_dequant")
+    ext = _pkg("_ext")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    shapes = cosmos14b_block_shapes()
+    table = [s for _ in range(36 * world) for s in shapes]        # N x 36 blocks
+    sizes = [a * b for a, b in table]
+    mine = bin_pack(sizes, world)[rank]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(20261201 + 1 + rank)
+    srcs, dsts = [], []
+    tasks = (ext.DequantTask * len(mine))()
+    n_values = 0
+    for k, i in enumerate(mine):
+        a, b = table[i]
+        n = a * b
+        src = fill_q4k(torch, n // 256, dev, gen)
+        dst = torch.empty((a, b), dtype=torch.bfloat16, device=dev)
+        srcs.append(src)
+        dsts.append(dst)
+        tasks[k].src, tasks[k].dst, tasks[k].n_values = src.data_ptr(), dst.data_ptr(), n
+        n_values += n
+    in_bytes = sum(s.numel() for s in srcs)
+    out_bytes = n_values * 2
+    lib = ext.lib()
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        rc = lib.wf_dequant_gguf_batch(tasks, len(mine), 12, 0, 1, stream.cuda_stream)
+        if rc:
+            ext.check(rc, "wf_dequant_gguf_batch")
+
+    launches_per_step = -(-len(mine) // 640)
+    for _ in range(args.warmup):
+        step()
+    barrier(torch, dist)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        barrier(torch, dist)
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for s in range(args.steps):
+            ev[s][0].record(stream)
+            step()
+            ev[s][1].record(stream)
+        t_end.record(stream)
+        barrier(torch, dist)
+    total_ms = max_over_ranks(torch, dist, t_start.elapsed_time(t_end))
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)  # one batched launch per step (per table)
+    total_out = sum_over_ranks(torch, dist, out_bytes * args.steps)
+    value = total_out / (total_ms / 1e3) / 1e9
+    del srcs, dsts
+    torch.cuda.empty_cache()
+    e2e = e2e_block(torch, gd, dev, args)
+    e2e_v = sum_over_ranks(torch, dist, e2e["value"])
+    e2e["value"] = round(e2e_v, 2)
+    launches = int(sum_over_ranks(torch, dist, launches_per_step * args.steps))
+    return {
+        "value": value, "ms_per_step": total_ms / args.steps, "kern_ms": kern_ms,
+        "alg_bytes_per_launch": (in_bytes + out_bytes) / launches_per_step, "clk": clk.summary(), "e2e": e2e,
+        "gpu_launches": launches,
+        "config": {"workload": "GGUF Q4_K -> bf16 sweep of a Cosmos-Predict2-14B checkpoint (configs[1])",
+                   "blocks_per_rank": 36, "tensors_per_rank": len(mine), "values_per_rank": n_values,
+                   "in_bytes_per_rank": in_bytes, "out_bytes_per_rank": out_bytes, "mid_dtype": "f16",
+                   "sharding": "by tensor, greedy bin-pack of an N x 36-block table, no communication",
+                   "l2": "inputs larger than L2 (36 GB per rank per step); no flush"},
+    }
+
+
+def e2e_block(torch, gd, dev, args):
+    """gguf_dequant.dequantize on one block's 16 Q4_K tensors with pinned host buffers: per step H2D of the packed
+    bytes, the dequantisation, D2H of the bf16 weights (two streams, so one tensor's copies overlap another's
+    dequantisation)."""
+    shapes = cosmos14b_block_shapes()
+    gen = torch.Generator()
+    gen.manual_seed(20261201 + 11)
+    hosts, houts, dsrc = [], [], []
+    for a, b in shapes:
+        raw = torch.randint(0, 256, (a * b // 256, Q4K_TS), dtype=torch.uint8, generator=gen)
+        raw[:, 0:4] = (torch.rand((a * b // 256, 2), generator=gen) * 0.01).half().view(torch.uint8)
+        hosts.append(raw.reshape(-1).pin_memory())
+        houts.append(torch.empty((a, b), dtype=torch.bfloat16).pin_memory())
+        dsrc.append(torch.empty(raw.numel(), dtype=torch.uint8, device=dev))
+    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    h2d = sum(h.numel() for h in hosts)
+    d2h = sum(h.numel() * 2 for h in houts)
+
+    def step():
+        for i, ((a, b), h) in enumerate(zip(shapes, hosts)):
+            s = streams[i % 2]
+            with torch.cuda.stream(s):
+                dsrc[i].copy_(h, non_blocking=True)
+                w = gd.dequantize(dsrc[i], 12, (a, b), None, torch.bfloat16)
+                houts[i].copy_(w, non_blocking=True)
+                w.record_stream(s)
+        for s in streams:
+            torch.cuda.current_stream(dev).wait_stream(s)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(3, args.steps // 2)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    return {"value": d2h / (ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": round(ms, 3), "sample": "one Cosmos-14B block (16 Q4_K tensors) per step"}
+
+
+def run_single_weight(torch, args, world, rank, dist, which):
+    """configs[0] (Q8_0 5120x5120) or configs[1]'s weight (Q4_K 5120x13824): one launch per step, L2 flushed."""
+    gd = _pkg("enhancers.gguf_dequant")
+    ext = _pkg("_ext")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev)
+    if which == "q8":
+        shape, qt, ts, vpb = (5120, 5120), 8, Q8_TS, 32
+        gen.manual_seed(20261201 + 0 + rank)
+        src = fill_q8(torch, shape[0] * shape[1] // 32, dev, gen)
+    else:
+        shape, qt, ts, vpb = (5120, 13824), 12, Q4K_TS, 256
+        gen.manual_seed(20261201 + 1 + rank)
+        src = fill_q4k(torch, shape[0] * shape[1] // 256, dev, gen)
+    n = shape[0] * shape[1]
+    dst = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)  # 512 MB > 126 MB L2
+    lib = ext.lib()
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        rc = lib.wf_dequant_gguf(src.data_ptr(), src.numel(), dst.data_ptr(), n, qt, 0, 1, stream.cuda_stream)
+        if rc:
+            ext.check(rc, "wf_dequant_gguf")
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    barrier(torch, dist)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        barrier(torch, dist)
+        for s in range(args.steps):
+            flush.zero_()
+            ev[s][0].record(stream)
+            step()
+            ev[s][1].record(stream)
+        barrier(torch, dist)
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    ms = max_over_ranks(torch, dist, kern_ms)
+    out_bytes = n * 2
+    value = sum_over_ranks(torch, dist, out_bytes / (ms / 1e3) / 1e9)
+    return {
+        "value": value, "ms_per_step": ms, "kern_ms": kern_ms, "alg_bytes_per_launch": src.numel() + out_bytes,
+        "clk": clk.summary(), "e2e": None, "gpu_launches": int(sum_over_ranks(torch, dist, args.steps)),
+        "config": {"workload": f"GGUF {'Q8_0' if qt == 8 else 'Q4_K'} {shape[0]}x{shape[1]} -> bf16 (one weight)",
+                   "mid_dtype": "f16", "l2": "flushed (512 MB write) before every timed launch",
+                   "timing": "sum of per-launch CUDA-event durations"},
+    }
+
+
+# ----------------------------------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "q8", "q4k"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    world, rank, local, dist = setup_dist(torch)
+    if args.workload == "sweep":
+        r = run_sweep(torch, args, world, rank, dist)
+    else:
+        r = run_single_weight(torch, args, world, rank, dist, args.workload)
+    peak, peak_kind = measured_peaks()
+    achieved = r["alg_bytes_per_launch"] / (r["kern_ms"] / 1e3) / 1e9
+    traffic = NCU_TRAFFIC.get(args.workload)
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline and args.workload in ("sweep", "q4k"):
+        gbs, threads, sample = cpu_baseline_sweep(args.cpu_seconds)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample}
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": "GGUF dequant out GB/s", "value": round(r["value"], 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8->bf16 (f32 math)",
+            "data": "synthetic (seeded, BASELINE configs distributions)", "config": r["config"],
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                         "kernel": "dequant_kernel<12,f16,bf16> (batched)" if args.workload == "sweep"
+                         else "dequant_kernel (single weight)"},
+            "cpu_baseline": cpu, "e2e": r["e2e"], "gpu_launches": r["gpu_launches"], "clocks": r["clk"],
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The reference arm: the reference's dequantisation arithmetic on the host cores (oracle port, OpenMP, all
+    threads) on the same metric / config; rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle
+    shapes = cosmos14b_block_shapes()
+    # bounded sample: 4 of the block's tensors (one of each kind) per step
+    sample = [shapes[0], shapes[6], shapes[8], shapes[11]]
+    rng = np.random.default_rng(20261201 + 1)
+    raws = []
+    for a, b in sample:
+        nb = a * b // 256
+        raw = rng.integers(0, 256, size=(nb, Q4K_TS), dtype=np.uint8)
+        raw[:, 0:4] = (rng.uniform(0, 0.01, (nb, 2)).astype(np.float16)).view(np.uint8)
+        raws.append((raw, a * b))
+    threads = oracle.max_threads()
+
+    def step():
+        for raw, n in raws:
+            oracle.dequant_gguf(raw, n, 12, 0, 1)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    out_bytes = sum(n for _r, n in raws) * 2 * args.steps
+    v = out_bytes / el / 1e9
+    desc = "Q4_K -> bf16 (mid f16) of 4 Cosmos-14B block tensors (5120x5120, 5120x1024, 20480x5120, 15360x256)"
+    print(json.dumps({
+        "impl": "reference", "metric": "GGUF dequant out GB/s", "value": round(v, 3), "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8->bf16 (f32 math)", "data": "synthetic (seeded)",
+        "config": {"workload": "GGUF Q4_K -> bf16 sweep (configs[1]), bounded CPU sample per step"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+if __name__ == "__main__":
+    main()

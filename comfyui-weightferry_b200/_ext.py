@@ -1,0 +1,104 @@
+"""ctypes binding of the C-ABI library (include/weightferry_b200.h, built by csrc/build.py into _lib/).
+
+There is no CPU fallback: a missing library raises ExtensionMissing, a rejected call raises WFError with the
+library's status string. Every launch takes the caller's current CUDA stream, as the reference's kernels do
+(enhancers/fused_int8.py:151 passes torch.cuda.current_stream(dev).cuda_stream)."""
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_lib", "libweightferry_b200.so")
+
+WF_F16, WF_BF16, WF_F32 = 0, 1, 2
+
+_lock = threading.Lock()
+_lib = None
+
+
+class ExtensionMissing(RuntimeError):
+    """The CUDA library is not built (run __graft_entry__.build() or comfyui-weightferry_b200/csrc/build.py)."""
+
+
+class WFError(RuntimeError):
+    def __init__(self, status, what):
+        self.status = int(status)
+        super().__init__(f"{what}: weightferry_b200 status {self.status} ({status_string(self.status)})")
+
+
+class DequantTask(ctypes.Structure):
+    _fields_ = [("src", ctypes.c_void_p), ("dst", ctypes.c_void_p), ("n_values", ctypes.c_int64)]
+
+
+# (name, restype, argtypes) of every exported function; the CPU test checks the header declares exactly these
+SIGNATURES = {
+    "wf_version": (ctypes.c_int, []),
+    "wf_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "wf_gguf_block_info": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
+    "wf_dequant_gguf": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                       ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "wf_dequant_gguf_batch": (ctypes.c_int, [ctypes.POINTER(DequantTask), ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_int, ctypes.c_void_p]),
+    "wf_dequant_gguf_lora": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                            ctypes.c_void_p]),
+    "wf_lora_add": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float,
+                                   ctypes.c_void_p]),
+}
+
+
+def _load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise ExtensionMissing(f"weightferry_b200 CUDA library not built: {LIB_PATH} is missing "
+                                   "(run __graft_entry__.build())")
+        try:
+            import torch  # noqa: F401 -- loads the CUDA runtime the library links against (one runtime per process)
+        except ImportError:
+            pass
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def lib():
+    """The loaded library (raises ExtensionMissing when it is not built)."""
+    return _load()
+
+
+def loaded():
+    return _lib is not None
+
+
+def status_string(status):
+    try:
+        s = _load().wf_status_string(int(status))
+    except ExtensionMissing:
+        return "library not loaded"
+    return s.decode() if s else "?"
+
+
+def check(status, what):
+    if status != 0:
+        raise WFError(status, what)
+
+
+def stream_of(device):
+    """cudaStream_t of the current PyTorch stream on `device`, as an integer for ctypes."""
+    import torch
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def dtype_code(dtype):
+    import torch
+    return {torch.float16: WF_F16, torch.bfloat16: WF_BF16, torch.float32: WF_F32}[dtype]

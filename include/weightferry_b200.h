@@ -1,0 +1,89 @@
+/*
+ * weightferry_b200.h -- C ABI of the B200 (sm_100a) kernels behind the WeightFerry quantized-weight path.
+ *
+ * Conventions shared by every entry point:
+ *   - all buffers are device pointers allocated by the caller; no entry point allocates device memory;
+ *   - `stream` is a cudaStream_t (the caller's current stream: the reference launches on
+ *     torch.cuda.current_stream(), enhancers/fused_int8.py:151); NULL means the legacy default stream;
+ *   - the return value is WF_OK (0), a negative WF_ERR_* for a rejected argument (nothing was launched), or a
+ *     positive cudaError_t reported by the launch;
+ *   - dtype codes follow the reference's _DT table (enhancers/gguf_dequant.py:58): 0 float16, 1 bfloat16, 2 float32.
+ *
+ * Reference citations are paths inside the ComfyUI-WeightFerry package.
+ */
+#ifndef WEIGHTFERRY_B200_H
+#define WEIGHTFERRY_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define WF_API __attribute__((visibility("default")))
+#else
+#define WF_API
+#endif
+
+typedef struct CUstream_st *wf_stream_t; /* identical to cudaStream_t */
+
+enum {
+    WF_OK = 0,
+    WF_ERR_ARG = -1,         /* a size, pointer or dtype outside the contract */
+    WF_ERR_UNSUPPORTED = -2, /* a GGML type id (or mode) this library does not decode */
+    WF_ERR_SHAPE = -3,       /* byte count and value count disagree for the format */
+    WF_ERR_DEVICE = -4       /* the current device is not an sm_100 part, or no device */
+};
+
+enum { WF_F16 = 0, WF_BF16 = 1, WF_F32 = 2 };
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+WF_API int wf_version(void);
+
+/* A static, human-readable string for a status returned by any entry point. */
+WF_API const char *wf_status_string(int status);
+
+/* Block geometry of a GGML quantisation type: values per block (32 or 256) and bytes per block.
+ * Replaces the reference's _FORMATS / _KFORMATS tables (enhancers/gguf_dequant.py:52-56).
+ * Returns WF_ERR_UNSUPPORTED for a type id outside Q4_0 (2), Q4_1 (3), Q5_0 (6), Q5_1 (7), Q8_0 (8), Q2_K (10),
+ * Q3_K (11), Q4_K (12), Q5_K (13), Q6_K (14). */
+WF_API int wf_gguf_block_info(int qtype, int *values_per_block, int *bytes_per_block);
+
+/* GGUF dequantisation of one packed tensor: `src_bytes` bytes of blocks -> `n_values` values of dtype `out`, every
+ * intermediate product / sum rounded to dtype `mid` exactly as ComfyUI-GGUF's PyTorch chain does.
+ * Replaces the Triton launches of dequantize() / _dequantize_k() (enhancers/gguf_dequant.py:277-326; kernels
+ * _deq :136-167 and _deq_k :188-256). src_bytes must equal n_values / values_per_block * bytes_per_block; dst must be
+ * aligned to the output element (16-byte aligned src and dst take the vectorised path). */
+WF_API int wf_dequant_gguf(const void *src, int64_t src_bytes, void *dst, int64_t n_values, int qtype, int mid, int out,
+                    wf_stream_t stream);
+
+/* One tensor of a batched (checkpoint-wide) dequantisation. */
+typedef struct wf_dequant_task {
+    const void *src; /* packed blocks */
+    void *dst;       /* n_values outputs */
+    int64_t n_values;
+} wf_dequant_task;
+
+/* Dequantise many tensors of one GGML type in one launch (a table of tensors, one persistent grid). Same arithmetic
+ * as wf_dequant_gguf on each task. The reference dequantises per tensor on use (enhancers/gguf_dequant.py:296); this
+ * is the sweep the streaming loader runs over a block's (or a shard's) tensors. n_tasks >= 0. */
+WF_API int wf_dequant_gguf_batch(const wf_dequant_task *tasks, int n_tasks, int qtype, int mid, int out, wf_stream_t stream);
+
+/* dequantisation with the first plain LoRA difference added in the same pass:
+ *   w = R_out(R_out(x) + R_out(diff * sa)),  x the value wf_dequant_gguf produces before its cast,
+ * diff the float32 (up @ down) of n_values, sa = float32(strength * alpha). Replaces the DEQ launch of _deq_add
+ * (enhancers/gguf_dequant.py:99-133, launched by _add_loras :387-406). Every GGML type of wf_dequant_gguf. */
+WF_API int wf_dequant_gguf_lora(const void *src, int64_t src_bytes, const float *diff, void *dst, int64_t n_values,
+                                int qtype, int mid, int out, float sa, wf_stream_t stream);
+
+/* One further LoRA difference added in place to a dequantised weight w of dtype `out`:
+ *   w = R_out(w + R_out(diff * sa)).
+ * Replaces the non-DEQ launch of _deq_add (enhancers/gguf_dequant.py:124-133). */
+WF_API int wf_lora_add(const float *diff, void *w, int64_t n_values, int out, float sa, wf_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WEIGHTFERRY_B200_H */
