@@ -63,8 +63,183 @@ template <> struct Legacy<3> { static constexpr bool HAS_M = true;  static const
 template <> struct Legacy<6> { static constexpr bool HAS_M = false; static constexpr int QH = 2,  QS = 6, SUB = 16; };
 template <> struct Legacy<7> { static constexpr bool HAS_M = true;  static constexpr int QH = 4,  QS = 8, SUB = 0;  };
 
+// ------------------------------------------------------------------------------------------------- float16 path
+// MID = float16 (the reference's default) in packed half arithmetic. Every step of the chain is an f16 value times a
+// small integer (exact in float32), or a sum / difference of two f16 values; the f16 operation rounds the exact
+// result once, and the reference rounds the float32 result to f16 -- the same value, since float32 holds the
+// products exactly and double rounding through float32 (24 bits) is innocuous for a sum of 11-bit values (24 >=
+// 2 * 11 + 1); results in the subnormal range are multiples of 2^-24 and exact either way. __h*2_rn keep the
+// compiler from contracting a product and a sum into one fma. Non-finite scales (inf * 0) give NaN payloads that
+// are not reproduced bit for bit; every finite result, overflow to inf included, is.
+
+// Two small non-negative integers (< 1024) held in bytes of `w` (chosen by the byte_perm selector `sel`, the second
+// and fourth selected bytes being 0x64) become the half2 (1024 + a, 1024 + b); subtracting `bias` (1024 + offset)
+// leaves (a - offset, b - offset), exactly.
+__device__ __forceinline__ __half2 ints_h2(uint32_t w, uint32_t sel, __half2 bias) {
+    const uint32_t bits = __byte_perm(w, 0x64646464u, sel);
+    return __hsub2_rn(*reinterpret_cast<const __half2 *>(&bits), bias);
+}
+
+// 4 bytes of w -> pairs (b0, b1), (b2, b3) minus `bias`
+__device__ __forceinline__ void bytes4_h2(uint32_t w, __half2 bias, __half2 &p01, __half2 &p23) {
+    p01 = ints_h2(w, 0x4140u, bias);
+    p23 = ints_h2(w, 0x4342u, bias);
+}
+
+__device__ __forceinline__ __half2 h2_bias(float b) { return __float2half2_rn(b); }
+__device__ __forceinline__ __half h_of_bits(uint32_t bits) { return __ushort_as_half(static_cast<unsigned short>(bits)); }
+__device__ __forceinline__ __half2 h2_splat_bits(uint32_t bits) { return __half2half2(h_of_bits(bits)); }
+// a small integer (0 <= v < 1024) minus `off`, as an exact half
+__device__ __forceinline__ __half h_int(uint32_t v, float off) {
+    return __hsub_rn(h_of_bits(0x6400u | v), __float2half_rn(1024.0f + off));
+}
+// bit i (i = 0..3) of v moved to bit 0 of byte i
+__device__ __forceinline__ uint32_t spread4(uint32_t v) { return ((v & 0xFu) * 0x00204081u) & 0x01010101u; }
+
+template <int QT>
+__device__ __forceinline__ void decode8_h(const uint8_t *blk, int v0, __half2 h[4]) {
+    if constexpr (QT == 8) {  // Q8_0
+        const __half2 d = h2_splat_bits(lds16(blk));
+        const uint2 q = lds8_any(blk + 2 + v0);
+        const __half2 bias = h2_bias(1152.0f);  // (q ^ 0x80) = q + 128
+        __half2 a, b, c, e;
+        bytes4_h2(q.x ^ 0x80808080u, bias, a, b);
+        bytes4_h2(q.y ^ 0x80808080u, bias, c, e);
+        h[0] = __hmul2_rn(d, a); h[1] = __hmul2_rn(d, b); h[2] = __hmul2_rn(d, c); h[3] = __hmul2_rn(d, e);
+    } else if constexpr (QT == 2 || QT == 3 || QT == 6 || QT == 7) {
+        using L = Legacy<QT>;
+        const __half2 d = h2_splat_bits(lds16(blk));
+        const uint2 b = lds8_any(blk + L::QS + (v0 & 15));
+        const uint32_t sh = (v0 >> 4) * 4;
+        uint32_t lo = (b.x >> sh) & 0x0F0F0F0Fu, hi = (b.y >> sh) & 0x0F0F0F0Fu;
+        if constexpr (L::QH >= 0) {
+            const uint32_t hb = blk[L::QH + (v0 >> 3)];
+            lo |= spread4(hb) << 4;
+            hi |= spread4(hb >> 4) << 4;
+        }
+        const __half2 bias = h2_bias(1024.0f + L::SUB);
+        bytes4_h2(lo, bias, h[0], h[1]);
+        bytes4_h2(hi, bias, h[2], h[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __hmul2_rn(d, h[i]);
+        if constexpr (L::HAS_M) {
+            const __half2 m = h2_splat_bits(lds16(blk + 2));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) h[i] = __hadd2_rn(h[i], m);
+        }
+    } else if constexpr (QT == 12 || QT == 13) {  // Q4_K / Q5_K
+        const int sub = v0 >> 5;
+        const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
+        const uint8_t *sc_b = blk + 4;
+        uint32_t sc, mn;
+        if (sub < 4) {
+            sc = sc_b[sub] & 63u;
+            mn = sc_b[4 + sub] & 63u;
+        } else {
+            const int j = sub - 4;
+            sc = (sc_b[8 + j] & 0xFu) | ((sc_b[j] >> 2) & 0x30u);
+            mn = (sc_b[8 + j] >> 4) | ((sc_b[4 + j] >> 2) & 0x30u);
+        }
+        const __half2 ds = __half2half2(__hmul_rn(h_of_bits(dd), h_int(sc, 0.f)));
+        const __half2 dm = __half2half2(__hmul_rn(h_of_bits(dd >> 16), h_int(mn, 0.f)));
+        constexpr int QS_OFF = (QT == 12) ? 16 : 48;
+        const uint2 b = *reinterpret_cast<const uint2 *>(blk + QS_OFF + (sub >> 1) * 32 + (v0 & 31));
+        const uint32_t sh = (sub & 1) * 4;
+        uint32_t lo = (b.x >> sh) & 0x0F0F0F0Fu, hi = (b.y >> sh) & 0x0F0F0F0Fu;
+        if constexpr (QT == 13) {
+            const uint2 hb = *reinterpret_cast<const uint2 *>(blk + 16 + (v0 & 31));
+            lo |= ((hb.x >> sub) & 0x01010101u) << 4;
+            hi |= ((hb.y >> sub) & 0x01010101u) << 4;
+        }
+        const __half2 bias = h2_bias(1024.0f);
+        bytes4_h2(lo, bias, h[0], h[1]);
+        bytes4_h2(hi, bias, h[2], h[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __hsub2_rn(__hmul2_rn(ds, h[i]), dm);
+    } else if constexpr (QT == 14) {  // Q6_K
+        const int hh = v0 >> 7, r = v0 & 127;
+        const uint2 lo = lds8_any(blk + hh * 64 + (r & 63));
+        const uint2 hi = lds8_any(blk + 128 + hh * 32 + (r & 31));
+        const uint32_t lsh = (r >> 6) * 4, hsh = (r >> 5) * 2;
+        const uint32_t q0 = ((lo.x >> lsh) & 0x0F0F0F0Fu) | (((hi.x >> hsh) & 0x03030303u) << 4);
+        const uint32_t q1 = ((lo.y >> lsh) & 0x0F0F0F0Fu) | (((hi.y >> hsh) & 0x03030303u) << 4);
+        const uint32_t scb = blk[192 + (v0 >> 4)];
+        const __half2 d = __half2half2(__hmul_rn(h_of_bits(lds16(blk + 208)), h_int(scb ^ 0x80u, 128.f)));
+        const __half2 bias = h2_bias(1056.0f);  // q - 32
+        bytes4_h2(q0, bias, h[0], h[1]);
+        bytes4_h2(q1, bias, h[2], h[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __hmul2_rn(d, h[i]);
+    } else if constexpr (QT == 11) {  // Q3_K
+        const int i16 = v0 >> 4;
+        const uint32_t ls = (blk[96 + (i16 & 7)] >> ((i16 >> 3) * 4)) & 0xFu;
+        const uint32_t hs = (blk[104 + (i16 & 3)] >> ((i16 >> 2) * 2)) & 3u;
+        const __half2 d = __half2half2(__hmul_rn(h_of_bits(lds16(blk + 108)), h_int(ls | (hs << 4), 32.f)));
+        const int r = v0 & 127;
+        const uint2 ql = lds8_any(blk + 32 + (v0 >> 7) * 32 + (r & 31));
+        const uint2 hm = lds8_any(blk + (v0 & 31));
+        const uint32_t qsh = (r >> 5) * 2, hsh = v0 >> 5;
+        // q = ql - 4 * (1 - bit) = (ql | bit << 2) - 4
+        const uint32_t q0 = ((ql.x >> qsh) & 0x03030303u) | (((hm.x >> hsh) & 0x01010101u) << 2);
+        const uint32_t q1 = ((ql.y >> qsh) & 0x03030303u) | (((hm.y >> hsh) & 0x01010101u) << 2);
+        const __half2 bias = h2_bias(1028.0f);
+        bytes4_h2(q0, bias, h[0], h[1]);
+        bytes4_h2(q1, bias, h[2], h[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __hmul2_rn(d, h[i]);
+    } else if constexpr (QT == 10) {  // Q2_K
+        const uint32_t sb = blk[v0 >> 4];
+        const __half2 dl = __half2half2(__hmul_rn(h_of_bits(lds16(blk + 80)), h_int(sb & 0xFu, 0.f)));
+        const __half2 ml = __half2half2(__hmul_rn(h_of_bits(lds16(blk + 82)), h_int(sb >> 4, 0.f)));
+        const int r = v0 & 127;
+        const uint2 qb = lds8_any(blk + 16 + (v0 >> 7) * 32 + (r & 31));
+        const uint32_t qsh = (r >> 5) * 2;
+        const __half2 bias = h2_bias(1024.0f);
+        bytes4_h2((qb.x >> qsh) & 0x03030303u, bias, h[0], h[1]);
+        bytes4_h2((qb.y >> qsh) & 0x03030303u, bias, h[2], h[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __hsub2_rn(__hmul2_rn(dl, h[i]), ml);
+    }
+}
+
+// Eight float16 results written as dtype OUT: float16 as they are, bfloat16 by the packed RNE conversion of their
+// float32 values (the reference's bit-level RNE gives the same bits on every non-NaN value), float32 widened.
+template <int OUT, bool VEC>
+__device__ __forceinline__ void store8_h(void *dst, const __half2 h[4]) {
+    if constexpr (OUT == WF_F16) {
+        if constexpr (VEC) {
+            *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(h);
+        } else {
+            const __half *hs = reinterpret_cast<const __half *>(h);
+            __half *ds = reinterpret_cast<__half *>(dst);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ds[i] = hs[i];
+        }
+    } else {
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(h[i]);
+            x[2 * i] = f.x;
+            x[2 * i + 1] = f.y;
+        }
+        store8<OUT, VEC>(dst, x);
+    }
+}
+
 template <int QT, int MID>
 __device__ __forceinline__ void decode8(const uint8_t *blk, int v0, float x[8]) {
+    if constexpr (MID == WF_F16) {
+        __half2 h[4];
+        decode8_h<QT>(blk, v0, h);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(h[i]);
+            x[2 * i] = f.x;
+            x[2 * i + 1] = f.y;
+        }
+        return;
+    }
     if constexpr (QT == 8) {  // Q8_0: x = R(R(d) * q), q the int8
         const float d = rnd<MID>(f16_bits_to_f32(lds16(blk)));
         const uint2 q = lds8_any(blk + 2 + v0);
@@ -194,10 +369,20 @@ __device__ __forceinline__ void decode_chunk(const uint8_t *sbuf, void *dst_chun
         const int g = threadIdx.x + i * kThreads;
         const int v = 8 * g;
         if (v >= valid_values) break;
+        if constexpr (MID == WF_F16 && !LORA) {
+            __half2 h[4];
+            decode8_h<QT>(sbuf + (v / VPB) * TS, v % VPB, h);
+            store8_h<OUT, ALIGNED>(static_cast<uint8_t *>(dst_chunk) + static_cast<size_t>(v) * dtype_size(OUT), h);
+            continue;
+        }
         float x[8];
         decode8<QT, MID>(sbuf + (v / VPB) * TS, v % VPB, x);
+        // the cast to OUT: store8's RNE conversion (bit-identical to the reference's rounding on non-NaN values);
+        // the LoRA add needs the rounded weight as float first
+        if constexpr (LORA || OUT == WF_F32) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) x[k] = rnd<OUT>(x[k]);
+            for (int k = 0; k < 8; ++k) x[k] = rnd<OUT>(x[k]);
+        }
         if constexpr (LORA) {
             float dl[8];
             if constexpr (ALIGNED) {
