@@ -45,6 +45,16 @@ SIGNATURES = {
                                             ctypes.c_void_p]),
     "wf_lora_add": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float,
                                    ctypes.c_void_p]),
+    "wf_modulate": (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]),
+    "wf_ln_modulate": (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3 + [ctypes.c_float,
+                                                                                      ctypes.c_void_p]),
+    "wf_rms_norm_128": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                       ctypes.c_int64, ctypes.c_float, ctypes.c_void_p]),
+    "wf_rms_rope128": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int64] * 4
+                       + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p] + [ctypes.c_int64] * 3
+                       + [ctypes.c_float, ctypes.c_void_p]),
+    "wf_quant_rows": (ctypes.c_int, [ctypes.c_void_p] * 6 + [ctypes.c_int64] * 3
+                      + [ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
 }
 
 

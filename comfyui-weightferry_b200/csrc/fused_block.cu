@@ -1,0 +1,518 @@
+// Fused Cosmos / Anima block prologue kernels for sm_100a: modulate, LayerNorm + modulate (kernel A), RMSNorm-128,
+// RMSNorm-128 + split-half 3D RoPE (kernel B), and the per-token int8 row quantiser of the W8A8 linear.
+//
+// Arithmetic follows the reference's Triton kernels operation by operation (enhancers/fused_kernels.py,
+// enhancers/sage_fused.py): every bf16 rounding where the reference rounds (_r16), the same summation orders (the
+// Welford order of PyTorch's vectorized layer norm, the lane trees of the RMS sums), fused multiply-adds exactly
+// where the reference writes them, and the same hardware approximations (rsqrt.approx.f32, and the approximate
+// float32 division Triton emits for `/`). All memory-bound: one read of the activations, one write.
+//
+// Data layout: rows of bf16, contiguous. A row of the layer-norm / quantiser kernels is one CTA of 128 threads,
+// thread t holding the 4-value vectors t, t + 128, ... of the row (PyTorch's layout, which fixes the Welford order);
+// the RMS kernels put one row of 128 on one warp.
+
+#include "wf_common.cuh"
+
+#include <algorithm>
+
+namespace wf {
+namespace {
+
+// ------------------------------------------------------------------------------------------------- helpers
+__device__ __forceinline__ float rsqrt_approx(float v) {
+    float r;
+    asm("rsqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
+
+// Triton's float32 `/` (the reference's quantiser divides with it): the full-range approximate division.
+__device__ __forceinline__ float div_full(float a, float b) {
+    float r;
+    asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// four bf16 (8 bytes) -> float
+__device__ __forceinline__ void unpack4(uint2 w, float v[4]) {
+    v[0] = bf_lo(w.x);
+    v[1] = bf_hi(w.x);
+    v[2] = bf_lo(w.y);
+    v[3] = bf_hi(w.y);
+}
+
+// two floats -> packed bf16 pair (RNE; equal to the reference's bit-level rounding on every non-NaN value)
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+__device__ __forceinline__ float load_w(const void *w, int wdt, int i) {
+    if (wdt == WF_BF16) return __bfloat162float(static_cast<const __nv_bfloat16 *>(w)[i]);
+    if (wdt == WF_F16) return __half2float(static_cast<const __half *>(w)[i]);
+    return static_cast<const float *>(w)[i];
+}
+
+// ------------------------------------------------------------------------------------------------- modulate
+// out = R16(R16(x * s1) + shift) (fused_kernels.py:51-62 _mod), 8 values per thread, grid-stride. d % 8 == 0.
+__global__ void __launch_bounds__(256) modulate_kernel(const uint4 *__restrict__ x, const __nv_bfloat16 *__restrict__ s1,
+                                                       const __nv_bfloat16 *__restrict__ sh, uint4 *__restrict__ out,
+                                                       int64_t n_vec, int64_t d, int64_t rows_per_group) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_vec; i += stride) {
+        const int64_t e = i * 8;
+        const int64_t row = e / d, col = e - row * d;
+        const int64_t goff = (row / rows_per_group) * d + col;
+        const uint4 xv = __ldg(x + i);
+        const uint4 sv = __ldg(reinterpret_cast<const uint4 *>(s1 + goff));
+        const uint4 hv = __ldg(reinterpret_cast<const uint4 *>(sh + goff));
+        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w},
+                       hs[4] = {hv.x, hv.y, hv.z, hv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float t0 = r16(__fmul_rn(bf_lo(xs[k]), bf_lo(ss[k])));
+            const float t1 = r16(__fmul_rn(bf_hi(xs[k]), bf_hi(ss[k])));
+            o[k] = pack2(__fadd_rn(t0, bf_lo(hs[k])), __fadd_rn(t1, bf_hi(hs[k])));
+        }
+        out[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------- Welford
+struct Welford {
+    float m, s, c;
+};
+
+// _wcombine (fused_kernels.py:84-93): own = the lower lane / warp, oth = the one merged into it
+__device__ __forceinline__ Welford wcombine(Welford own, Welford oth) {
+    const float delta = __fsub_rn(own.m, oth.m);
+    const float count = __fadd_rn(oth.c, own.c);
+    const float coef = __fdiv_rn(1.0f, count);
+    const float n_a = __fmul_rn(oth.c, coef);
+    const float n_b = __fmul_rn(own.c, coef);
+    Welford r;
+    r.m = __fmaf_rn(n_a, oth.m, __fmul_rn(n_b, own.m));
+    r.s = __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), oth.c), n_b, __fadd_rn(oth.s, own.s));
+    r.c = count;
+    return r;
+}
+
+// PyTorch's vectorized layer-norm statistics of one row, as _ln_stats reproduces them (fused_kernels.py:106-135):
+// this thread's Welford state over its values v (already in its vector order), then shuffle-down merges 16 .. 1,
+// then warps 2, 3 into 0, 1 and 1 into 0. Returns (mean, sigma2 / K) to every thread. 128 threads.
+__device__ __forceinline__ void welford_step(Welford &w, float v) {
+    const float delta = __fsub_rn(v, w.m);
+    w.c = __fadd_rn(w.c, 1.0f);
+    w.m = __fmaf_rn(delta, __fdiv_rn(1.0f, w.c), w.m);
+    w.s = __fmaf_rn(delta, __fsub_rn(v, w.m), w.s);
+}
+
+__device__ __forceinline__ void ln_merge(Welford w, int64_t K, float &mu, float &var, float *red);
+
+__device__ __forceinline__ void ln_stats(const float *v, int nv, int64_t K, float &mu, float &var, float *red) {
+    Welford w{0.f, 0.f, 0.f};
+    for (int i = 0; i < nv; ++i) welford_step(w, v[i]);
+    ln_merge(w, K, mu, var, red);
+}
+
+// the same statistics with this thread's nvec vectors of 4 in shared memory at p, p + 512, ... (floats)
+__device__ __forceinline__ void ln_stats_strided(const float *p, int nvec, int64_t K, float &mu, float &var,
+                                                 float *red) {
+    Welford w{0.f, 0.f, 0.f};
+    for (int j = 0; j < nvec; ++j) {
+        const float4 v = *reinterpret_cast<const float4 *>(p + 512 * j);
+        welford_step(w, v.x);
+        welford_step(w, v.y);
+        welford_step(w, v.z);
+        welford_step(w, v.w);
+    }
+    ln_merge(w, K, mu, var, red);
+}
+
+__device__ __forceinline__ void ln_merge(Welford w, int64_t K, float &mu, float &var, float *red) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        Welford o;
+        o.m = __shfl_down_sync(0xFFFFFFFFu, w.m, off);
+        o.s = __shfl_down_sync(0xFFFFFFFFu, w.s, off);
+        o.c = __shfl_down_sync(0xFFFFFFFFu, w.c, off);
+        w = wcombine(w, o);  // meaningful for lanes < off; lane 0 ends with the warp's state
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        red[warp * 3 + 0] = w.m;
+        red[warp * 3 + 1] = w.s;
+        red[warp * 3 + 2] = w.c;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        Welford w0{red[0], red[1], red[2]}, w1{red[3], red[4], red[5]}, w2{red[6], red[7], red[8]},
+            w3{red[9], red[10], red[11]};
+        w0 = wcombine(w0, w2);
+        w1 = wcombine(w1, w3);
+        w0 = wcombine(w0, w1);
+        red[12] = w0.m;
+        red[13] = __fdiv_rn(w0.s, static_cast<float>(K));
+    }
+    __syncthreads();
+    mu = red[12];
+    var = red[13];
+}
+
+// ------------------------------------------------------------------------------------------------- kernel A
+// LayerNorm (no affine) + modulate, one row per CTA of 128 threads (fused_kernels.py:219-232 _lnmod):
+// x = R16((x - mu) * rsqrt.approx(var + eps)); out = R16(R16(x * s1) + shift). K % 512 == 0, NV = K / 512.
+template <int NV>
+__global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *__restrict__ x,
+                                                          const __nv_bfloat16 *__restrict__ s1,
+                                                          const __nv_bfloat16 *__restrict__ sh,
+                                                          __nv_bfloat16 *__restrict__ out, int64_t K,
+                                                          int64_t rows_per_group, float eps) {
+    __shared__ float red[16];
+    const int64_t row = blockIdx.x;
+    const int t = threadIdx.x;
+    const __nv_bfloat16 *xr = x + row * K;
+    float v[NV * 4];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) unpack4(__ldg(reinterpret_cast<const uint2 *>(xr) + t + 128 * j), v + 4 * j);
+    float mu, var;
+    ln_stats(v, NV * 4, K, mu, var, red);
+    const float rstd = rsqrt_approx(__fadd_rn(var, eps));
+    const int64_t goff = (row / rows_per_group) * K;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int64_t c = static_cast<int64_t>(t + 128 * j) * 4;
+        float s[4], h[4];
+        unpack4(__ldg(reinterpret_cast<const uint2 *>(s1 + goff + c)), s);
+        unpack4(__ldg(reinterpret_cast<const uint2 *>(sh + goff + c)), h);
+        float o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float n = r16(__fmul_rn(__fsub_rn(v[4 * j + k], mu), rstd));
+            o[k] = __fadd_rn(r16(__fmul_rn(n, s[k])), h[k]);
+        }
+        *reinterpret_cast<uint2 *>(out + row * K + c) = make_uint2(pack2(o[0], o[1]), pack2(o[2], o[3]));
+    }
+}
+
+// ------------------------------------------------------------------------------------------------- RMSNorm-128
+// One row of 128 per warp (fused_kernels.py:189-217 _rms128): lane t squares values 4t .. 4t+3 and adds them as
+// ((a + b) + c) + d, a pairwise tree over the lanes (lane t + lane t + 16, ...), rstd = rsqrt.approx(sum / 128 +
+// eps), y = R16((x * rstd) * w). 8 warps per CTA, rows grid-strided.
+__global__ void __launch_bounds__(256) rms128_kernel(const __nv_bfloat16 *__restrict__ x, const void *__restrict__ w,
+                                                     int wdt, __nv_bfloat16 *__restrict__ out, int64_t n_rows,
+                                                     float eps) {
+    const int lane = threadIdx.x & 31;
+    float wv[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) wv[k] = load_w(w, wdt, 4 * lane + k);
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n_rows;
+         r += warps) {
+        float v[4];
+        unpack4(__ldg(reinterpret_cast<const uint2 *>(x + r * 128) + lane), v);
+        float s = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(v[0], v[0]), __fmul_rn(v[1], v[1])), __fmul_rn(v[2], v[2])),
+                            __fmul_rn(v[3], v[3]));
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_down_sync(0xFFFFFFFFu, s, off));
+        s = __shfl_sync(0xFFFFFFFFu, s, 0);
+        const float rstd = rsqrt_approx(__fadd_rn(__fmul_rn(s, 0.0078125f), eps));
+        float o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] = __fmul_rn(__fmul_rn(v[k], rstd), wv[k]);
+        *reinterpret_cast<uint2 *>(out + r * 128 + 4 * lane) = make_uint2(pack2(o[0], o[1]), pack2(o[2], o[3]));
+    }
+}
+
+// ------------------------------------------------------------------------------------------------- kernel B
+// RMSNorm-128 + split-half RoPE of contiguous (B, L, H, 128) rows (sage_fused.py:246-272 _rms_rope128, the
+// reproduction of comfy_kitchen's rope kernel): lane t owns values t, t+32, t+64, t+96; squares summed by fma from
+// 0 in that order, pairwise lane tree, rr = rsqrt.approx(sum / 128 + eps), n = R16((x * rr) * w); then the pairs
+// (d, d + 64) rotate: y0 = R16(fma(f00, lo, f01 * hi)), y1 = R16(fma(f10, lo, f11 * hi)). Rotations f[token, d] are
+// float32 2x2 with element strides (s_tok, s_d, s_i, s_j). One row per warp, grid-strided.
+__global__ void __launch_bounds__(256) rms_rope_kernel(const __nv_bfloat16 *__restrict__ x,
+                                                       const float *__restrict__ f, const void *__restrict__ w,
+                                                       int wdt, __nv_bfloat16 *__restrict__ out, int64_t n_rows,
+                                                       int64_t heads, int64_t tokens, float eps, int64_t s_tok,
+                                                       int64_t s_d, int64_t s_i, int64_t s_j) {
+    const int lane = threadIdx.x & 31;
+    float wv[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) wv[k] = load_w(w, wdt, lane + 32 * k);
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n_rows;
+         r += warps) {
+        const __nv_bfloat16 *xr = x + r * 128;
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = __bfloat162float(xr[lane + 32 * k]);
+        float a = __fmul_rn(v[0], v[0]);
+        a = __fmaf_rn(v[1], v[1], a);
+        a = __fmaf_rn(v[2], v[2], a);
+        a = __fmaf_rn(v[3], v[3], a);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xFFFFFFFFu, a, off));
+        a = __shfl_sync(0xFFFFFFFFu, a, 0);
+        const float rr = rsqrt_approx(__fadd_rn(__fmul_rn(a, 0.0078125f), eps));
+        float n[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) n[k] = r16(__fmul_rn(__fmul_rn(v[k], rr), wv[k]));
+        const int64_t tok = (r / heads) % tokens;
+        __nv_bfloat16 *orow = out + r * 128;
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {  // d = lane (+ 32): pairs (n[p], n[p + 2])
+            const int d = lane + 32 * p;
+            const float *fd = f + tok * s_tok + d * s_d;
+            const float f00 = __ldg(fd), f01 = __ldg(fd + s_j), f10 = __ldg(fd + s_i), f11 = __ldg(fd + s_i + s_j);
+            const float lo = n[p], hi = n[p + 2];
+            orow[d] = __float2bfloat16_rn(__fmaf_rn(f00, lo, __fmul_rn(f01, hi)));
+            orow[d + 64] = __float2bfloat16_rn(__fmaf_rn(f10, lo, __fmul_rn(f11, hi)));
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------- quantiser
+// Per-token int8 quantisation of a row (fused_kernels.py:137-174 _quant_row), one row per CTA of 128 threads:
+//   PRE 0 none | 1 GELU of the bf16 value from a 65536-entry bf16 table | 2 modulate | 3 LayerNorm + modulate;
+//   ROT: the ConvRot Hadamard of every 256 values (four radix-4 stages of stride 1, 4, 16, 64, each 4-tuple
+//        (a, b, c, d) -> (a+b+c-d, a+b-c+d, a-b+c+d, -a+b+c+d) summed left to right, then x 1/16) -- off for the
+//        plain per-token absmax quantiser;
+//   amax = min(max |x|, 3.38953139e38), scale = max(amax / 127, 1e-30) (stored),
+//   q = rint(R16(R16(x) / R16(scale))) clamped to [-128, 127].
+// The row (after PRE) is staged in shared memory as float32 (K * 4 bytes, dynamic).
+template <int PRE, bool ROT>
+__global__ void __launch_bounds__(128) quant_rows_kernel(const __nv_bfloat16 *__restrict__ x,
+                                                         const __nv_bfloat16 *__restrict__ s1,
+                                                         const __nv_bfloat16 *__restrict__ sh,
+                                                         const __nv_bfloat16 *__restrict__ gelu,
+                                                         int8_t *__restrict__ q, float *__restrict__ scale_out,
+                                                         int64_t K, int64_t rows_per_group, float eps) {
+    extern __shared__ __align__(16) float srow[];
+    __shared__ float red[16];
+    const int64_t row = blockIdx.x;
+    const int t = threadIdx.x;
+    const __nv_bfloat16 *xr = x + row * K;
+    const int nvec = static_cast<int>(K / 512);  // vectors of 4 per thread (K % 512 == 0) ...
+    const int64_t goff = (row / rows_per_group) * K;
+    if constexpr (PRE == 3) {
+        // the row goes to shared memory first; this thread's Welford pass reads its own vectors back in order
+        for (int j = 0; j < nvec; ++j) {
+            float v[4];
+            unpack4(__ldg(reinterpret_cast<const uint2 *>(xr) + t + 128 * j), v);
+            *reinterpret_cast<float4 *>(srow + (t + 128 * j) * 4) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        float mu, var;
+        ln_stats_strided(srow + 4 * t, nvec, K, mu, var, red);
+        const float rstd = rsqrt_approx(__fadd_rn(var, eps));
+        for (int j = 0; j < nvec; ++j) {
+            const int64_t c = static_cast<int64_t>(t + 128 * j) * 4;
+            float s[4], h[4];
+            unpack4(__ldg(reinterpret_cast<const uint2 *>(s1 + goff + c)), s);
+            unpack4(__ldg(reinterpret_cast<const uint2 *>(sh + goff + c)), h);
+            const float4 v4 = *reinterpret_cast<const float4 *>(srow + c);
+            const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+            float o[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float n = r16(__fmul_rn(__fsub_rn(v[k], mu), rstd));
+                o[k] = r16(__fadd_rn(r16(__fmul_rn(n, s[k])), h[k]));
+            }
+            *reinterpret_cast<float4 *>(srow + c) = make_float4(o[0], o[1], o[2], o[3]);
+        }
+    } else {
+        // ... or, without the layer norm, any K % 4 == 0: vectors t, t + 128, ...
+        for (int64_t vi = t; vi < K / 4; vi += 128) {
+            const int64_t c = vi * 4;
+            float v[4];
+            unpack4(__ldg(reinterpret_cast<const uint2 *>(xr + c)), v);
+            if constexpr (PRE == 1) {
+                const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(xr + c));
+                const uint32_t b[4] = {raw.x & 0xFFFFu, raw.x >> 16, raw.y & 0xFFFFu, raw.y >> 16};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[k] = __bfloat162float(gelu[b[k]]);
+            } else if constexpr (PRE == 2) {
+                float s[4], h[4];
+                unpack4(__ldg(reinterpret_cast<const uint2 *>(s1 + goff + c)), s);
+                unpack4(__ldg(reinterpret_cast<const uint2 *>(sh + goff + c)), h);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[k] = r16(__fadd_rn(r16(__fmul_rn(v[k], s[k])), h[k]));
+            }
+            *reinterpret_cast<float4 *>(srow + c) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+    }
+    __syncthreads();
+    if constexpr (ROT) {
+        for (int S = 1; S <= 64; S *= 4) {
+            for (int64_t u = t; u < K / 4; u += 128) {
+                const int64_t grp = u / 64, uu = u - grp * 64;           // 64 tuples per 256-group
+                const int64_t base = grp * 256 + (uu / S) * 4 * S + (uu % S);
+                const float a = srow[base], b = srow[base + S], c = srow[base + 2 * S], d = srow[base + 3 * S];
+                const float y0 = __fsub_rn(__fadd_rn(__fadd_rn(a, b), c), d);
+                const float y1 = __fadd_rn(__fsub_rn(__fadd_rn(a, b), c), d);
+                const float y2 = __fadd_rn(__fadd_rn(__fsub_rn(a, b), c), d);
+                const float y3 = __fadd_rn(__fadd_rn(__fadd_rn(-a, b), c), d);
+                srow[base] = y0;
+                srow[base + S] = y1;
+                srow[base + 2 * S] = y2;
+                srow[base + 3 * S] = y3;
+            }
+            __syncthreads();
+        }
+    }
+    // amax of the row (after the 1/16 scaling when rotated)
+    float amax = 0.f;
+    for (int64_t c = 4 * t; c < K; c += 512) {
+        float4 f4 = *reinterpret_cast<const float4 *>(srow + c);
+        if constexpr (ROT) {
+            f4.x = __fmul_rn(f4.x, 0.0625f); f4.y = __fmul_rn(f4.y, 0.0625f);
+            f4.z = __fmul_rn(f4.z, 0.0625f); f4.w = __fmul_rn(f4.w, 0.0625f);
+            *reinterpret_cast<float4 *>(srow + c) = f4;
+        }
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(f4.x), fabsf(f4.y)), fmaxf(fabsf(f4.z), fabsf(f4.w))));
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+    if ((t & 31) == 0) red[t >> 5] = amax;
+    __syncthreads();
+    amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    amax = fminf(amax, 3.38953139e38f);
+    const float scale = fmaxf(div_full(amax, 127.0f), 1.0e-30f);
+    if (t == 0) scale_out[row] = scale;
+    const float sb = r16(scale);
+    for (int64_t c = 4 * t; c < K; c += 512) {
+        const float4 f4 = *reinterpret_cast<const float4 *>(srow + c);
+        const float fv[4] = {f4.x, f4.y, f4.z, f4.w};
+        uint32_t packed = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float y = rintf(r16(div_full(r16(fv[k]), sb)));
+            y = fminf(fmaxf(y, -128.0f), 127.0f);
+            packed |= (static_cast<uint32_t>(static_cast<int>(y)) & 0xFFu) << (8 * k);
+        }
+        *reinterpret_cast<uint32_t *>(q + row * K + c) = packed;
+    }
+}
+
+template <int PRE, bool ROT>
+int launch_quant(const void *x, const void *s1, const void *sh, const void *gelu, int8_t *q, float *sc, int64_t rows,
+                 int64_t K, int64_t rpg, float eps, cudaStream_t s) {
+    const size_t smem = static_cast<size_t>(K) * 4;
+    auto kern = quant_rows_kernel<PRE, ROT>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return static_cast<int>(e);
+    }
+    kern<<<static_cast<unsigned>(rows), 128, smem, s>>>(
+        static_cast<const __nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(s1),
+        static_cast<const __nv_bfloat16 *>(sh), static_cast<const __nv_bfloat16 *>(gelu), q, sc, K, rpg, eps);
+    return static_cast<int>(cudaGetLastError());
+}
+
+int grid_for(int64_t items, int per_block) {
+    const int64_t want = (items + per_block - 1) / per_block;
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(device_sm_count()) * 16)));
+}
+
+bool al(const void *p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+}  // namespace wf
+
+using namespace wf;
+
+extern "C" WF_API int wf_modulate(const void *x, const void *s1, const void *shift, void *out, int64_t rows,
+                                 int64_t d, int64_t rows_per_group, wf_stream_t stream) {
+    if (rows < 0 || d <= 0 || rows_per_group <= 0 || d % 8 != 0) return WF_ERR_ARG;
+    if (rows == 0) return WF_OK;
+    if (!x || !s1 || !shift || !out || !al(x, 16) || !al(s1, 16) || !al(shift, 16) || !al(out, 16)) return WF_ERR_ARG;
+    int rc = check_device();
+    if (rc != WF_OK) return rc;
+    const int64_t n_vec = rows * d / 8;
+    modulate_kernel<<<grid_for(n_vec, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4 *>(x), static_cast<const __nv_bfloat16 *>(s1),
+        static_cast<const __nv_bfloat16 *>(shift), static_cast<uint4 *>(out), n_vec, d, rows_per_group);
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" WF_API int wf_ln_modulate(const void *x, const void *s1, const void *shift, void *out, int64_t rows,
+                                    int64_t K, int64_t rows_per_group, float eps, wf_stream_t stream) {
+    if (rows < 0 || K <= 0 || K % 512 != 0 || K > 512 * 16 || rows_per_group <= 0) return WF_ERR_ARG;
+    if (rows == 0) return WF_OK;
+    if (!x || !s1 || !shift || !out || !al(x, 8) || !al(s1, 8) || !al(shift, 8) || !al(out, 8)) return WF_ERR_ARG;
+    int rc = check_device();
+    if (rc != WF_OK) return rc;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    auto X = static_cast<const __nv_bfloat16 *>(x);
+    auto S = static_cast<const __nv_bfloat16 *>(s1);
+    auto H = static_cast<const __nv_bfloat16 *>(shift);
+    auto O = static_cast<__nv_bfloat16 *>(out);
+    const unsigned g = static_cast<unsigned>(rows);
+    switch (K / 512) {
+        case 1: ln_modulate_kernel<1><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
+        case 2: ln_modulate_kernel<2><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
+        case 3: ln_modulate_kernel<3><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
+        case 4: ln_modulate_kernel<4><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
+        case 5: ln_modulate_kernel<5><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
+        case 6: ln_modulate_kernel<6><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
+        case 8: ln_modulate_kernel<8><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
+        case 10: ln_modulate_kernel<10><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
+        case 12: ln_modulate_kernel<12><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
+        case 16: ln_modulate_kernel<16><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
+        default: return WF_ERR_UNSUPPORTED;
+    }
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" WF_API int wf_rms_norm_128(const void *x, const void *w, int w_dtype, void *out, int64_t n_rows, float eps,
+                                     wf_stream_t stream) {
+    if (n_rows < 0 || w_dtype < WF_F16 || w_dtype > WF_F32) return WF_ERR_ARG;
+    if (n_rows == 0) return WF_OK;
+    if (!x || !w || !out || !al(x, 8) || !al(out, 8) || !al(w, dtype_size(w_dtype))) return WF_ERR_ARG;
+    int rc = check_device();
+    if (rc != WF_OK) return rc;
+    rms128_kernel<<<grid_for(n_rows, 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __nv_bfloat16 *>(x), w, w_dtype, static_cast<__nv_bfloat16 *>(out), n_rows, eps);
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" WF_API int wf_rms_rope128(const void *x, const float *freqs, int64_t f_stride_token, int64_t f_stride_d,
+                                    int64_t f_stride_i, int64_t f_stride_j, const void *w, int w_dtype, void *out,
+                                    int64_t batch, int64_t tokens, int64_t heads, float eps, wf_stream_t stream) {
+    if (batch < 0 || tokens < 0 || heads < 0 || w_dtype < WF_F16 || w_dtype > WF_F32) return WF_ERR_ARG;
+    const int64_t n_rows = batch * tokens * heads;
+    if (n_rows == 0) return WF_OK;
+    if (!x || !freqs || !w || !out || !al(x, 2) || !al(out, 2) || !al(freqs, 4) || !al(w, dtype_size(w_dtype)))
+        return WF_ERR_ARG;
+    int rc = check_device();
+    if (rc != WF_OK) return rc;
+    rms_rope_kernel<<<grid_for(n_rows, 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __nv_bfloat16 *>(x), freqs, w, w_dtype, static_cast<__nv_bfloat16 *>(out), n_rows, heads,
+        tokens, eps, f_stride_token, f_stride_d, f_stride_i, f_stride_j);
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" WF_API int wf_quant_rows(const void *x, const void *s1, const void *shift, const void *gelu_table,
+                                   int8_t *q, float *scale, int64_t rows, int64_t K, int64_t rows_per_group,
+                                   float eps, int pre, int rotate, wf_stream_t stream) {
+    if (rows < 0 || K <= 0 || K % 4 != 0 || rows_per_group <= 0 || pre < 0 || pre > 3) return WF_ERR_ARG;
+    if (rotate && K % 256 != 0) return WF_ERR_ARG;
+    if (pre == 3 && (K % 512 != 0 || K > 8192)) return WF_ERR_ARG;
+    if (static_cast<size_t>(K) * 4 > 200 * 1024) return WF_ERR_UNSUPPORTED;
+    if (rows == 0) return WF_OK;
+    if (!x || !q || !scale || !al(x, 8) || !al(q, 4) || !al(scale, 4)) return WF_ERR_ARG;
+    if ((pre == 2 || pre == 3) && (!s1 || !shift || !al(s1, 8) || !al(shift, 8))) return WF_ERR_ARG;
+    if (pre == 1 && (!gelu_table || !al(gelu_table, 2))) return WF_ERR_ARG;
+    int rc = check_device();
+    if (rc != WF_OK) return rc;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+#define WF_Q(P, R) return launch_quant<P, R>(x, s1, shift, gelu_table, q, scale, rows, K, rows_per_group, eps, s)
+    if (rotate) {
+        switch (pre) { case 0: WF_Q(0, true); case 1: WF_Q(1, true); case 2: WF_Q(2, true); default: WF_Q(3, true); }
+    } else {
+        switch (pre) { case 0: WF_Q(0, false); case 1: WF_Q(1, false); case 2: WF_Q(2, false); default: WF_Q(3, false); }
+    }
+#undef WF_Q
+}

@@ -82,6 +82,43 @@ WF_API int wf_dequant_gguf_lora(const void *src, int64_t src_bytes, const float 
  * Replaces the non-DEQ launch of _deq_add (enhancers/gguf_dequant.py:124-133). */
 WF_API int wf_lora_add(const float *diff, void *w, int64_t n_values, int out, float sa, wf_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------- fused block prologue
+ * bf16 tensors, contiguous rows. */
+
+/* out = R16(R16(x * s1) + shift) for rows of d (d % 8 == 0; 16-byte aligned buffers); s1 = bf16(1 + scale) and
+ * shift are [rows / rows_per_group, d]. Replaces the Triton launch of modulate() (enhancers/fused_block.py:103-124,
+ * kernel _mod fused_kernels.py:51-62). */
+WF_API int wf_modulate(const void *x, const void *s1, const void *shift, void *out, int64_t rows, int64_t d,
+                       int64_t rows_per_group, wf_stream_t stream);
+
+/* LayerNorm (no affine, PyTorch's vectorized Welford order) + modulate in one pass over rows of K (K % 512 == 0,
+ * K <= 8192): x = R16((x - mean) * rsqrt(var + eps)); out = R16(R16(x * s1) + shift). Replaces ln_modulate()'s
+ * launch (enhancers/fused_block.py:165-179, kernel _lnmod fused_kernels.py:219-232). */
+WF_API int wf_ln_modulate(const void *x, const void *s1, const void *shift, void *out, int64_t rows, int64_t K,
+                          int64_t rows_per_group, float eps, wf_stream_t stream);
+
+/* RMSNorm over rows of 128: y = R16((x * rsqrt(mean(x^2) + eps)) * w), w of dtype w_dtype [128]. Replaces
+ * rms_norm_128()'s launch (enhancers/fused_block.py:127-139, kernel _rms128 fused_kernels.py:189-217). */
+WF_API int wf_rms_norm_128(const void *x, const void *w, int w_dtype, void *out, int64_t n_rows, float eps,
+                           wf_stream_t stream);
+
+/* RMSNorm-128 + split-half RoPE of a contiguous (batch, tokens, heads, 128) tensor with float32 rotations
+ * freqs[token, d, i, j] (element strides given; (1, tokens, 1, 64, 2, 2) contiguous is (256, 4, 2, 1)), weight w
+ * [128] of dtype w_dtype. Replaces rms_rope()'s launch (enhancers/sage_fused.py:325-334, kernels _rope_rows :159-176
+ * / _rms_rope128 :246-272). */
+WF_API int wf_rms_rope128(const void *x, const float *freqs, int64_t f_stride_token, int64_t f_stride_d,
+                          int64_t f_stride_i, int64_t f_stride_j, const void *w, int w_dtype, void *out,
+                          int64_t batch, int64_t tokens, int64_t heads, float eps, wf_stream_t stream);
+
+/* Per-token int8 quantisation of rows of K: q [rows, K] int8, scale [rows] float32 (scale = max(amax / 127,
+ * 1e-30)). pre: 0 none, 1 GELU by a 65536-entry bf16 table (gelu_table), 2 modulate (s1, shift), 3 LayerNorm +
+ * modulate (K % 512 == 0, K <= 8192); rotate: the 256-wide ConvRot Hadamard (K % 256 == 0) -- the reference always
+ * rotates, rotate = 0 is the plain absmax quantiser of BASELINE's W8A8 configuration. Replaces the quant_row launches
+ * of _quantise_pre / _int8_quantised (enhancers/fused_int8.py:60-75, :172-176; kernel fused_kernels.py:137-174). */
+WF_API int wf_quant_rows(const void *x, const void *s1, const void *shift, const void *gelu_table, int8_t *q,
+                         float *scale, int64_t rows, int64_t K, int64_t rows_per_group, float eps, int pre, int rotate,
+                         wf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -217,3 +217,216 @@ WFO_API int wfo_lora_add(const float *diff, void *w, int64_t n, int out, float s
 }
 
 WFO_API int wfo_max_threads(void) { return set_threads(0); }
+
+/* ================================================================================================ fused block */
+static inline float bf(uint16_t b) { return u2f((uint32_t)b << 16); }
+static inline uint16_t bf_bits(float x) { return isnan(x) ? (uint16_t)0x7FFF : (uint16_t)(f2u(r_bf16(x)) >> 16); }
+/* the reference's rsqrt.approx.f32, restated as the correctly rounded reciprocal square root */
+static inline float rsqrt_cr(float v) { return (float)(1.0 / sqrt((double)v)); }
+/* x moved by k float32 ulps (k < 0: toward -inf): the tests evaluate a row with each reciprocal square root within
+ * 2 ulps of the correctly rounded one, the error bound of the hardware approximation the kernels use */
+static inline float ulp_shift(float x, int k) {
+    while (k > 0) { x = nextafterf(x, INFINITY); --k; }
+    while (k < 0) { x = nextafterf(x, -INFINITY); ++k; }
+    return x;
+}
+
+/* modulate: out = R16(R16(x * s1) + shift), s1 = bf16(1 + scale) per group of rows
+ * (enhancers/fused_kernels.py:51-62 _mod; fused_block.py:103-124) */
+WFO_API void wfo_modulate(const uint16_t *x, const uint16_t *s1, const uint16_t *sh, uint16_t *out, int64_t rows,
+                          int64_t d, int64_t rows_per_group, int threads) {
+    set_threads(threads);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+        const int64_t g = r / rows_per_group;
+        for (int64_t c = 0; c < d; ++c) {
+            float t = r_bf16(bf(x[r * d + c]) * bf(s1[g * d + c]));
+            out[r * d + c] = bf_bits(t + bf(sh[g * d + c]));
+        }
+    }
+}
+
+/* PyTorch's vectorized layer-norm statistics of one row of K (K % 512 == 0) as the reference reproduces them
+ * (enhancers/fused_kernels.py:84-135 _wcombine / _whalf / _ln_stats): 128 threads, thread t updating a Welford
+ * (mean, sigma2, count) with the 4-value vectors t, t + 128, ... in order; lanes merged by shuffle-down 16 .. 1
+ * within each warp of 32, then warps 2, 3 into 0, 1 and warp 1 into 0. Returns mean and sigma2 / K. */
+static void ln_stats(const uint16_t *row, int64_t K, float *mu_out, float *var_out) {
+    float m[128], s[128], c[128];
+    for (int t = 0; t < 128; ++t) {
+        float mean = 0.f, sig = 0.f, cnt = 0.f;
+        for (int64_t j = 0; j < K / 512; ++j)
+            for (int ii = 0; ii < 4; ++ii) {
+                float v = bf(row[(t + j * 128) * 4 + ii]);
+                float delta = v - mean;
+                cnt = cnt + 1.0f;
+                mean = fmaf(delta, 1.0f / cnt, mean);
+                sig = fmaf(delta, v - mean, sig);
+            }
+        m[t] = mean; s[t] = sig; c[t] = cnt;
+    }
+    /* combine(own = lower lane, other = upper lane) as _wcombine */
+#define WCOMB(o, x)                                                   \
+    do {                                                              \
+        float delta = m[o] - m[x];                                    \
+        float count = c[x] + c[o];                                    \
+        float coef = 1.0f / count;                                    \
+        float n_a = c[x] * coef, n_b = c[o] * coef;                   \
+        float mean = fmaf(n_a, m[x], n_b * m[o]);                     \
+        float sig = fmaf(delta * delta * c[x], n_b, s[x] + s[o]);     \
+        m[o] = mean; s[o] = sig; c[o] = count;                        \
+    } while (0)
+    for (int w = 0; w < 4; ++w)
+        for (int n = 32; n >= 2; n /= 2)
+            for (int t = 0; t < n / 2; ++t) WCOMB(w * 32 + t, w * 32 + t + n / 2);
+    WCOMB(0, 64);
+    WCOMB(32, 96);
+    WCOMB(0, 32);
+#undef WCOMB
+    *mu_out = m[0];
+    *var_out = s[0] / (float)K;
+}
+
+/* LayerNorm (no affine) + modulate, one row (fused_kernels.py:219-232 _lnmod):
+ * x = R16((x - mu) * rsqrt(var + eps)); out = R16(R16(x * s1) + shift) */
+WFO_API void wfo_ln_modulate(const uint16_t *x, const uint16_t *s1, const uint16_t *sh, uint16_t *out, int64_t rows,
+                             int64_t K, int64_t rows_per_group, float eps, int rstd_ulps, int threads) {
+    set_threads(threads);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+        const uint16_t *xr = x + r * K;
+        const int64_t g = r / rows_per_group;
+        float mu, var;
+        ln_stats(xr, K, &mu, &var);
+        const float rstd = ulp_shift(rsqrt_cr(var + eps), rstd_ulps);
+        for (int64_t c = 0; c < K; ++c) {
+            float v = r_bf16((bf(xr[c]) - mu) * rstd);
+            float t = r_bf16(v * bf(s1[g * K + c]));
+            out[r * K + c] = bf_bits(t + bf(sh[g * K + c]));
+        }
+    }
+}
+
+/* RMSNorm over rows of 128 (fused_kernels.py:189-217 _rms128): thread t of 32 sums the squares of values 4t .. 4t+3
+ * as ((a + b) + c) + d, a pairwise tree 16 .. 1 over the threads, rstd = rsqrt(sum / 128 + eps),
+ * y = R16((x * rstd) * w) */
+WFO_API void wfo_rms_norm_128(const uint16_t *x, const uint16_t *w, uint16_t *out, int64_t n_rows, float eps,
+                              int rstd_ulps, int threads) {
+    set_threads(threads);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < n_rows; ++r) {
+        const uint16_t *xr = x + r * 128;
+        float acc[32];
+        for (int t = 0; t < 32; ++t) {
+            float a = bf(xr[4 * t]), b = bf(xr[4 * t + 1]), c = bf(xr[4 * t + 2]), d = bf(xr[4 * t + 3]);
+            acc[t] = ((a * a + b * b) + c * c) + d * d;
+        }
+        for (int n = 32; n >= 2; n /= 2)
+            for (int t = 0; t < n / 2; ++t) acc[t] = acc[t] + acc[t + n / 2];
+        const float rstd = ulp_shift(rsqrt_cr(acc[0] / 128.0f + eps), rstd_ulps);
+        for (int c = 0; c < 128; ++c) out[r * 128 + c] = bf_bits((bf(xr[c]) * rstd) * bf(w[c]));
+    }
+}
+
+/* RMSNorm-128 + split-half RoPE of contiguous (B, L, H, 128) rows (sage_fused.py:246-272 _rms_rope128, :159-176
+ * _rope_rows): lane t of 32 sums the squares of values t, t+32, t+64, t+96 by fma from 0, a pairwise tree 16 .. 1,
+ * rr = rsqrt(sum / 128 + eps), n = R16((x * rr) * w); then for d < 64, with f = freqs[token, d] (2 x 2, float32):
+ * out[d] = R16(fma(f00, n[d], f01 * n[d+64])), out[d+64] = R16(fma(f10, n[d], f11 * n[d+64])).
+ * w is given as float32 (the reference loads bf16 / fp16 / fp32 weights and widens them). */
+WFO_API void wfo_rms_rope128(const uint16_t *x, const float *freqs, const float *w, uint16_t *out, int64_t n_rows,
+                             int64_t heads, int64_t tokens, float eps, int rstd_ulps, int threads) {
+    set_threads(threads);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < n_rows; ++r) {
+        const uint16_t *xr = x + r * 128;
+        const int64_t tok = (r / heads) % tokens;
+        float acc[32];
+        for (int t = 0; t < 32; ++t) {
+            float v0 = bf(xr[t]), v1 = bf(xr[t + 32]), v2 = bf(xr[t + 64]), v3 = bf(xr[t + 96]);
+            float a = v0 * v0;
+            a = fmaf(v1, v1, a);
+            a = fmaf(v2, v2, a);
+            a = fmaf(v3, v3, a);
+            acc[t] = a;
+        }
+        for (int n = 32; n >= 2; n /= 2)
+            for (int t = 0; t < n / 2; ++t) acc[t] = acc[t] + acc[t + n / 2];
+        const float rr = ulp_shift(rsqrt_cr(acc[0] / 128.0f + eps), rstd_ulps);
+        float nv[128];
+        for (int c = 0; c < 128; ++c) nv[c] = r_bf16((bf(xr[c]) * rr) * w[c]);
+        for (int d = 0; d < 64; ++d) {
+            const float *f = freqs + (tok * 64 + d) * 4;
+            float lo = nv[d], hi = nv[d + 64];
+            out[r * 128 + d] = bf_bits(fmaf(f[0], lo, f[1] * hi));
+            out[r * 128 + d + 64] = bf_bits(fmaf(f[2], lo, f[3] * hi));
+        }
+    }
+}
+
+/* 256-wide Hadamard of comfy_kitchen's ConvRot as the reference computes it (fused_kernels.py:64-81 _h4): four
+ * radix-4 stages of stride 1, 4, 16, 64, each mapping the 4-tuple (a, b, c, d) at stride S to
+ * (a + b + c - d, a + b - c + d, a - b + c + d, -a + b + c + d) summed left to right; then x 1/16. */
+static void hadamard256(float *g) {
+    for (int S = 1; S <= 64; S *= 4) {
+        float y[256];
+        for (int blk = 0; blk < 256 / (4 * S); ++blk)
+            for (int s = 0; s < S; ++s) {
+                int base = blk * 4 * S + s;
+                float a = g[base], b = g[base + S], c = g[base + 2 * S], d = g[base + 3 * S];
+                y[base] = ((a + b) + c) - d;
+                y[base + S] = ((a + b) - c) + d;
+                y[base + 2 * S] = ((a - b) + c) + d;
+                y[base + 3 * S] = ((-a + b) + c) + d;
+            }
+        memcpy(g, y, sizeof(y));
+    }
+    for (int i = 0; i < 256; ++i) g[i] = g[i] * 0.0625f;
+}
+
+/* int8 row quantiser (fused_kernels.py:137-174 _quant_row). pre: 0 none, 1 GELU by table (gelu[bits of x]),
+ * 2 modulate, 3 LayerNorm + modulate. rotate: the ConvRot Hadamard (the reference always rotates; rotate = 0 is the
+ * plain per-token absmax quantiser of the same arithmetic). amax = min(max |x|, 3.38953139e38),
+ * scale = max(amax / 127, 1e-30) (stored), q = rint(R16(R16(x) / R16(scale))) clamped to [-128, 127].
+ * The reference divides with the GPU's approximate division; this restatement divides exactly (IEEE). */
+WFO_API void wfo_quant_rows(const uint16_t *x, const uint16_t *s1, const uint16_t *sh, const uint16_t *gelu,
+                            int8_t *q, float *scale_out, int64_t rows, int64_t K, int64_t rows_per_group, float eps,
+                            int pre, int rotate, int threads) {
+    set_threads(threads);
+#pragma omp parallel
+    {
+        float *v = (float *)__builtin_alloca(sizeof(float) * (size_t)K);
+#pragma omp for schedule(static)
+        for (int64_t r = 0; r < rows; ++r) {
+            const uint16_t *xr = x + r * K;
+            const int64_t g = r / rows_per_group;
+            if (pre == 3) {
+                float mu, var;
+                ln_stats(xr, K, &mu, &var);
+                const float rstd = rsqrt_cr(var + eps);
+                for (int64_t c = 0; c < K; ++c) {
+                    float t = r_bf16((bf(xr[c]) - mu) * rstd);
+                    v[c] = r_bf16(r_bf16(t * bf(s1[g * K + c])) + bf(sh[g * K + c]));
+                }
+            } else if (pre == 1) {
+                for (int64_t c = 0; c < K; ++c) v[c] = bf(gelu[xr[c]]);
+            } else if (pre == 2) {
+                for (int64_t c = 0; c < K; ++c)
+                    v[c] = r_bf16(r_bf16(bf(xr[c]) * bf(s1[g * K + c])) + bf(sh[g * K + c]));
+            } else {
+                for (int64_t c = 0; c < K; ++c) v[c] = bf(xr[c]);
+            }
+            if (rotate)
+                for (int64_t c = 0; c < K; c += 256) hadamard256(v + c);
+            float amax = 0.f;
+            for (int64_t c = 0; c < K; ++c) amax = fmaxf(amax, fabsf(v[c]));
+            amax = fminf(amax, 3.38953139e38f);
+            float scale = fmaxf(amax / 127.0f, 1.0e-30f);
+            scale_out[r] = scale;
+            const float sb = r_bf16(scale);
+            for (int64_t c = 0; c < K; ++c) {
+                float t = rintf(r_bf16(r_bf16(v[c]) / sb));
+                t = fminf(fmaxf(t, -128.0f), 127.0f);
+                q[r * K + c] = (int8_t)t;
+            }
+        }
+    }
+}

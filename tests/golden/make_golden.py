@@ -93,6 +93,14 @@ def patch_interpreter():
     def create_fma(self, x, y, z):
         return it.TensorHandle(_fma_exact_checked(x.data, y.data, z.data), z.dtype.scalar)
 
+    # libdevice.rint outside the builder: the interpreter does not route tl.extra.cuda.libdevice through it
+    import triton.language as tl
+    from triton.language.extra.cuda import libdevice
+
+    def rint(x, _semantic=None, **_kw):
+        return tl.tensor(it.TensorHandle(np.rint(x.handle.data).astype(x.handle.data.dtype), x.handle.dtype), x.type)
+    libdevice.rint = rint
+
     B.create_inline_asm = create_inline_asm
     B.create_extern_elementwise = create_extern_elementwise
     B.create_fma = create_fma
@@ -222,6 +230,87 @@ def make_gguf(ref):
     print("gguf_dequant.npz:", len(out), "arrays")
 
 
+def _bf16_bits(t):
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def make_fused(ref):
+    """The fused-block kernels: _mod, _lnmod, _rms128 (fused_kernels.py), _rope_rows (sage_fused.py) and the int8
+    row quantiser _quant_row with each PRE operation (fused_kernels.py:137-174)."""
+    import triton
+    fk = load_ref(ref, "enhancers/fused_kernels.py", "fused_kernels")
+    ks = fk._get_kernels()
+    hoist_closures(fk, [ks[k].fn for k in ks])
+    sf = load_ref(ref, "enhancers/sage_fused.py", "sage_fused")
+    sf._get_kernel()
+    g = torch.Generator().manual_seed(SEED + 7)
+    out = {}
+    # modulate: rows of D = 1024 in 3 groups of 4 rows
+    R, D, RPG = 12, 1024, 4
+    x = (torch.randn(R, D, generator=g) * 1.5).to(torch.bfloat16)
+    x[0, :8] = torch.tensor([0.0, -0.0, 1e-30, 3e38, -3e38, 65504.0, 1.0, -1.0])
+    scale = (torch.randn(R // RPG, D, generator=g) * 0.1).to(torch.bfloat16)
+    shift = (torch.randn(R // RPG, D, generator=g) * 0.1).to(torch.bfloat16)
+    s1 = (1 + scale).contiguous()  # the bf16 (1 + scale) the reference's host code makes
+    o = torch.empty_like(x)
+    ks["mod"].fn[(R,)](x, s1, shift, o, D, RPG, BLOCK=D)
+    out.update(mod_x=_bf16_bits(x), mod_s1=_bf16_bits(s1), mod_shift=_bf16_bits(shift), mod_out=_bf16_bits(o),
+               mod_rpg=np.array([RPG]))
+    # LayerNorm (no affine, eps 1e-6) + modulate: K = 1024 and 2048
+    for K in (1024, 2048):
+        xl = (torch.randn(R, K, generator=g) * 2.0 + 0.3).to(torch.bfloat16)
+        sc = (torch.randn(R // RPG, K, generator=g) * 0.1).to(torch.bfloat16)
+        sh = (torch.randn(R // RPG, K, generator=g) * 0.1).to(torch.bfloat16)
+        s1 = (1 + sc).contiguous()
+        o = torch.empty_like(xl)
+        ks["lnmod"].fn[(R,)](xl, s1, sh, o, RPG, 1e-6, K=K)
+        out.update({f"lnmod{K}_x": _bf16_bits(xl), f"lnmod{K}_s1": _bf16_bits(s1), f"lnmod{K}_shift": _bf16_bits(sh),
+                    f"lnmod{K}_out": _bf16_bits(o)})
+    # RMSNorm over 128 (rs 0: rsqrt.approx), 40 rows (two programs of 32, the second masked)
+    n = 40
+    xr = (torch.randn(n, 128, generator=g) * 1.2).to(torch.bfloat16)
+    w = (1 + torch.randn(128, generator=g) * 0.02).to(torch.bfloat16)
+    o = torch.empty_like(xr)
+    ks["rms128"].fn[(triton.cdiv(n, 32),)](xr, w, o, n, 1e-6, ROWS=32, RS=0)
+    out.update(rms_x=_bf16_bits(xr), rms_w=_bf16_bits(w), rms_out=_bf16_bits(o))
+    # RMSNorm-128 + split-half RoPE on (B, L, H, 128) with rotations (1, L, 1, 64, 2, 2) float32
+    B, L, H = 2, 6, 4
+    xq = (torch.randn(B, L, H, 128, generator=g)).to(torch.bfloat16)
+    ang = torch.rand(L, 64, generator=g) * 6.2831853
+    f = torch.stack([torch.cos(ang), -torch.sin(ang), torch.sin(ang), torch.cos(ang)], dim=-1)
+    f = f.reshape(1, L, 1, 64, 2, 2).float().contiguous()
+    wq = (1 + torch.randn(128, generator=g) * 0.02).to(torch.bfloat16)
+    o = torch.empty_like(xq)
+    n = B * L * H
+    sf._kernel["rope_rows"][(triton.cdiv(n, 32),)](xq, f, wq, o, n, H, L, 1e-6, f.stride(1), f.stride(3),
+                                                   f.stride(4), f.stride(5), ROWS=32)
+    out.update(rope_x=_bf16_bits(xq), rope_f=f.numpy().copy(), rope_w=_bf16_bits(wq), rope_out=_bf16_bits(o),
+               rope_shape=np.array([B, L, H]))
+    # int8 row quantiser with rotation (ConvRot 256): PRE none / gelu / mod / lnmod, K = 1024, 12 rows
+    K = 1024
+    xs = (torch.randn(R, K, generator=g) * 1.3).to(torch.bfloat16)
+    xs[3] = 0  # an all-zero row: scale 1e-30, int8 0
+    sc = (torch.randn(R // RPG, K, generator=g) * 0.1).to(torch.bfloat16)
+    sh = (torch.randn(R // RPG, K, generator=g) * 0.1).to(torch.bfloat16)
+    s1 = (1 + sc).contiguous()
+    allbf = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    gelu_tab = torch.nn.functional.gelu(allbf).contiguous()
+    out.update(q_x=_bf16_bits(xs), q_s1=_bf16_bits(s1), q_shift=_bf16_bits(sh), q_gelu=_bf16_bits(gelu_tab))
+    for pre in (0, 1, 2, 3):
+        q = torch.empty(R, K, dtype=torch.int8)
+        qs = torch.empty(R, 1, dtype=torch.float32)
+        if pre == 1:
+            ks["quant_row"].fn[(R,)](xs, gelu_tab, xs, q, qs, 1, 0.0, K=K, PRE=1)
+        elif pre == 0:
+            ks["quant_row"].fn[(R,)](xs, xs, xs, q, qs, 1, 0.0, K=K, PRE=0)
+        else:
+            ks["quant_row"].fn[(R,)](xs, s1, sh, q, qs, RPG, 1e-6, K=K, PRE=pre)
+        out[f"q_pre{pre}_q"] = q.numpy().copy()
+        out[f"q_pre{pre}_scale"] = qs.numpy().reshape(-1).copy()
+    np.savez_compressed(os.path.join(HERE, "fused_block.npz"), **out)
+    print("fused_block.npz:", len(out), "arrays")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="the ComfyUI-WeightFerry source folder")
@@ -230,6 +319,8 @@ def main():
     patch_interpreter()
     if a.only in (None, "gguf"):
         make_gguf(a.ref)
+    if a.only in (None, "fused"):
+        make_fused(a.ref)
 
 
 if __name__ == "__main__":

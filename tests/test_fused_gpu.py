@@ -1,0 +1,261 @@
+"""Fused-block prologue kernels on the GPU through the C ABI / the drop-in functions, against the reference's golden
+vectors and the CPU oracle.
+
+Tolerances: modulate is exact (no approximation on either side). The kernels that go through the hardware
+rsqrt.approx (LayerNorm + modulate, RMSNorm-128, RMSNorm + RoPE) compute one reciprocal square root per row; the
+goldens and the oracle use the correctly rounded one. Each row must therefore equal, bit for bit, the oracle's row
+computed with a reciprocal square root within 2 float32 ulps of the correctly rounded one (the approximation's
+bound) -- a tighter check than "2 bf16 ulps" of the outputs, which a cancellation in x * (1 + scale) + shift would
+make meaningless. The quantiser divides with the hardware's approximate division like the reference on the GPU, so
+its scales are within 2 float32 ulps of the exact-division goldens and its int8 values within 1 of them, on a
+handful of values at most."""
+
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, oracle, wf
+
+pytestmark = pytest.mark.gpu
+
+F = np.load(os.path.join(GOLDEN, "fused_block.npz"))
+
+
+def _t(bits, shape=None):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).cuda()
+    return t.reshape(shape) if shape is not None else t
+
+
+def _bits(t):
+    import torch
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16).reshape(-1)
+
+
+def _ord(b):
+    b = b.astype(np.int32)
+    return np.where(b & 0x8000, -(b & 0x7FFF), b)
+
+
+def ulp16(a, b):
+    return np.abs(_ord(np.asarray(a).reshape(-1)) - _ord(np.asarray(b).reshape(-1)))
+
+
+def test_modulate_golden(cuda):
+    fk = wf("enhancers.fused_kernels")
+    import torch
+    x = _t(F["mod_x"])
+    o = torch.empty_like(x)
+    fk._get_kernels()["mod"][(12,)](x, _t(F["mod_s1"]), _t(F["mod_shift"]), o, 1024, int(F["mod_rpg"][0]))
+    assert np.array_equal(_bits(o), F["mod_out"].reshape(-1))
+
+
+def test_modulate_entry_point_baseline_shape(cuda):
+    """modulate() on BASELINE configs[3]: x (2, 1, 64, 64, 2048), scale / shift (2, 1, 1, 1, 2048)."""
+    import torch
+    fb = wf("enhancers.fused_block")
+    g = torch.Generator(device="cuda").manual_seed(20261201 + 3)
+    x = torch.randn((2, 1, 64, 64, 2048), device="cuda", generator=g).to(torch.bfloat16)
+    sc = (torch.randn((2, 1, 1, 1, 2048), device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    sh = (torch.randn((2, 1, 1, 1, 2048), device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    out = fb.modulate(x, sc, sh)
+    ref = oracle().modulate(_bits(x).reshape(-1, 2048), _bits((1 + sc).contiguous()).reshape(2, 2048),
+                            _bits(sh).reshape(2, 2048), 64 * 64)
+    assert np.array_equal(_bits(out), ref.reshape(-1))
+    # and PyTorch's own two bf16 kernels give the same bits
+    assert torch.equal(out, x * (1 + sc) + sh)
+
+
+@pytest.mark.parametrize("K", [1024, 2048])
+def test_ln_modulate_golden(cuda, K):
+    import torch
+    fk = wf("enhancers.fused_kernels")
+    x = _t(F[f"lnmod{K}_x"])
+    o = torch.empty_like(x)
+    fk._get_kernels()["lnmod"][(12,)](x, _t(F[f"lnmod{K}_s1"]), _t(F[f"lnmod{K}_shift"]), o, 4, 1e-6, K=K)
+    got = _bits(o)
+    exact = np.all(got.reshape(12, K) == F[f"lnmod{K}_out"].reshape(12, K), axis=1)
+    ok = oracle().rows_match_some_rstd(got, lambda k: oracle().ln_modulate(
+        F[f"lnmod{K}_x"].reshape(12, K), F[f"lnmod{K}_s1"], F[f"lnmod{K}_shift"], 4, 1e-6, rstd_ulps=k), K)
+    assert (exact | ok).all()
+
+
+def test_ln_modulate_baseline_vs_oracle_and_torch(cuda):
+    """Kernel A at BASELINE configs[3] (8192 rows of 2048) against the oracle (2 ulp) and against PyTorch's own
+    LayerNorm + two bf16 kernels (2 ulp)."""
+    import torch
+    fb = wf("enhancers.fused_block")
+    g = torch.Generator(device="cuda").manual_seed(20261201 + 3)
+    x = torch.randn((2, 1, 64, 64, 2048), device="cuda", generator=g).to(torch.bfloat16)
+    sc = (torch.randn((2, 1, 1, 1, 2048), device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    sh = (torch.randn((2, 1, 1, 1, 2048), device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    out = fb.ln_modulate_rows(x, sc, sh, 1e-6)
+    xb, s1b, shb = _bits(x).reshape(-1, 2048), _bits((1 + sc).contiguous()).reshape(2, 2048), _bits(sh).reshape(2, 2048)
+    ok = oracle().rows_match_some_rstd(_bits(out), lambda k: oracle().ln_modulate(xb, s1b, shb, 4096, 1e-6,
+                                                                                  rstd_ulps=k), 2048)
+    assert ok.all(), f"{(~ok).sum()} rows"
+    # PyTorch's own LayerNorm (the same vectorized Welford order and hardware rsqrt) then its two bf16 kernels
+    norm = torch.nn.LayerNorm(2048, elementwise_affine=False, eps=1e-6)
+    pt = norm(x) * (1 + sc) + sh
+    same = torch.eq(out.view(torch.int16), pt.view(torch.int16)).all(dim=-1).float().mean().item()
+    assert same > 0.999, f"rows bit-identical with PyTorch: {same}"
+
+
+@pytest.mark.parametrize("K", [512, 1536, 5120])
+def test_ln_modulate_other_widths_vs_oracle(cuda, K):
+    import torch
+    lib, ext = wf("_ext").lib(), wf("_ext")
+    g = torch.Generator(device="cuda").manual_seed(K)
+    rows = 300
+    x = (torch.randn((rows, K), device="cuda", generator=g) * 3 - 1).to(torch.bfloat16)
+    s1 = (1 + torch.randn((3, K), device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    sh = (torch.randn((3, K), device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    o = torch.empty_like(x)
+    ext.check(lib.wf_ln_modulate(x.data_ptr(), s1.data_ptr(), sh.data_ptr(), o.data_ptr(), rows, K, 100, 1e-5,
+                                 ext.stream_of(x.device)), "ln")
+    xb, s1b, shb = _bits(x).reshape(rows, K), _bits(s1).reshape(3, K), _bits(sh).reshape(3, K)
+    ok = oracle().rows_match_some_rstd(_bits(o), lambda k: oracle().ln_modulate(xb, s1b, shb, 100, 1e-5,
+                                                                                rstd_ulps=k), K)
+    assert ok.all()
+
+
+def test_rms_norm_128_golden_and_torch(cuda):
+    import torch
+    fb = wf("enhancers.fused_block")
+    x = _t(F["rms_x"], (40, 128))
+    w = _t(F["rms_w"])
+    out = fb.rms_norm_128(x, w, 1e-6)
+    ok = oracle().rows_match_some_rstd(_bits(out), lambda k: oracle().rms_norm_128(F["rms_x"], F["rms_w"], 1e-6,
+                                                                                   rstd_ulps=k), 128)
+    assert ok.all()
+    big = torch.randn((2, 4096, 16, 128), device="cuda").to(torch.bfloat16)
+    o2 = fb.rms_norm_128(big, w, 1e-6)
+    bb, wb = _bits(big).reshape(-1, 128), _bits(w)
+    ok = oracle().rows_match_some_rstd(_bits(o2), lambda k: oracle().rms_norm_128(bb, wb, 1e-6, rstd_ulps=k), 128)
+    assert ok.all()
+    pt = torch.nn.functional.rms_norm(big, (128,), w, 1e-6)
+    same = torch.eq(o2.view(torch.int16), pt.view(torch.int16)).all(dim=-1).float().mean().item()
+    assert same > 0.99, f"rows bit-identical with PyTorch's rms_norm: {same}"
+    assert fb.rms_norm_128(big.float(), w, 1e-6) is None
+
+
+def test_rms_rope_golden(cuda):
+    import torch
+    sf = wf("enhancers.sage_fused")
+    B, L, H = (int(v) for v in F["rope_shape"])
+    x = _t(F["rope_x"], (B, L, H, 128))
+    f = torch.from_numpy(F["rope_f"]).cuda()
+    w = _t(F["rope_w"])
+    out = sf.rms_rope(x, f, w, 1e-6)
+    wf32 = (F["rope_w"].astype(np.uint32) << 16).view(np.float32)
+    ok = oracle().rows_match_some_rstd(_bits(out), lambda k: oracle().rms_rope128(
+        F["rope_x"], F["rope_f"], wf32, H, L, 1e-6, rstd_ulps=k), 128)
+    assert ok.all()
+
+
+def rope3d_table(T, H, W, theta=10000.0, h_extra=4.0, w_extra=4.0, t_extra=1.0):
+    """Cosmos-Predict2's 3D RoPE rotations (1, T*H*W, 1, 64, 2, 2): head dim 128 -> 42 h / 42 w / 44 t channels,
+    NTK factors from the extrapolation ratios, tokens in (t h w) order, t then h then w frequencies."""
+    import torch
+    dim_h, dim_t = 42, 44
+    rng_hw = torch.arange(0, dim_h, 2, dtype=torch.float64) / dim_h
+    rng_t = torch.arange(0, dim_t, 2, dtype=torch.float64) / dim_t
+    h_ntk = h_extra ** (dim_h / (dim_h - 2))
+    w_ntk = w_extra ** (dim_h / (dim_h - 2))
+    t_ntk = t_extra ** (dim_t / (dim_t - 2))
+    hf = 1.0 / ((theta * h_ntk) ** rng_hw)
+    wf_ = 1.0 / ((theta * w_ntk) ** rng_hw)
+    tf = 1.0 / ((theta * t_ntk) ** rng_t)
+    ht, wt, tt = torch.outer(torch.arange(H).double(), hf), torch.outer(torch.arange(W).double(), wf_), \
+        torch.outer(torch.arange(T).double(), tf)
+
+    def rot(e):
+        return torch.stack([torch.cos(e), -torch.sin(e), torch.sin(e), torch.cos(e)], dim=-1)
+    ht, wt, tt = rot(ht), rot(wt), rot(tt)
+    em = torch.cat([tt[:, None, None].expand(T, H, W, 22, 4), ht[None, :, None].expand(T, H, W, 21, 4),
+                    wt[None, None, :].expand(T, H, W, 21, 4)], dim=-2)
+    return em.reshape(1, T * H * W, 1, 64, 2, 2).float().contiguous()
+
+
+def test_rms_rope_baseline_vs_oracle(cuda):
+    """Kernel B at BASELINE configs[3]: q, k (2, 4096, 16, 128) with the 3D RoPE of 1 x 64 x 64 latent patches."""
+    import torch
+    sf = wf("enhancers.sage_fused")
+    g = torch.Generator(device="cuda").manual_seed(20261201 + 3)
+    q = torch.randn((2, 4096, 16, 128), device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn((2, 4096, 16, 128), device="cuda", generator=g).to(torch.bfloat16)
+    wq = (1 + torch.randn(128, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    wk = (1 + torch.randn(128, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    f = rope3d_table(1, 64, 64).cuda()
+    assert sf.rope_ok(q, k, f, wq, wk, 1e-6)
+    qo, ko = sf.rms_rope_pair(q, k, f, wq, wk, 1e-6)
+    fn = f.cpu().numpy()
+    for src, w, o in ((q, wq, qo), (k, wk, ko)):
+        wf32 = w.float().cpu().numpy()
+        sb = _bits(src).reshape(2, 4096, 16, 128)
+        ok = oracle().rows_match_some_rstd(_bits(o), lambda kk: oracle().rms_rope128(sb, fn, wf32, 16, 4096, 1e-6,
+                                                                                    rstd_ulps=kk), 128)
+        assert ok.all()
+
+
+@pytest.mark.parametrize("pre", [0, 1, 2, 3])
+def test_quant_rows_golden(cuda, pre):
+    import torch
+    fk = wf("enhancers.fused_kernels")
+    x = _t(F["q_x"], (12, 1024))
+    s = _t(F["q_gelu"]) if pre == 1 else _t(F["q_s1"], (3, 1024))
+    h = _t(F["q_shift"], (3, 1024))
+    q = torch.empty((12, 1024), dtype=torch.int8, device="cuda")
+    sc = torch.empty((12, 1), dtype=torch.float32, device="cuda")
+    rpg, eps = (4, 1e-6) if pre in (2, 3) else (1, 0.0)
+    fk._get_kernels()["quant_row"][(12,)](x, s, h, q, sc, rpg, eps, K=1024, PRE=pre)
+    torch.cuda.synchronize()
+    gs = F[f"q_pre{pre}_scale"]
+    got_s = sc.cpu().numpy().reshape(-1)
+    assert np.max(np.abs(got_s.view(np.int32).astype(np.int64) - gs.view(np.int32).astype(np.int64))) <= 2
+    dq = np.abs(q.cpu().numpy().astype(np.int32) - F[f"q_pre{pre}_q"].astype(np.int32))
+    assert dq.max() <= 1 and (dq > 0).sum() <= 8
+
+
+def test_quant_rows_plain_baseline_vs_oracle(cuda):
+    """The plain per-token absmax quantiser at BASELINE configs[2] (X [8192, 2048] ~ N(0, 1))."""
+    import torch
+    fk = wf("enhancers.fused_kernels")
+    g = torch.Generator(device="cuda").manual_seed(20261201 + 2)
+    x = torch.randn((8192, 2048), device="cuda", generator=g).to(torch.bfloat16)
+    x_q, x_s = fk.quantize_rows(x, rotate=False)
+    torch.cuda.synchronize()
+    rq, rs = oracle().quant_rows(_bits(x).reshape(8192, 2048), pre=0, rotate=False)
+    ds = np.abs(x_s.cpu().numpy().reshape(-1).view(np.int32).astype(np.int64) - rs.view(np.int32).astype(np.int64))
+    assert ds.max() <= 2
+    dq = np.abs(x_q.cpu().numpy().astype(np.int32) - rq.astype(np.int32))
+    assert dq.max() <= 1 and (dq > 0).mean() < 1e-4
+
+
+def test_quant_rows_rotated_ragged_rows(cuda):
+    import torch
+    fk = wf("enhancers.fused_kernels")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    for k in (256, 768, 5120):
+        x = (torch.randn((33, k), device="cuda", generator=g) * 4).to(torch.bfloat16)
+        x[7] = 0
+        x_q, x_s = fk.quantize_rows(x, rotate=True)
+        torch.cuda.synchronize()
+        rq, rs = oracle().quant_rows(_bits(x).reshape(33, k), pre=0, rotate=True)
+        assert float(x_s[7, 0]) == 1e-30 or abs(float(x_s[7, 0]) - 1e-30) < 1e-36
+        dq = np.abs(x_q.cpu().numpy().astype(np.int32) - rq.astype(np.int32))
+        assert dq.max() <= 1 and (dq > 0).sum() <= 4
+
+
+def test_fused_c_abi_rejections(cuda):
+    import torch
+    ext = wf("_ext")
+    L = ext.lib()
+    x = torch.zeros((4, 1000), dtype=torch.bfloat16, device="cuda")
+    st = ext.stream_of(x.device)
+    p = x.data_ptr()
+    assert L.wf_ln_modulate(p, p, p, p, 4, 1000, 1, 1e-6, st) == -1     # K not a multiple of 512
+    assert L.wf_modulate(p, p, p, p, 4, 1001, 1, st) == -1              # d not a multiple of 8
+    assert L.wf_quant_rows(p, None, None, None, p, p, 4, 1000, 1, 0.0, 0, 1, st) == -1  # rotate needs K % 256
+    assert L.wf_quant_rows(p, None, None, None, p, p, 4, 1024, 1, 0.0, 2, 0, st) == -1  # modulate needs s1 / shift

@@ -64,3 +64,42 @@ def test_oracle_f32_matches_gguf_py(qt):
     ref = gguf.quants.dequantize(raw.reshape(-1, ts), gguf.GGMLQuantizationType(qt)).reshape(-1).astype(np.float32)
     got = oracle().dequant_gguf(raw, n, qt, 2, 2)
     assert _same_bits(got, ref)
+
+
+# ---------------------------------------------------------------------------------------------- fused block
+F = np.load(os.path.join(GOLDEN, "fused_block.npz"))
+
+
+def test_modulate_matches_reference_kernel():
+    got = oracle().modulate(F["mod_x"], F["mod_s1"], F["mod_shift"], int(F["mod_rpg"][0]))
+    assert np.array_equal(got, F["mod_out"])
+
+
+@pytest.mark.parametrize("K", [1024, 2048])
+def test_ln_modulate_matches_reference_kernel(K):
+    got = oracle().ln_modulate(F[f"lnmod{K}_x"], F[f"lnmod{K}_s1"], F[f"lnmod{K}_shift"], 4, 1e-6)
+    assert np.array_equal(got, F[f"lnmod{K}_out"])
+
+
+def test_rms_norm_128_matches_reference_kernel():
+    got = oracle().rms_norm_128(F["rms_x"], F["rms_w"], 1e-6)
+    assert np.array_equal(got, F["rms_out"])
+
+
+def test_rms_rope128_matches_reference_kernel():
+    B, L, H = (int(v) for v in F["rope_shape"])
+    w = (F["rope_w"].astype(np.uint32) << 16).view(np.float32)
+    got = oracle().rms_rope128(F["rope_x"], F["rope_f"], w, H, L, 1e-6)
+    assert np.array_equal(got, F["rope_out"])
+
+
+@pytest.mark.parametrize("pre", [0, 1, 2, 3])
+def test_quant_rows_matches_reference_kernel(pre):
+    kw = dict(pre=pre, rotate=True)
+    if pre == 1:
+        kw.update(gelu=F["q_gelu"])
+    if pre in (2, 3):
+        kw.update(s1=F["q_s1"], shift=F["q_shift"], rows_per_group=4, eps=1e-6)
+    q, sc = oracle().quant_rows(F["q_x"], **kw)
+    assert np.array_equal(sc.view(np.uint32), F[f"q_pre{pre}_scale"].view(np.uint32))
+    assert np.array_equal(q, F[f"q_pre{pre}_q"])
