@@ -1,0 +1,400 @@
+// W8A8 linear for sm_100a: y[m, n] = bf16( float(acc[m, n]) * x_s[m] * w_s[n] ), acc = sum_k xq[m, k] * wq[n, k]
+// (int8 x int8 -> int32), the GEMM and epilogue behind the reference's int8 linear (enhancers/fused_int8.py:191-206,
+// which calls comfy_kitchen's compiled CUTLASS kernel; the arithmetic here is this library's own, with the epilogue
+// order written below).
+//
+// Blackwell-native structure, one persistent CTA per SM (192 threads):
+//   warp 4      TMA producer: 128x128 tiles of xq and 256x128 tiles of wq (K-major, 128-byte swizzle) into a
+//               4-stage shared-memory ring, completion counted on an mbarrier per stage;
+//   warp 5      MMA issuer: one thread issues tcgen05.mma.cta_group::1.kind::i8 (M=128, N=256, K=32; 4 per stage)
+//               with int32 accumulation in tensor memory; tcgen05.commit releases each stage and, per tile, hands
+//               the accumulator to the epilogue. Two 256-column accumulators (all 512 TMEM columns) let tile i+1's
+//               MMAs run while tile i is written out;
+//   warps 0..3  epilogue: warp w reads TMEM lanes 32w..32w+31 (one output row per thread) with tcgen05.ld,
+//               y = bf16_rn((float(acc) * x_s[m]) * w_s[n]) (two float32 products, rounded to nearest each),
+//               optional raw int32 copy of the accumulators, 16-byte stores.
+// Every mbarrier wait is bounded in time (about 2 s): on expiry the CTA records an error code (read with
+// wf_w8a8_gemm_status), stops issuing work, waits (bounded) for its own copies and MMAs in flight, frees its tensor
+// memory and returns. No load in this file uses cluster multicast; operands are always this GPU's own memory.
+
+#include "wf_common.cuh"
+
+#include <cuda.h>
+
+#include <mutex>
+
+namespace wf {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
+constexpr int A_STAGE = BM * BK;  // 16 KB
+constexpr int B_STAGE = BN * BK;  // 32 KB
+constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;  // ring + alignment slack + barriers
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// instruction descriptor of kind::i8: D int32 (bits 4-5 = 2), A and B signed int8 (bits 7-9, 10-12 = 1), both
+// K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) | ((BM >> 4) << 24);
+
+__device__ int g_gemm_status;  // 0 ok; 1 producer wait expired; 2 MMA wait expired; 3 epilogue wait expired
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t a, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t a) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase of the given parity, at most kWaitLimitNs; gives up early when another role aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile int *abort_flag, int code) {
+    if (mbar_try(a, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try(a, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicCAS(&g_gemm_status, 0, code);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1, uint32_t mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(mbar)
+        : "memory");
+}
+
+// shared-memory matrix descriptor: K-major, 128-byte swizzle, rows 128 B apart, 8-row groups 1024 B apart
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);        // start address
+    d |= static_cast<uint64_t>(1u) << 16;                      // leading byte offset (16 B; unused when swizzled)
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;              // stride byte offset
+    d |= static_cast<uint64_t>(1u) << 46;                      // descriptor version (Blackwell)
+    d |= static_cast<uint64_t>(2u) << 61;                      // SWIZZLE_128B
+    return d;
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                 const float *__restrict__ xs, const float *__restrict__ ws, __nv_bfloat16 *__restrict__ y,
+                 int32_t *__restrict__ acc_out, int M, int N, int K) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte aligned ring (the 128-byte swizzle pattern repeats every 8 rows of 128 bytes)
+    uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + STAGES * STAGE_BYTES);
+    // bars: full[0..3], empty[0..3], tmem_full[0..1], tmem_empty[0..1], drain
+    __shared__ uint32_t s_tmem_base;
+    __shared__ int s_abort;
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), tfull0 = smem_u32(bars + 2 * STAGES),
+                   tempty0 = smem_u32(bars + 2 * STAGES + 2), drain = smem_u32(bars + 2 * STAGES + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
+    const int n_tiles = tiles_m * tiles_n;
+    const int kb_count = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull0 + 8 * b, 1);
+            mbar_init(tempty0 + 8 * b, 4 * 32);
+        }
+        mbar_init(drain, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 5) {  // the MMA warp owns the tensor memory
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(&s_tmem_base)), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem_base = s_tmem_base;
+    volatile int *abort_flag = &s_abort;
+
+    if (warp == 4) {
+        // ------------------------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_a)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_b)) : "memory");
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_phase[STAGES];
+            bool pending[STAGES];
+            for (int s = 0; s < STAGES; ++s) pending[s] = false, issued_phase[s] = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+                for (int kb = 0; kb < kb_count; ++kb) {
+                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, abort_flag, 1)) { ok = false; break; }
+                    const uint32_t fb = full0 + 8 * stage;
+                    mbar_expect_tx(fb, STAGE_BYTES);
+                    const uint32_t a_dst = smem_u32(ring + stage * STAGE_BYTES);
+                    tma_load_2d(a_dst, &tma_a, kb * BK, m0, fb);
+                    tma_load_2d(a_dst + A_STAGE, &tma_b, kb * BK, n0, fb);
+                    pending[stage] = true;
+                    issued_phase[stage] = phase;
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok) {
+                // drain: every issued load lands before the CTA leaves (bounded)
+                for (int s = 0; s < STAGES; ++s) {
+                    if (!pending[s]) continue;
+                    const uint64_t t0 = global_ns();
+                    while (!mbar_try(full0 + 8 * s, issued_phase[s]) && global_ns() - t0 < kWaitLimitNs) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 5) {
+        // ------------------------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, abort_flag, 2)) { ok = false; break; }
+                fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < kb_count; ++kb) {
+                    if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, 2)) { ok = false; break; }
+                    fence_after();
+                    const uint32_t a_addr = smem_u32(ring + stage * STAGE_BYTES);
+                    const uint32_t b_addr = a_addr + A_STAGE;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 32; ++kk)
+                        mma_i8(d_tmem, smem_desc(a_addr + 32 * kk), smem_desc(b_addr + 32 * kk),
+                               (kb | kk) != 0 ? 1u : 0u);
+                    mma_commit(empty0 + 8 * stage);  // the stage is free once these MMAs have read it
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                mma_commit(tfull0 + 8 * acc);  // the accumulator is complete
+                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+            // every MMA issued by this thread has finished before the tensor memory is released
+            mma_commit(drain);
+            const uint64_t t0 = global_ns();
+            while (!mbar_try(drain, 0) && global_ns() - t0 < kWaitLimitNs) {
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------------------------ epilogue (warps 0-3)
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+            const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+            if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, 3)) break;
+            fence_after();
+            const int row = m0 + warp * 32 + lane;
+            const bool row_ok = row < M;
+            const float xsr = row_ok ? __ldg(xs + row) : 0.f;
+            const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) +
+                                       static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(lane_addr + static_cast<uint32_t>(c * 32), r);
+                const int col0 = n0 + c * 32;
+                if (!row_ok || col0 >= N) continue;
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {  // 8 columns = one 16-byte store
+                    const int col = col0 + 8 * g;
+                    if (col >= N) break;
+                    const float4 w0 = __ldg(reinterpret_cast<const float4 *>(ws + col));
+                    const float4 w1 = __ldg(reinterpret_cast<const float4 *>(ws + col) + 1);
+                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                    uint32_t packed[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float a0 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[8 * g + 2 * j])), xsr),
+                                                   wv[2 * j]);
+                        const float a1 = __fmul_rn(
+                            __fmul_rn(__int2float_rn(static_cast<int>(r[8 * g + 2 * j + 1])), xsr), wv[2 * j + 1]);
+                        __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
+                        packed[j] = *reinterpret_cast<uint32_t *>(&h);
+                    }
+                    const size_t off = static_cast<size_t>(row) * N + col;
+                    *reinterpret_cast<uint4 *>(y + off) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                    if (acc_out != nullptr) {
+                        int4 *dst = reinterpret_cast<int4 *>(acc_out + off);
+                        dst[0] = make_int4(r[8 * g], r[8 * g + 1], r[8 * g + 2], r[8 * g + 3]);
+                        dst[1] = make_int4(r[8 * g + 4], r[8 * g + 5], r[8 * g + 6], r[8 * g + 7]);
+                    }
+                }
+            }
+            fence_before();
+            mbar_arrive(tempty0 + 8 * acc);  // this accumulator may be overwritten
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (warp == 5) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------------------------- host
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// a [rows, K] int8 K-major matrix as a TMA map with boxes of box_rows x 128 bytes, 128-byte swizzle, zero fill
+int make_map(CUtensorMap *map, const void *base, int rows, int K, int box_rows) {
+    EncodeTiled enc = encoder();
+    if (enc == nullptr) return WF_ERR_DEVICE;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? WF_OK : WF_ERR_ARG;
+}
+
+}  // namespace
+
+int w8a8_gemm_launch(const int8_t *xq, const int8_t *wq, const float *xs, const float *ws, __nv_bfloat16 *y,
+                     int32_t *acc_out, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0) return (M == 0 || N == 0) ? WF_OK : WF_ERR_ARG;
+    if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return WF_ERR_ARG;
+    if (K % 16 != 0 || N % 8 != 0) return WF_ERR_ARG;  // TMA row pitch and 16-byte output stores
+    auto al = [](const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
+    if (!xq || !wq || !xs || !ws || !y || !al(xq, 16) || !al(wq, 16) || !al(ws, 16) || !al(xs, 4) || !al(y, 16) ||
+        (acc_out && !al(acc_out, 16)))
+        return WF_ERR_ARG;
+    int rc = check_device();
+    if (rc != WF_OK) return rc;
+    CUtensorMap ma, mb;
+    if ((rc = make_map(&ma, xq, static_cast<int>(M), static_cast<int>(K), BM)) != WF_OK) return rc;
+    if ((rc = make_map(&mb, wq, static_cast<int>(N), static_cast<int>(K), BN)) != WF_OK) return rc;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             SMEM_BYTES);
+        if (e != cudaSuccess) return static_cast<int>(e);
+        attr_set[dev] = true;
+    }
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, device_sm_count()));
+    w8a8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, xs, ws, y, acc_out, static_cast<int>(M),
+                                                            static_cast<int>(N), static_cast<int>(K));
+    return static_cast<int>(cudaGetLastError());
+}
+
+int w8a8_gemm_status(int *status) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(int));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    if (v != 0) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(int));
+    }
+    *status = v;
+    return WF_OK;
+}
+
+}  // namespace wf
+
+extern "C" WF_API int wf_w8a8_gemm(const int8_t *xq, const int8_t *wq, const float *xs, const float *ws, void *y,
+                                  int32_t *acc_dbg, int64_t m, int64_t n, int64_t k, wf_stream_t stream) {
+    return wf::w8a8_gemm_launch(xq, wq, xs, ws, static_cast<__nv_bfloat16 *>(y), acc_dbg, m, n, k,
+                                reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" WF_API int wf_w8a8_gemm_status(int *status) {
+    if (status == nullptr) return WF_ERR_ARG;
+    return wf::w8a8_gemm_status(status);
+}

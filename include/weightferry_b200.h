@@ -119,6 +119,22 @@ WF_API int wf_quant_rows(const void *x, const void *s1, const void *shift, const
                          float *scale, int64_t rows, int64_t K, int64_t rows_per_group, float eps, int pre, int rotate,
                          wf_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------- W8A8 linear */
+
+/* y[m, n] = bf16_rn((float(acc[m, n]) * xs[m]) * ws[n]), acc = sum_k xq[m, k] * wq[n, k] in int32:
+ * xq [m, k] and wq [n, k] int8 row-major (k % 16 == 0, 16-byte aligned), xs [m] and ws [n] float32 (ws 16-byte
+ * aligned), y [m, n] bf16 (n % 8 == 0, 16-byte aligned); acc_dbg (optional, may be NULL) receives the raw int32
+ * accumulators [m, n]. tcgen05 kind::i8 tensor-core GEMM with TMA-fed shared-memory stages and TMEM accumulators.
+ * Replaces comfy_kitchen's cutlass_int8_dequant as the reference calls it (enhancers/fused_int8.py:200-203; the
+ * per-channel ws expanded as at :185-186). */
+WF_API int wf_w8a8_gemm(const int8_t *xq, const int8_t *wq, const float *xs, const float *ws, void *y,
+                        int32_t *acc_dbg, int64_t m, int64_t n, int64_t k, wf_stream_t stream);
+
+/* Status word of the GEMM kernel: 0, or the code of a pipeline wait that ran out of time (the kernel then stopped
+ * early and its output is incomplete). Reading it synchronises the device and clears it. No reference counterpart
+ * (the reference's GEMM is a closed library call); it is this library's failure report. */
+WF_API int wf_w8a8_gemm_status(int *status);
+
 #ifdef __cplusplus
 }
 #endif

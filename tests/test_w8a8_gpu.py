@@ -1,0 +1,102 @@
+"""W8A8 linear on the GPU: the tcgen05 int8 GEMM's int32 accumulators bit for bit against an exact (float64) matrix
+product of the same int8 operands, its bf16 outputs within 1 bf16 ulp of the float64 restatement
+bf16(acc * x_s[m] * w_s[n]), for one tile, ragged edges, many tiles and the BASELINE shape; the kernel's status word
+must read 0 (no pipeline wait ran out of time)."""
+
+import numpy as np
+import pytest
+
+from conftest import wf
+
+pytestmark = pytest.mark.gpu
+
+
+def _gemm(xq, wq, xs, ws, with_acc=True):
+    import torch
+    ext = wf("_ext")
+    m, k = xq.shape
+    n = wq.shape[0]
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=xq.device)
+    acc = torch.empty((m, n), dtype=torch.int32, device=xq.device) if with_acc else None
+    rc = ext.lib().wf_w8a8_gemm(xq.data_ptr(), wq.data_ptr(), xs.data_ptr(), ws.data_ptr(), y.data_ptr(),
+                                acc.data_ptr() if acc is not None else None, m, n, k, ext.stream_of(xq.device))
+    ext.check(rc, "wf_w8a8_gemm")
+    torch.cuda.synchronize()
+    st = __import__("ctypes").c_int(-1)
+    ext.check(ext.lib().wf_w8a8_gemm_status(__import__("ctypes").byref(st)), "status")
+    assert st.value == 0, f"GEMM pipeline wait expired (code {st.value})"
+    return y, acc
+
+
+def _ord16(t):
+    import torch
+    b = t.contiguous().view(torch.int16).to(torch.int32)
+    return torch.where(b < 0, -(b & 0x7FFF), b)
+
+
+def _check(xq, wq, xs, ws, y, acc):
+    import torch
+    exact = xq.double() @ wq.double().t()
+    if acc is not None:
+        assert torch.equal(acc.double(), exact), "int32 accumulators differ"
+    ref = (exact * xs.double().view(-1, 1) * ws.double().view(1, -1)).to(torch.bfloat16)
+    d = (_ord16(y) - _ord16(ref)).abs()
+    assert int(d.max()) <= 1, f"bf16 outputs differ by {int(d.max())} ulp"
+
+
+def _operands(m, n, k, seed):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    xq = torch.randint(-128, 128, (m, k), dtype=torch.int16, device="cuda", generator=g).to(torch.int8)
+    wq = torch.randint(-127, 128, (n, k), dtype=torch.int16, device="cuda", generator=g).to(torch.int8)
+    xs = torch.rand((m,), device="cuda", generator=g) * 0.02 + 1e-4
+    ws = torch.rand((n,), device="cuda", generator=g) * 0.001 + 1e-5
+    return xq, wq, xs, ws
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 128), (128, 256, 2048), (300, 520, 272), (1, 8, 16),
+                                   (1024, 2048, 2048), (2048, 512, 4096)])
+def test_gemm_exact_accumulators(cuda, m, n, k):
+    xq, wq, xs, ws = _operands(m, n, k, seed=m * 7 + n * 3 + k)
+    y, acc = _gemm(xq, wq, xs, ws)
+    _check(xq, wq, xs, ws, y, acc)
+
+
+def test_gemm_extreme_values(cuda):
+    """All operands at -128 / 127: accumulators at their largest magnitude (k * 128 * 128 fits int32)."""
+    import torch
+    m, n, k = 256, 256, 4096
+    xq = torch.full((m, k), -128, dtype=torch.int8, device="cuda")
+    wq = torch.full((n, k), 127, dtype=torch.int8, device="cuda")
+    wq[::2] = -128
+    xs = torch.ones(m, device="cuda")
+    ws = torch.full((n,), 1e-6, device="cuda")
+    y, acc = _gemm(xq, wq, xs, ws)
+    _check(xq, wq, xs, ws, y, acc)
+
+
+def test_gemm_baseline_shape(cuda):
+    """X [8192, 2048] per-token quantised, W [8192, 2048] per-channel -> Y [8192, 8192]."""
+    import torch
+    fk = wf("enhancers.fused_kernels")
+    g = torch.Generator(device="cuda").manual_seed(20261201 + 2)
+    x = torch.randn((8192, 2048), device="cuda", generator=g).to(torch.bfloat16)
+    w_fp = torch.randn((8192, 2048), device="cuda", generator=g) * 0.02
+    ws = (w_fp.abs().amax(dim=1) / 127.0).float().contiguous()
+    wq = torch.clamp(torch.round(w_fp / ws.view(-1, 1)), -127, 127).to(torch.int8).contiguous()
+    xq, xs = fk.quantize_rows(x, rotate=False)
+    y, acc = _gemm(xq, wq, xs.view(-1), ws)
+    _check(xq, wq, xs.view(-1), ws, y, acc)
+    y2, _ = _gemm(xq, wq, xs.view(-1), ws, with_acc=False)
+    assert torch.equal(y, y2)
+
+
+def test_gemm_rejections(cuda):
+    import torch
+    ext = wf("_ext")
+    t = torch.zeros(4096, dtype=torch.int8, device="cuda")
+    p = t.data_ptr()
+    st = ext.stream_of(t.device)
+    assert ext.lib().wf_w8a8_gemm(p, p, p, p, p, None, 16, 16, 24, st) == -1   # k % 16
+    assert ext.lib().wf_w8a8_gemm(p, p, p, p, p, None, 16, 12, 32, st) == -1   # n % 8
+    assert ext.lib().wf_w8a8_gemm(p + 1, p, p, p, p, None, 16, 16, 32, st) == -1  # alignment
