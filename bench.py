@@ -326,6 +326,155 @@ def e2e_block(torch, gd, dev, args):
             "ms_per_step": round(ms, 3), "sample": "one Cosmos-14B block (16 Q4_K tensors) per step"}
 
 
+def w8a8_operands(torch, dev, seed):
+    """X bf16 [2 x 4096, 2048] ~ N(0, 1); W_fp ~ N(0, 0.02) [8192, 2048] -> int8 per output
+    channel (symmetric, scale = amax / 127), as the int8 layout the reference consumes."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    x = torch.randn((8192, 2048), device=dev, generator=g).to(torch.bfloat16)
+    w_fp = torch.randn((8192, 2048), device=dev, generator=g) * 0.02
+    ws = (w_fp.abs().amax(dim=1) / 127.0).float().contiguous()
+    wq = torch.clamp(torch.round(w_fp / ws.view(-1, 1)), -127, 127).to(torch.int8).contiguous()
+    return x, wq, ws
+
+
+def run_w8a8(torch, args, world, rank, dist):
+    """per-token quantisation (plain absmax) + tcgen05 int8 GEMM + rescale epilogue, one step = the whole
+    linear; L2 flushed before every step (X and W together fit in L2)."""
+    fk = _pkg("enhancers.fused_kernels")
+    fi = _pkg("enhancers.fused_int8")
+    ext = _pkg("_ext")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    x, wq, ws = w8a8_operands(torch, dev, 20261201 + 2 + rank)
+    M, K = x.shape
+    N = wq.shape[0]
+    xq = torch.empty((M, K), dtype=torch.int8, device=dev)
+    xs = torch.empty((M, 1), dtype=torch.float32, device=dev)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    lib = ext.lib()
+    stream = torch.cuda.current_stream(dev)
+    kq = fk._get_kernels()["quant_row"][(M,)]
+
+    def quant():
+        kq(x, None, None, xq, xs, 1, 0.0, K=K, PRE=fk.PRE_NONE, ROTATE=False)
+
+    def gemm():
+        rc = lib.wf_w8a8_gemm(xq.data_ptr(), wq.data_ptr(), xs.data_ptr(), ws.data_ptr(), y.data_ptr(), None, M, N,
+                              K, stream.cuda_stream)
+        if rc:
+            ext.check(rc, "wf_w8a8_gemm")
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        quant()
+        gemm()
+    barrier(torch, dist)
+    evq = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    evg = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        barrier(torch, dist)
+        for s in range(args.steps):
+            flush.zero_()
+            evq[s][0].record(stream)
+            quant()
+            evq[s][1].record(stream)
+            gemm()
+            evg[s][1].record(stream)
+        barrier(torch, dist)
+    q_ms = statistics.mean(a.elapsed_time(b) for a, b in evq)
+    g_ms = statistics.mean(evq[s][1].elapsed_time(evg[s][1]) for s in range(args.steps))
+    step_ms = max_over_ranks(torch, dist, q_ms + g_ms)
+    ops = 2.0 * M * N * K
+    value = sum_over_ranks(torch, dist, ops / (step_ms / 1e3) / 1e12)
+    st = __import__("ctypes").c_int(0)
+    lib.wf_w8a8_gemm_status(__import__("ctypes").byref(st))
+    # cuBLASLt int8 through torch._int_mm on the same operands, for context (a library GEMM without the epilogue)
+    lib_ms = None
+    try:
+        for _ in range(3):
+            torch._int_mm(xq, wq.t())
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        tot = 0.0
+        for _ in range(5):
+            flush.zero_()
+            e0.record(stream)
+            torch._int_mm(xq, wq.t())
+            e1.record(stream)
+            torch.cuda.synchronize()
+            tot += e0.elapsed_time(e1)
+        lib_ms = tot / 5
+    except Exception:  # noqa: BLE001 -- context only
+        lib_ms = None
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_w8a8(torch, fi, x, wq, ws, dev, args)
+        e2e["value"] = round(sum_over_ranks(torch, dist, e2e["value"]), 2)
+    return {
+        "value": value, "ms_per_step": step_ms, "kern_ms": g_ms, "alg_ops_per_launch": ops, "clk": clk.summary(),
+        "e2e": e2e, "gpu_launches": int(sum_over_ranks(torch, dist, 2 * args.steps)), "gemm_status": st.value,
+        "config": {"workload": "W8A8 linear, X bf16 [8192, 2048] x W int8 [8192, 2048]^T -> Y bf16 [8192, 8192] "
+                               "(configs[2], Cosmos-Predict2-2B MLP up-projection)",
+                   "quantiser": "per-token absmax int8 (plain, no rotation)", "quant_ms": round(q_ms, 4),
+                   "gemm_ms": round(g_ms, 4),
+                   "cublaslt_int_mm_ms": None if lib_ms is None else round(lib_ms, 4),
+                   "l2": "flushed (512 MB write) before every step"},
+    }
+
+
+def e2e_w8a8(torch, fi, x, wq, ws, dev, args):
+    """fused_int8.int8_linear (the package's entry point) with pinned host buffers: per step H2D of X, the linear,
+    D2H of Y."""
+    hx = x.cpu().pin_memory()
+    hy = torch.empty((x.shape[0], wq.shape[0]), dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty_like(x)
+
+    def step():
+        dx.copy_(hx, non_blocking=True)
+        y = fi.int8_linear(dx, wq, ws)
+        hy.copy_(y, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(3, args.steps // 2)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    ops = 2.0 * x.shape[0] * wq.shape[0] * x.shape[1]
+    return {"value": ops / (ms / 1e3) / 1e12, "unit": "TOPS", "h2d_bytes_per_step": x.numel() * 2,
+            "d2h_bytes_per_step": hy.numel() * 2, "ms_per_step": round(ms, 3)}
+
+
+def cpu_baseline_w8a8(seconds=10.0):
+    """The reference's arithmetic on the host: per-token quantisation (oracle) + an exact int8 GEMM (torch CPU,
+    int8 operands widened to float64) + the rescale, on the first 64-row slices of configs[2] until ~seconds."""
+    import torch
+    from oracle import oracle
+    g = torch.Generator().manual_seed(20261201 + 2)
+    rows = 64
+    x = torch.randn((rows, 2048), generator=g).to(torch.bfloat16)
+    w_fp = torch.randn((8192, 2048), generator=g) * 0.02
+    ws = (w_fp.abs().amax(dim=1) / 127.0).double()
+    wq = torch.clamp(torch.round(w_fp / ws.float().view(-1, 1)), -127, 127).double()
+    xb = x.view(torch.int16).numpy().view(np.uint16)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        q, sc = oracle.quant_rows(xb, pre=0, rotate=False)
+        acc = torch.from_numpy(q.astype(np.float64)) @ wq.t()
+        _y = (acc * torch.from_numpy(sc.astype(np.float64)).view(-1, 1) * ws.view(1, -1)).to(torch.bfloat16)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    ops = 2.0 * rows * 8192 * 2048 * reps
+    return ops / el / 1e12, torch.get_num_threads(), f"{reps} x 64 rows of configs[2] in {el:.1f} s"
+
+
 def run_single_weight(torch, args, world, rank, dist, which):
     """configs[0] (Q8_0 5120x5120) or configs[1]'s weight (Q4_K 5120x13824): one launch per step, L2 flushed."""
     gd = _pkg("enhancers.gguf_dequant")
@@ -383,7 +532,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="sweep", choices=["sweep", "q8", "q4k"])
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "q8", "q4k", "w8a8"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -399,6 +548,8 @@ def main():
     world, rank, local, dist = setup_dist(torch)
     if args.workload == "sweep":
         r = run_sweep(torch, args, world, rank, dist)
+    elif args.workload == "w8a8":
+        return finish_w8a8(torch, args, world, rank, dist, run_w8a8(torch, args, world, rank, dist))
     else:
         r = run_single_weight(torch, args, world, rank, dist, args.workload)
     peak, peak_kind = measured_peaks()
@@ -424,6 +575,43 @@ def main():
             "cpu_baseline": cpu, "e2e": r["e2e"], "gpu_launches": r["gpu_launches"], "clocks": r["clk"],
         }
         print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def measured_int8_peak():
+    """Dense int8 tensor peak: twice the measured dense bf16 GEMM rate (B200's int8 dense rate is twice bf16's)."""
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return 2.0 * float(p["bf16_tflops"]), "2 x MEASURED_PEAKS.json bf16_tflops (measured, burst)"
+    except (OSError, KeyError, ValueError):
+        return 2.0 * 1590.0, "2 x fallback bf16 1590 TFLOP/s"
+
+
+def finish_w8a8(torch, args, world, rank, dist, r):
+    peak, src = measured_int8_peak()
+    achieved = r["alg_ops_per_launch"] / (r["kern_ms"] / 1e3) / 1e12
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        v, threads, sample = cpu_baseline_w8a8(args.cpu_seconds)
+        cpu = {"value": round(v, 4), "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample}
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "W8A8 linear int8 TOPS (quantise + GEMM + rescale)", "value": round(r["value"], 2),
+            "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(r["ms_per_step"], 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 x int8 -> int32, bf16 out", "data": "synthetic (seeded)",
+            "config": r["config"],
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
+                         "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC.get("w8a8"), "peak_source": src,
+                         "kernel": "w8a8_gemm_kernel"},
+            "cpu_baseline": cpu, "e2e": r["e2e"], "gpu_launches": r["gpu_launches"], "clocks": r["clk"],
+            "gemm_status": r["gemm_status"]}), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

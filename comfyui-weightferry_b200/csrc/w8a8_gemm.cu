@@ -3,16 +3,17 @@
 // which calls comfy_kitchen's compiled CUTLASS kernel; the arithmetic here is this library's own, with the epilogue
 // order written below).
 //
-// Blackwell-native structure, one persistent CTA per SM (192 threads):
-//   warp 4      TMA producer: 128x128 tiles of xq and 256x128 tiles of wq (K-major, 128-byte swizzle) into a
+// Blackwell-native structure, one persistent CTA per SM (320 threads):
+//   warp 8      TMA producer: 128x128 tiles of xq and 256x128 tiles of wq (K-major, 128-byte swizzle) into a
 //               4-stage shared-memory ring, completion counted on an mbarrier per stage;
-//   warp 5      MMA issuer: one thread issues tcgen05.mma.cta_group::1.kind::i8 (M=128, N=256, K=32; 4 per stage)
+//   warp 9      MMA issuer: one thread issues tcgen05.mma.cta_group::1.kind::i8 (M=128, N=256, K=32; 4 per stage)
 //               with int32 accumulation in tensor memory; tcgen05.commit releases each stage and, per tile, hands
 //               the accumulator to the epilogue. Two 256-column accumulators (all 512 TMEM columns) let tile i+1's
 //               MMAs run while tile i is written out;
-//   warps 0..3  epilogue: warp w reads TMEM lanes 32w..32w+31 (one output row per thread) with tcgen05.ld,
-//               y = bf16_rn((float(acc) * x_s[m]) * w_s[n]) (two float32 products, rounded to nearest each),
-//               optional raw int32 copy of the accumulators, 16-byte stores.
+//   warps 0..7  epilogue: warp w reads TMEM lanes 32(w%4)..+31 (one output row per thread), columns
+//               128(w/4)..+127, with tcgen05.ld (the next 32 columns in flight while the current ones are
+//               converted), y = bf16_rn((float(acc) * x_s[m]) * w_s[n]) (two float32 products, each rounded to
+//               nearest), w_s of the tile staged in shared memory, optional raw int32 copy, 16-byte stores.
 // Every mbarrier wait is bounded in time (about 2 s): on expiry the CTA records an error code (read with
 // wf_w8a8_gemm_status), stops issuing work, waits (bounded) for its own copies and MMAs in flight, frees its tensor
 // memory and returns. No load in this file uses cluster multicast; operands are always this GPU's own memory.
@@ -30,9 +31,10 @@ constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
 constexpr int A_STAGE = BM * BK;  // 16 KB
 constexpr int B_STAGE = BN * BK;  // 32 KB
 constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;
+constexpr int EPI_THREADS = 256;
 constexpr int TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;  // ring + alignment slack + barriers
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + 2 * BN * 4;  // ring, slack, barriers, w_s
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 // instruction descriptor of kind::i8: D int32 (bits 4-5 = 2), A and B signed int8 (bits 7-9, 10-12 = 1), both
@@ -124,6 +126,8 @@ __device__ __forceinline__ void mma_commit(uint32_t mbar) {
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// tcgen05.ld of 32 consecutive columns of this thread's lane; the registers are valid only after tmem_wait32 on
+// the same array (the wait names them as operands, so no use can be scheduled before it)
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -133,8 +137,48 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        : "r"(taddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait32(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+
+// 32 accumulators of one row -> bf16 (and the optional int32 copy); col0 is the first column, cols >= N skipped
+__device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], const float *ws_s, int cbase, float xsr,
+                                            __nv_bfloat16 *y, int32_t *acc_out, int row, int col0, int N) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const int col = col0 + 8 * g;
+        if (col >= N) break;
+        const float4 w0 = *reinterpret_cast<const float4 *>(ws_s + cbase + 8 * g);
+        const float4 w1 = *reinterpret_cast<const float4 *>(ws_s + cbase + 8 * g + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        uint32_t packed[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float a0 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[8 * g + 2 * j])), xsr), wv[2 * j]);
+            const float a1 =
+                __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[8 * g + 2 * j + 1])), xsr), wv[2 * j + 1]);
+            __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
+            packed[j] = *reinterpret_cast<uint32_t *>(&h);
+        }
+        const size_t off = static_cast<size_t>(row) * N + col;
+        *reinterpret_cast<uint4 *>(y + off) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        if (acc_out != nullptr) {
+            int4 *dst = reinterpret_cast<int4 *>(acc_out + off);
+            dst[0] = make_int4(r[8 * g], r[8 * g + 1], r[8 * g + 2], r[8 * g + 3]);
+            dst[1] = make_int4(r[8 * g + 4], r[8 * g + 5], r[8 * g + 6], r[8 * g + 7]);
+        }
+    }
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -145,11 +189,13 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     // 1024-byte aligned ring (the 128-byte swizzle pattern repeats every 8 rows of 128 bytes)
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(ring + STAGES * STAGE_BYTES);
-    // bars: full[0..3], empty[0..3], tmem_full[0..1], tmem_empty[0..1], drain
+    float *ws_smem = reinterpret_cast<float *>(ring + STAGES * STAGE_BYTES + 256);  // 2 x BN w_s of a tile
+    // bars: full[0..3], empty[0..3], tmem_full[0..1], tmem_empty[0..1], drain, ws_ready[0..1]
     __shared__ uint32_t s_tmem_base;
     __shared__ int s_abort;
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), tfull0 = smem_u32(bars + 2 * STAGES),
-                   tempty0 = smem_u32(bars + 2 * STAGES + 2), drain = smem_u32(bars + 2 * STAGES + 4);
+                   tempty0 = smem_u32(bars + 2 * STAGES + 2), drain = smem_u32(bars + 2 * STAGES + 4),
+                   wsrdy0 = smem_u32(bars + 2 * STAGES + 5);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
@@ -164,13 +210,14 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull0 + 8 * b, 1);
-            mbar_init(tempty0 + 8 * b, 4 * 32);
+            mbar_init(tempty0 + 8 * b, EPI_THREADS);
+            mbar_init(wsrdy0 + 8 * b, EPI_THREADS);
         }
         mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    if (warp == 5) {  // the MMA warp owns the tensor memory
+    if (warp == 9) {  // the MMA warp owns the tensor memory
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_u32(&s_tmem_base)), "r"(TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -181,7 +228,7 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     const uint32_t tmem_base = s_tmem_base;
     volatile int *abort_flag = &s_abort;
 
-    if (warp == 4) {
+    if (warp == 8) {
         // ------------------------------------------------------------------------------------ TMA producer
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_a)) : "memory");
@@ -216,7 +263,7 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
                 }
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         // ------------------------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             int stage = 0;
@@ -252,50 +299,41 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         }
         __syncwarp();
     } else {
-        // ------------------------------------------------------------------------------------ epilogue (warps 0-3)
+        // ------------------------------------------------------------------------------------ epilogue (warps 0-7)
+        const int quarter = warp & 3, half = warp >> 2;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
             const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+            // this tile's w_s into shared memory, buffer `acc`: every epilogue thread has finished the tile that last
+            // used it (they arrived on the other buffer's barrier after it, and this thread waited there)
+            float *ws_s = ws_smem + acc * BN;
+            {
+                const int c = static_cast<int>(threadIdx.x);  // 0 .. 255
+                ws_s[c] = (n0 + c < N) ? __ldg(ws + n0 + c) : 0.f;
+            }
+            mbar_arrive(wsrdy0 + 8 * acc);
             if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, 3)) break;
             fence_after();
-            const int row = m0 + warp * 32 + lane;
+            if (!mbar_wait(wsrdy0 + 8 * acc, acc_phase, abort_flag, 3)) break;
+            const int row = m0 + quarter * 32 + lane;
             const bool row_ok = row < M;
             const float xsr = row_ok ? __ldg(xs + row) : 0.f;
-            const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) +
-                                       static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(lane_addr + static_cast<uint32_t>(c * 32), r);
-                const int col0 = n0 + c * 32;
-                if (!row_ok || col0 >= N) continue;
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {  // 8 columns = one 16-byte store
-                    const int col = col0 + 8 * g;
-                    if (col >= N) break;
-                    const float4 w0 = __ldg(reinterpret_cast<const float4 *>(ws + col));
-                    const float4 w1 = __ldg(reinterpret_cast<const float4 *>(ws + col) + 1);
-                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-                    uint32_t packed[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float a0 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[8 * g + 2 * j])), xsr),
-                                                   wv[2 * j]);
-                        const float a1 = __fmul_rn(
-                            __fmul_rn(__int2float_rn(static_cast<int>(r[8 * g + 2 * j + 1])), xsr), wv[2 * j + 1]);
-                        __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
-                        packed[j] = *reinterpret_cast<uint32_t *>(&h);
-                    }
-                    const size_t off = static_cast<size_t>(row) * N + col;
-                    *reinterpret_cast<uint4 *>(y + off) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                    if (acc_out != nullptr) {
-                        int4 *dst = reinterpret_cast<int4 *>(acc_out + off);
-                        dst[0] = make_int4(r[8 * g], r[8 * g + 1], r[8 * g + 2], r[8 * g + 3]);
-                        dst[1] = make_int4(r[8 * g + 4], r[8 * g + 5], r[8 * g + 6], r[8 * g + 7]);
-                    }
-                }
-            }
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN + half * 128);
+            uint32_t ra[32], rb[32];
+            tmem_ld32(taddr, ra);
+            tmem_wait32(ra);
+            tmem_ld32(taddr + 32, rb);
+            if (row_ok) store_chunk(ra, ws_s, half * 128, xsr, y, acc_out, row, n0 + half * 128, N);
+            tmem_wait32(rb);
+            tmem_ld32(taddr + 64, ra);
+            if (row_ok) store_chunk(rb, ws_s, half * 128 + 32, xsr, y, acc_out, row, n0 + half * 128 + 32, N);
+            tmem_wait32(ra);
+            tmem_ld32(taddr + 96, rb);
+            if (row_ok) store_chunk(ra, ws_s, half * 128 + 64, xsr, y, acc_out, row, n0 + half * 128 + 64, N);
+            tmem_wait32(rb);
+            if (row_ok) store_chunk(rb, ws_s, half * 128 + 96, xsr, y, acc_out, row, n0 + half * 128 + 96, N);
             fence_before();
             mbar_arrive(tempty0 + 8 * acc);  // this accumulator may be overwritten
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
@@ -304,7 +342,7 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     fence_before();
     __syncthreads();
     fence_after();
-    if (warp == 5) {
+    if (warp == 9) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                      : "memory");
     }

@@ -100,3 +100,37 @@ def test_gemm_rejections(cuda):
     assert ext.lib().wf_w8a8_gemm(p, p, p, p, p, None, 16, 16, 24, st) == -1   # k % 16
     assert ext.lib().wf_w8a8_gemm(p, p, p, p, p, None, 16, 12, 32, st) == -1   # n % 8
     assert ext.lib().wf_w8a8_gemm(p + 1, p, p, p, p, None, 16, 16, 32, st) == -1  # alignment
+
+
+def test_int8_linear_entry_points(cuda):
+    """int8_linear (plain) equals quantise + GEMM; the reference-named _int8_linear_shared shares one quantisation
+    between q / k / v under _Overrides' cache and handles a pending modulate inside the quantiser."""
+    import torch
+    fi = wf("enhancers.fused_int8")
+    fk = wf("enhancers.fused_kernels")
+    fs = wf("enhancers.fused_state")
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn((2, 300, 1024), device="cuda", generator=g).to(torch.bfloat16)
+    wq = torch.randint(-127, 128, (768, 1024), dtype=torch.int16, device="cuda", generator=g).to(torch.int8)
+    ws = torch.rand(768, device="cuda", generator=g) * 1e-3
+    y = fi.int8_linear(x, wq, ws)
+    xq, xs = fk.quantize_rows(x.reshape(-1, 1024), rotate=False)
+    y2 = fi.gemm(xq, wq, xs, ws)
+    assert torch.equal(y.reshape(-1, 768), y2)
+    fs._tls.qkv = {}
+    try:
+        a = fi._int8_linear_shared(x, (wq, ws), None)
+        b = fi._int8_linear_shared(x, (wq, ws), None)
+        assert torch.equal(a, y) and torch.equal(b, y)
+        # pending modulate: the quantiser applies bf16(bf16(x * (1 + scale)) + shift) itself
+        scale = (torch.randn((2, 1, 1024), device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+        shift = (torch.randn((2, 1, 1024), device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+        fi._set_pre(x, "mod", scale, shift)
+        c = fi._int8_linear_shared(x, (wq, ws), None)
+        fi._clear_pre()
+        real = x * (1 + scale) + shift
+        d = fi.int8_linear(real, wq, ws)
+        assert torch.equal(c, d)
+    finally:
+        fs._tls.qkv = None
+        fi._clear_pre()
