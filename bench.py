@@ -475,6 +475,167 @@ def cpu_baseline_w8a8(seconds=10.0):
     return ops / el / 1e12, torch.get_num_threads(), f"{reps} x 64 rows of configs[2] in {el:.1f} s"
 
 
+def h2d_probe(torch, dev, nbytes=1 << 30, reps=5):
+    """Pinned -> device cudaMemcpyAsync of 1 GiB, best of `reps` (the measured PCIe H2D bandwidth)."""
+    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    dst.copy_(host, non_blocking=True)
+    torch.cuda.synchronize()
+    best = 0.0
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dst.copy_(host, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        best = max(best, nbytes / (e0.elapsed_time(e1) / 1e3) / 1e9)
+    del host, dst
+    return best
+
+
+def run_stack(torch, args, world, rank, dist):
+    """a Cosmos-Predict2-14B-shaped stack of 36 blocks, Q8_0 weights in pinned host RAM streamed through
+    3 GPU slots and dequantised on arrival, batch 2 x 4096 tokens (+ 512 context tokens), tensor-parallel over the
+    ranks (column / row split, NCCL all-gather / reduce-scatter of the token rows). One step = one forward."""
+    cb = _pkg("streaming.cosmos_block")
+    stk = _pkg("streaming.stack")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = cb.COSMOS_14B
+    tp = cb.TP()
+    batch, T, H, W, S = 2, 1, 64, 64, 512
+    tokens = T * H * W
+    probe = h2d_probe(torch, dev)
+    t_build = time.perf_counter()
+    stack = stk.StreamedStack(cfg, args.blocks, dev, tp, seed=20261201 + 4, num_slots=args.slots)
+    build_s = time.perf_counter() - t_build
+    g = torch.Generator(device=dev)
+    g.manual_seed(20261201 + 4)
+    rows = batch * tokens // tp.world
+    x_full = torch.randn((batch * tokens, cfg.hidden), device=dev, generator=g).to(torch.bfloat16)
+    x = x_full[tp.rank * rows:(tp.rank + 1) * rows].contiguous()
+    del x_full
+    emb = (torch.randn((batch, cfg.hidden), device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    lora = (torch.randn((batch, 3 * cfg.hidden), device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    ctx = torch.randn((batch, S, cfg.ctx_dim), device=dev, generator=g).to(torch.bfloat16)
+    rope = cb.rope3d_table(T, H, W, device=dev)
+
+    def step():
+        return stack.forward(x, emb, ctx, rope, batch, tokens, lora)
+
+    for _ in range(args.warmup):
+        out = step()
+    barrier(torch, dist)
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        barrier(torch, dist)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            out = step()
+        e1.record(stream)
+        barrier(torch, dist)
+    ms = max_over_ranks(torch, dist, e0.elapsed_time(e1) / args.steps)
+    finite = bool(torch.isfinite(out.float()).all().item())
+    h2d_rank = args.blocks * stack.bytes_per_block
+    h2d_rate = h2d_rank / (ms / 1e3) / 1e9
+    # one more forward with the event timeline on (not timed)
+    from importlib import import_module
+    prof_mod = import_module("comfyui-weightferry_b200.streaming.profiler")
+    stack.state.profiler = prof_mod._StreamProfiler(stack.state.num_stream, stack.bytes_per_block)
+    step()
+    summ = stack.state.profile_summary()["per_forward"][-1]
+    stack.state.profiler = None
+    flops = cb.flops_per_block(cfg, batch, tokens, S) * args.blocks
+    e2e = None
+    if not args.no_e2e:
+        hx = x.cpu().pin_memory()
+        hy = torch.empty_like(hx).pin_memory()
+        dx = torch.empty_like(x)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(max(1, args.steps // 2)):
+            dx.copy_(hx, non_blocking=True)
+            y = stack.forward(dx, emb, ctx, rope, batch, tokens, lora)
+            hy.copy_(y, non_blocking=True)
+        t1.record()
+        torch.cuda.synchronize()
+        e_ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / max(1, args.steps // 2))
+        e2e = {"value": round(e_ms / 1e3, 4), "unit": "s/step", "h2d_bytes_per_step": hx.numel() * 2 + h2d_rank,
+               "d2h_bytes_per_step": hy.numel() * 2,
+               "note": "activation rows H2D + D2H per step around the streamed forward; weights stream H2D inside"}
+    stack.close()
+    return {"ms": ms, "clk": clk.summary(), "e2e": e2e, "finite": finite, "probe": probe, "h2d_rate": h2d_rate,
+            "h2d_rank": h2d_rank, "flops": flops, "summary": summ, "build_s": build_s,
+            "slots": stack.state.num_slots}
+
+
+def cpu_baseline_stack(seconds=10.0):
+    """The block's work on the host: the oracle's Q8_0 dequantisation of one Cosmos-14B block (all tensors) and a
+    torch CPU forward of its projections on 64 token rows, extrapolated by FLOPs to 8192 rows and 36 blocks."""
+    import torch
+    from oracle import oracle
+    rng = np.random.default_rng(4)
+    sizes = [(a, b) for a, b in cosmos14b_block_shapes()]
+    t0 = time.perf_counter()
+    deq_s = 0.0
+    gemm_s = 0.0
+    reps = 0
+    while time.perf_counter() - t0 < seconds:
+        for a, b in sizes[:4] + sizes[8:10]:
+            nb = a * b // 32
+            raw = np.empty((nb, 34), dtype=np.uint8)
+            raw[:, 2:] = rng.integers(0, 256, size=(nb, 32), dtype=np.uint8)
+            raw[:, 0:2] = (np.abs(rng.standard_normal((nb, 1))) * 0.002).astype(np.float16).view(np.uint8)
+            t = time.perf_counter()
+            w = oracle.dequant_gguf(raw, a * b, 8, 0, 1)
+            deq_s += time.perf_counter() - t
+            wt = torch.from_numpy(w.view(np.int16)).view(torch.bfloat16).reshape(a, b).float()
+            x = torch.randn((64, b))
+            t = time.perf_counter()
+            _y = x @ wt.t()
+            gemm_s += time.perf_counter() - t
+        reps += 1
+    # the sample covered q/k/v/o and the MLP (the block's dominant bytes and FLOPs): scale GEMMs to 8192 rows
+    per_block = deq_s / reps * (417_792_000 / (34 / 32 * sum(a * b for a, b in sizes[:4] + sizes[8:10])))
+    per_block += gemm_s / reps * (8192 / 64)
+    return per_block * 36, torch.get_num_threads(), (f"{reps} reps of the oracle dequant + CPU GEMMs of one block's "
+                                                     "q/k/v/o/MLP weights on 64 rows, extrapolated to 8192 rows, "
+                                                     "all weights and 36 blocks")
+
+
+def finish_stack(torch, args, world, rank, dist, r):
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        v, threads, sample = cpu_baseline_stack(args.cpu_seconds)
+        cpu = {"value": round(v, 2), "unit": "s/step", "cores": threads, "kind": "port", "sample": sample}
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        frac = r["h2d_rate"] / r["probe"]
+        print(json.dumps({
+            "metric": "streamed 14B DiT block-stack s/step", "value": round(r["ms"] / 1e3, 5), "unit": "s/step",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 3),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "Q8_0 -> bf16",
+            "data": "synthetic (seeded)",
+            "config": {"workload": "Cosmos-Predict2-14B-shaped stack (configs[4]): 36 blocks, hidden 5120, 40 x 128 "
+                                   "heads, MLP 20480, Q8_0 weights in pinned host RAM, batch 2 x 4096 tokens + 512 "
+                                   "context tokens", "blocks": args.blocks, "slots": r["slots"],
+                       "parallelism": f"tp{world} (column/row split, sequence-sharded residual)",
+                       "h2d_bytes_per_block_per_rank": r["h2d_rank"] // args.blocks,
+                       "h2d_probe_gbs_per_rank": round(r["probe"], 2), "finite_output": r["finite"],
+                       "build_s": round(r["build_s"], 1),
+                       "timeline_one_forward": r["summary"]},
+            "roofline": {"bound": "pcie_h2d", "achieved": round(r["h2d_rate"], 2), "peak": round(r["probe"], 2),
+                         "unit": "GB/s per rank", "frac": round(frac, 4), "traffic": None,
+                         "peak_source": "pinned 1 GiB cudaMemcpyAsync H2D measured in this run",
+                         "tflops_per_gpu": round(r["flops"] / world / (r["ms"] / 1e3) / 1e12, 1)},
+            "cpu_baseline": cpu, "e2e": r["e2e"], "gpu_launches": None, "clocks": r["clk"]}), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_single_weight(torch, args, world, rank, dist, which):
     """configs[0] (Q8_0 5120x5120) or configs[1]'s weight (Q4_K 5120x13824): one launch per step, L2 flushed."""
     gd = _pkg("enhancers.gguf_dequant")
@@ -532,7 +693,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="sweep", choices=["sweep", "q8", "q4k", "w8a8"])
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "q8", "q4k", "w8a8", "stack"])
+    ap.add_argument("--slots", type=int, default=3, help="stack: GPU slots of the streaming ring")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -548,6 +710,8 @@ def main():
     world, rank, local, dist = setup_dist(torch)
     if args.workload == "sweep":
         r = run_sweep(torch, args, world, rank, dist)
+    elif args.workload == "stack":
+        return finish_stack(torch, args, world, rank, dist, run_stack(torch, args, world, rank, dist))
     elif args.workload == "w8a8":
         return finish_w8a8(torch, args, world, rank, dist, run_w8a8(torch, args, world, rank, dist))
     else:

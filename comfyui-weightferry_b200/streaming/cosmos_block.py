@@ -1,0 +1,301 @@
+"""The Cosmos-Predict2 DiT block on B200, single-GPU or tensor-parallel, on streamed (dequantised) weights.
+
+The block is ComfyUI's comfy/ldm/cosmos/predict2.py Block as the reference's fused forward runs it
+(enhancers/fused_block.py:652-703): adaLN shift / scale / gate from the timestep embedding (+ the AdaLN-LoRA term),
+then three sub-layers, each ``x = x + gate * sublayer(LayerNorm(x) * (1 + scale) + shift)``:
+
+* self-attention: q / k / v projections, per-head RMSNorm-128 + 3D RoPE on q and k (kernel B), attention
+  (PyTorch SDPA), output projection;
+* cross-attention: q projection + RMSNorm-128 of q, k / v from the text context + RMSNorm-128 of k, attention,
+  output projection;
+* MLP: layer1, GELU, layer2.
+
+LayerNorm + modulate is kernel A (one pass), the projections are cuBLAS bf16 GEMMs on the weights the streaming
+state dequantised on arrival.
+
+Tensor parallel over N GPUs (one process per GPU, NCCL over NVLink): the residual stream is sharded by token rows
+(each rank holds rows [r * R, (r + 1) * R) of the B * L rows); before each sub-layer the modulated rows are
+all-gathered, q / k / v / layer1 (and the cross-attention's q, k, v) are column-parallel (each rank owns
+heads / N heads and 20480 / N MLP channels), the output projections are row-parallel and their partial sums are
+reduce-scattered back to the token shards. Each rank streams only its shards of the block's weights (the adaLN
+weights, 4 % of the bytes, are replicated). Parameter names follow ComfyUI's module paths.
+"""
+
+import torch
+import torch.nn.functional as F
+
+from ..enhancers import fused_block as _fb
+from ..enhancers import sage_fused as _sf
+from .state import ParamSpec
+
+Q8_0 = 8
+
+
+class CosmosConfig:
+    def __init__(self, hidden=5120, heads=40, head_dim=128, mlp=20480, ctx_dim=1024, lora=256, eps=1e-6):
+        self.hidden, self.heads, self.head_dim, self.mlp = hidden, heads, head_dim, mlp
+        self.ctx_dim, self.lora, self.eps = ctx_dim, lora, eps
+
+
+COSMOS_14B = CosmosConfig()
+COSMOS_2B = CosmosConfig(hidden=2048, heads=16, mlp=8192)
+
+
+def block_specs(cfg, world=1, rank=0, qtype=Q8_0):
+    """ParamSpecs of this rank's share of one block: column-parallel projections split their output rows,
+    row-parallel ones their input columns; adaLN and norm weights replicated."""
+    if cfg.heads % world or cfg.mlp % world or cfg.hidden % world:
+        raise ValueError(f"{world} ranks do not divide heads {cfg.heads} / mlp {cfg.mlp}")
+    D, Dw, Mw = cfg.hidden, cfg.hidden // world, cfg.mlp // world
+    s = []
+    for name in ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight"):
+        s.append(ParamSpec(name, (Dw, D), qtype=qtype))
+    s.append(ParamSpec("self_attn.output_proj.weight", (D, Dw), qtype=qtype))
+    s.append(ParamSpec("cross_attn.q_proj.weight", (Dw, D), qtype=qtype))
+    s.append(ParamSpec("cross_attn.k_proj.weight", (Dw, cfg.ctx_dim), qtype=qtype))
+    s.append(ParamSpec("cross_attn.v_proj.weight", (Dw, cfg.ctx_dim), qtype=qtype))
+    s.append(ParamSpec("cross_attn.output_proj.weight", (D, Dw), qtype=qtype))
+    s.append(ParamSpec("mlp.layer1.weight", (Mw, D), qtype=qtype))
+    s.append(ParamSpec("mlp.layer2.weight", (D, Mw), qtype=qtype))
+    for sub in ("self_attn", "cross_attn", "mlp"):
+        s.append(ParamSpec(f"adaln_modulation_{sub}.1.weight", (cfg.lora, D), qtype=qtype))
+        s.append(ParamSpec(f"adaln_modulation_{sub}.2.weight", (3 * D, cfg.lora), qtype=qtype))
+    for sub in ("self_attn", "cross_attn"):
+        s.append(ParamSpec(f"{sub}.q_norm.weight", (cfg.head_dim,), dtype=torch.bfloat16))
+        s.append(ParamSpec(f"{sub}.k_norm.weight", (cfg.head_dim,), dtype=torch.bfloat16))
+    return s
+
+
+def shard_of(name, world, rank):
+    """How parameter `name` is split across ranks: ("col", lo, hi) on rows, ("row", lo, hi) on columns (fractions
+    of the full dimension as rank / world), or None (replicated)."""
+    if world == 1:
+        return None
+    if name.endswith(("q_proj.weight", "k_proj.weight", "v_proj.weight", "mlp.layer1.weight")):
+        return ("col", rank, world)
+    if name.endswith(("output_proj.weight", "mlp.layer2.weight")):
+        return ("row", rank, world)
+    return None
+
+
+def full_shape(spec, world):
+    kind = shard_of(spec.name, world, 0)
+    if kind is None:
+        return spec.shape
+    if kind[0] == "col":
+        return (spec.shape[0] * world, spec.shape[1])
+    return (spec.shape[0], spec.shape[1] * world)
+
+
+def q8_0_pack(q_int8, d_f16):
+    """Q8_0 blocks from int8 quants [rows, cols] and float16 scales [rows, cols / 32]: (rows, cols / 32 * 34) bytes."""
+    rows, cols = q_int8.shape
+    nb = cols // 32
+    q = q_int8.view(torch.uint8).reshape(rows, nb, 32)
+    d = d_f16.contiguous().view(torch.uint8).reshape(rows, nb, 2)
+    return torch.cat([d, q], dim=2).reshape(rows, nb * 34)
+
+
+def q8_0_shard(packed_full, shape, kind):
+    """The packed bytes of one rank's shard of a Q8_0 weight [rows, cols] (kind from shard_of)."""
+    rows, cols = shape
+    nb = cols // 32
+    p = packed_full.view(rows, nb, 34)
+    if kind is None:
+        return p.reshape(-1)
+    _, r, w = kind
+    if kind[0] == "col":
+        lo, hi = rows * r // w, rows * (r + 1) // w
+        return p[lo:hi].reshape(-1)
+    lo, hi = nb * r // w, nb * (r + 1) // w
+    return p[:, lo:hi].contiguous().reshape(-1)
+
+
+def make_block_params(cfg, specs, world, rank, seed, device, d_scale=0.002):
+    """Seeded synthetic weights of one block as BASELINE configs[4] describes them (Q8_0 as configs[0]: quants
+    uniform in [-127, 127], d = fp16(|N(0,1)| * 0.002); the adaLN weights scaled down so the gates stay small;
+    norm weights 1 + N(0, 0.02)), generated in full on `device` and cut to this rank's shard. Returns name -> CPU
+    tensor (packed uint8 for quantised parameters)."""
+    out = {}
+    g = torch.Generator(device=device)
+    for i, sp in enumerate(specs):
+        g.manual_seed(seed * 1000 + i)
+        if sp.qtype is None:
+            w = (1 + torch.randn(sp.shape, device=device, generator=g) * 0.02).to(sp.dtype)
+            out[sp.name] = w.cpu()
+            continue
+        rows, cols = full_shape(sp, world)
+        q = torch.randint(-127, 128, (rows, cols), dtype=torch.int16, device=device, generator=g).to(torch.int8)
+        scale = d_scale * (0.05 if "adaln" in sp.name else 1.0)
+        d = (torch.randn((rows, cols // 32), device=device, generator=g).abs() * scale).half()
+        packed = q8_0_pack(q, d)
+        out[sp.name] = q8_0_shard(packed, (rows, cols), shard_of(sp.name, world, rank)).cpu()
+    return out
+
+
+# ---------------------------------------------------------------------------------------------- RoPE
+def rope3d_table(T, H, W, head_dim=128, theta=10000.0, h_extra=4.0, w_extra=4.0, t_extra=1.0, device=None):
+    """Cosmos-Predict2's 3D RoPE rotations as a (1, T*H*W, 1, head_dim/2, 2, 2) float32 table (VideoRopePosition3DEmb's
+    layout as the reference's rope_scale.py:29-60 restates it): head dim split into h / w / t channel groups
+    (128 -> 42 / 42 / 44), NTK factors from the extrapolation ratios, tokens in (t h w) order, t then h then w."""
+    dim_h = head_dim // 6 * 2
+    dim_t = head_dim - 2 * dim_h
+    rng_hw = torch.arange(0, dim_h, 2, dtype=torch.float64) / dim_h
+    rng_t = torch.arange(0, dim_t, 2, dtype=torch.float64) / dim_t
+    h_ntk = h_extra ** (dim_h / (dim_h - 2))
+    w_ntk = w_extra ** (dim_h / (dim_h - 2))
+    t_ntk = t_extra ** (dim_t / (dim_t - 2))
+    hf = 1.0 / ((theta * h_ntk) ** rng_hw)
+    wf = 1.0 / ((theta * w_ntk) ** rng_hw)
+    tf = 1.0 / ((theta * t_ntk) ** rng_t)
+    ht = torch.outer(torch.arange(H, dtype=torch.float64), hf)
+    wt = torch.outer(torch.arange(W, dtype=torch.float64), wf)
+    tt = torch.outer(torch.arange(T, dtype=torch.float64), tf)
+
+    def rot(e):
+        return torch.stack([torch.cos(e), -torch.sin(e), torch.sin(e), torch.cos(e)], dim=-1)
+    ht, wt, tt = rot(ht), rot(wt), rot(tt)
+    nt, nh = tt.shape[1], ht.shape[1]
+    em = torch.cat([tt[:, None, None].expand(T, H, W, nt, 4), ht[None, :, None].expand(T, H, W, nh, 4),
+                    wt[None, None, :].expand(T, H, W, nh, 4)], dim=-2)
+    return em.reshape(1, T * H * W, 1, head_dim // 2, 2, 2).float().contiguous().to(device)
+
+
+# ---------------------------------------------------------------------------------------------- TP plumbing
+class TP:
+    """The tensor-parallel group of the stack (None-like when world == 1)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist = dist if dist.is_available() and dist.is_initialized() else None
+        self.group = group
+        self.world = self.dist.get_world_size(group) if self.dist else 1
+        self.rank = self.dist.get_rank(group) if self.dist else 0
+
+    def all_gather_rows(self, x_local):
+        if self.world == 1:
+            return x_local
+        out = torch.empty((x_local.shape[0] * self.world,) + tuple(x_local.shape[1:]), dtype=x_local.dtype,
+                          device=x_local.device)
+        self.dist.all_gather_into_tensor(out, x_local.contiguous(), group=self.group)
+        return out
+
+    def reduce_scatter_rows(self, x_full):
+        if self.world == 1:
+            return x_full
+        rows = x_full.shape[0] // self.world
+        out = torch.empty((rows,) + tuple(x_full.shape[1:]), dtype=x_full.dtype, device=x_full.device)
+        self.dist.reduce_scatter_tensor(out, x_full.contiguous(), group=self.group)
+        return out
+
+
+def _ln_mod_rows(x_rows, scale_b, shift_b, row0, rows_per_batch, eps):
+    """Kernel A over this rank's token rows [row0, row0 + n) of a (B * L, D) stream whose batch b has rows
+    [b * L, (b + 1) * L): scale / shift are (B, D). The shard either holds whole batches or lies inside one."""
+    n, D = x_rows.shape
+    if n >= rows_per_batch:
+        b0, nb = row0 // rows_per_batch, n // rows_per_batch
+        sc, sh, rpg = scale_b[b0:b0 + nb], shift_b[b0:b0 + nb], rows_per_batch
+    else:
+        b0 = row0 // rows_per_batch
+        sc, sh, rpg = scale_b[b0:b0 + 1], shift_b[b0:b0 + 1], n
+    g = sc.shape[0]
+    out = _fb.ln_modulate_rows(x_rows.view(g, 1, 1, rpg, D), sc.view(g, 1, 1, 1, D), sh.view(g, 1, 1, 1, D), eps)
+    return out.view(n, D)
+
+
+def _residual(x_rows, gate_b, o, row0, rows_per_batch):
+    """x + gate * o on the shard's rows (ComfyUI's torch.addcmul), gate_b (B, D) broadcast over each batch's rows."""
+    n, D = x_rows.shape
+    b0 = row0 // rows_per_batch
+    if n >= rows_per_batch:
+        nb = n // rows_per_batch
+        return torch.addcmul(x_rows.view(nb, rows_per_batch, D), gate_b[b0:b0 + nb].view(nb, 1, D),
+                             o.view(nb, rows_per_batch, D)).view(n, D)
+    return torch.addcmul(x_rows, gate_b[b0:b0 + 1], o)
+
+
+def _attention(q, k, v):
+    """softmax(q k^T / sqrt(d)) v for (B, L, H, d) tensors -> (B, L, H * d)."""
+    o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+    B, H, L, d = o.shape
+    return o.transpose(1, 2).reshape(B, L, H * d)
+
+
+def adaln(W, sub, emb, lora_term):
+    """(shift, scale, gate), each (B, D), of one sub-layer: Linear(Linear(SiLU(emb))) + AdaLN-LoRA term."""
+    h = F.linear(F.silu(emb), W[f"adaln_modulation_{sub}.1.weight"])
+    m = F.linear(h, W[f"adaln_modulation_{sub}.2.weight"]) + lora_term
+    return m.chunk(3, dim=-1)
+
+
+def block_forward(x_rows, emb, ctx, rope, W, cfg, tp, batch, tokens, lora_term=None):
+    """One block on this rank's token rows x_rows (n, D) of the (batch * tokens, D) stream; emb (B, D) timestep
+    embedding, ctx (B, S, ctx_dim) text context, rope (1, tokens, 1, 64, 2, 2), lora_term (B, 3D) the AdaLN-LoRA
+    term (or None). W: name -> this rank's tensors. Returns the new (n, D) rows."""
+    n, D = x_rows.shape
+    row0 = tp.rank * n
+    hd = cfg.head_dim
+    Hw = cfg.heads // tp.world
+    if lora_term is None:
+        lora_term = emb.new_zeros(())
+    eps = cfg.eps
+
+    # --- self-attention
+    shift, scale, gate = adaln(W, "self_attn", emb, lora_term)
+    normed = tp.all_gather_rows(_ln_mod_rows(x_rows, scale, shift, row0, tokens, eps))       # (B*L, D)
+    q = F.linear(normed, W["self_attn.q_proj.weight"]).view(batch, tokens, Hw, hd)
+    k = F.linear(normed, W["self_attn.k_proj.weight"]).view(batch, tokens, Hw, hd)
+    v = F.linear(normed, W["self_attn.v_proj.weight"]).view(batch, tokens, Hw, hd)
+    q = _sf.rms_rope(q, rope, W["self_attn.q_norm.weight"], eps)
+    k = _sf.rms_rope(k, rope, W["self_attn.k_norm.weight"], eps)
+    a = _attention(q, k, v).view(batch * tokens, Hw * hd)
+    o = tp.reduce_scatter_rows(F.linear(a, W["self_attn.output_proj.weight"]))              # (n, D)
+    x_rows = _residual(x_rows, gate, o, row0, tokens)
+
+    # --- cross-attention
+    shift, scale, gate = adaln(W, "cross_attn", emb, lora_term)
+    normed = tp.all_gather_rows(_ln_mod_rows(x_rows, scale, shift, row0, tokens, eps))
+    q = F.linear(normed, W["cross_attn.q_proj.weight"]).view(batch, tokens, Hw, hd)
+    q = _fb.rms_norm_128(q.contiguous(), W["cross_attn.q_norm.weight"], eps)
+    S = ctx.shape[1]
+    kc = F.linear(ctx, W["cross_attn.k_proj.weight"]).view(batch, S, Hw, hd)
+    kc = _fb.rms_norm_128(kc.contiguous(), W["cross_attn.k_norm.weight"], eps)
+    vc = F.linear(ctx, W["cross_attn.v_proj.weight"]).view(batch, S, Hw, hd)
+    a = _attention(q, kc, vc).view(batch * tokens, Hw * hd)
+    o = tp.reduce_scatter_rows(F.linear(a, W["cross_attn.output_proj.weight"]))
+    x_rows = _residual(x_rows, gate, o, row0, tokens)
+
+    # --- MLP
+    shift, scale, gate = adaln(W, "mlp", emb, lora_term)
+    normed = tp.all_gather_rows(_ln_mod_rows(x_rows, scale, shift, row0, tokens, eps))
+    h = F.gelu(F.linear(normed, W["mlp.layer1.weight"]))
+    o = tp.reduce_scatter_rows(F.linear(h, W["mlp.layer2.weight"]))
+    return _residual(x_rows, gate, o, row0, tokens)
+
+
+def block_forward_fused(self, x_B_T_H_W_D, emb_B_T_D, crossattn_emb, rope_emb_L_1_1_D=None, adaln_lora_B_T_3D=None,
+                        extra_per_block_pos_emb=None, transformer_options={}):
+    """ComfyUI Block.forward semantics on a block module with ComfyUI's attribute names (single GPU): the fused
+    parts' body used by fused_block._block_forward."""
+    if extra_per_block_pos_emb is not None:
+        x_B_T_H_W_D = x_B_T_H_W_D + extra_per_block_pos_emb
+    B, T, H, Wd, D = x_B_T_H_W_D.shape
+    W = {k: v.data for k, v in self.named_parameters()}
+    lora = None if adaln_lora_B_T_3D is None else adaln_lora_B_T_3D.reshape(B, -1)
+    cfg = getattr(self, "_wf_cfg", None) or CosmosConfig(hidden=D, heads=D // 128)
+    rope = rope_emb_L_1_1_D
+    if rope is not None and rope.dim() != 6:
+        rope = rope.reshape(1, T * H * Wd, 1, 64, 2, 2).float()
+    out = block_forward(x_B_T_H_W_D.reshape(B * T * H * Wd, D), emb_B_T_D.reshape(B, D), crossattn_emb, rope, W, cfg,
+                        TP(), B, T * H * Wd, lora_term=lora)
+    return out.view(B, T, H, Wd, D)
+
+
+def flops_per_block(cfg, batch, tokens, ctx_tokens):
+    """Dense GEMM + attention FLOPs of one block (all ranks together)."""
+    M, D, Mh = batch * tokens, cfg.hidden, cfg.mlp
+    gemm = 2 * M * D * D * 4 + 2 * M * D * D * 2 + 2 * batch * ctx_tokens * cfg.ctx_dim * D * 2 + 2 * M * D * Mh * 2
+    attn = 4 * batch * tokens * tokens * D + 4 * batch * tokens * ctx_tokens * D
+    return gemm + attn
+
