@@ -16,7 +16,7 @@
 //               nearest), w_s of the tile staged in shared memory, optional raw int32 copy, 16-byte stores.
 // Every mbarrier wait is bounded in time (about 2 s): on expiry the CTA records an error code (read with
 // wf_w8a8_gemm_status), stops issuing work, waits (bounded) for its own copies and MMAs in flight, frees its tensor
-// memory and returns. No load in this file uses cluster multicast; operands are always this GPU's own memory.
+// memory and returns. Every TMA load here is a plain per-CTA load of this GPU's own memory.
 
 #include "wf_common.cuh"
 

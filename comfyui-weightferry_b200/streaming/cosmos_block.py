@@ -163,29 +163,44 @@ def rope3d_table(T, H, W, head_dim=128, theta=10000.0, h_extra=4.0, w_extra=4.0,
 
 # ---------------------------------------------------------------------------------------------- TP plumbing
 class TP:
-    """The tensor-parallel group of the stack (None-like when world == 1)."""
+    """The tensor-parallel group of the stack: the initialised torch.distributed group (NCCL over NVLink for CUDA
+    tensors), or a single rank when there is none / ``single=True``."""
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, single=False):
         import torch.distributed as dist
-        self.dist = dist if dist.is_available() and dist.is_initialized() else None
+        on = dist.is_available() and dist.is_initialized() and not single
+        self.dist = dist if on else None
         self.group = group
         self.world = self.dist.get_world_size(group) if self.dist else 1
         self.rank = self.dist.get_rank(group) if self.dist else 0
+        self.gloo = bool(self.dist) and self.dist.get_backend(group) == "gloo"
 
     def all_gather_rows(self, x_local):
+        """(R, ...) rows of every rank -> (world * R, ...) in rank order."""
         if self.world == 1:
             return x_local
+        x_local = x_local.contiguous()
+        if self.gloo:  # gloo has no all_gather_into_tensor
+            parts = [torch.empty_like(x_local) for _ in range(self.world)]
+            self.dist.all_gather(parts, x_local, group=self.group)
+            return torch.cat(parts, dim=0)
         out = torch.empty((x_local.shape[0] * self.world,) + tuple(x_local.shape[1:]), dtype=x_local.dtype,
                           device=x_local.device)
-        self.dist.all_gather_into_tensor(out, x_local.contiguous(), group=self.group)
+        self.dist.all_gather_into_tensor(out, x_local, group=self.group)
         return out
 
     def reduce_scatter_rows(self, x_full):
+        """Sum over ranks of (world * R, ...) -> this rank's (R, ...) rows."""
         if self.world == 1:
             return x_full
         rows = x_full.shape[0] // self.world
+        x_full = x_full.contiguous()
+        if self.gloo:  # gloo has no reduce_scatter_tensor
+            t = x_full.clone()
+            self.dist.all_reduce(t, group=self.group)
+            return t[self.rank * rows:(self.rank + 1) * rows].contiguous()
         out = torch.empty((rows,) + tuple(x_full.shape[1:]), dtype=x_full.dtype, device=x_full.device)
-        self.dist.reduce_scatter_tensor(out, x_full.contiguous(), group=self.group)
+        self.dist.reduce_scatter_tensor(out, x_full, group=self.group)
         return out
 
 
