@@ -52,6 +52,7 @@ extern "C" WF_API const char *wf_status_string(int status) {
         case WF_ERR_UNSUPPORTED: return "unsupported type or mode";
         case WF_ERR_SHAPE: return "byte count and value count disagree for this format";
         case WF_ERR_DEVICE: return "no usable sm_100 device is current";
+        case WF_ERR_TOO_LARGE: return "problem larger than the library's fixed buffer (no-allocation entry point)";
         default: break;
     }
     if (status > 0) return cudaGetErrorString(static_cast<cudaError_t>(status));

@@ -33,7 +33,8 @@ enum {
     WF_ERR_ARG = -1,         /* a size, pointer or dtype outside the contract */
     WF_ERR_UNSUPPORTED = -2, /* a GGML type id (or mode) this library does not decode */
     WF_ERR_SHAPE = -3,       /* byte count and value count disagree for the format */
-    WF_ERR_DEVICE = -4       /* the current device is not an sm_100 part, or no device */
+    WF_ERR_DEVICE = -4,      /* the current device is not an sm_100 part, or no device */
+    WF_ERR_TOO_LARGE = -5    /* the problem exceeds a fixed-size buffer of the library */
 };
 
 enum { WF_F16 = 0, WF_BF16 = 1, WF_F32 = 2 };
@@ -134,6 +135,18 @@ WF_API int wf_w8a8_gemm(const int8_t *xq, const int8_t *wq, const float *xs, con
  * early and its output is incomplete). Reading it synchronises the device and clears it. No reference counterpart
  * (the reference's GEMM is a closed library call); it is this library's failure report. */
 WF_API int wf_w8a8_gemm_status(int *status);
+
+/* W8A8 linear that allocates nothing: y = bf16((float(xq @ wq^T) * xs) * ws) where xq / xs are the per-token absmax
+ * int8 quantisation of the bf16 activations x [m, k] (what wf_quant_rows with pre 0, rotate 0 produces), kept in a
+ * fixed buffer inside the library instead of caller memory. For callers that cannot allocate device memory when
+ * they run (an application whose allocator owns the GPU's memory, or a path where a cudaMalloc and its possible
+ * device synchronisation are not allowed). Limits: m * k <= 16,777,216 and m <= 65,536, else WF_ERR_TOO_LARGE;
+ * the operand rules of wf_quant_rows and wf_w8a8_gemm apply. The buffer (about 16.3 MB per GPU that loads the
+ * library) is shared by every call: calls that overlap on the GPU race. The first call on a device looks the
+ * buffer up for that device; make it before any stream capture. This entry point has no counterpart in the
+ * reference. */
+WF_API int wf_w8a8_linear_noalloc(const void *x, const int8_t *wq, const float *ws, void *y, int64_t m, int64_t n,
+                                  int64_t k, wf_stream_t stream);
 
 #ifdef __cplusplus
 }
