@@ -110,11 +110,97 @@ __device__ __forceinline__ void welford_step(Welford &w, float v) {
     w.s = __fmaf_rn(delta, __fsub_rn(v, w.m), w.s);
 }
 
+// The same update when this is the thread's i-th value (i = 0, 1, ...): the count is i + 1 for every thread, so the
+// correctly rounded 1 / count comes from a table (the host's IEEE division of 1 by i + 1: the same bits as div.rn).
+struct RcpTable {
+    float v[64];
+};
+constexpr RcpTable make_rcp() {
+    RcpTable t{};
+    for (int i = 0; i < 64; ++i) t.v[i] = 1.0f / static_cast<float>(i + 1);
+    return t;
+}
+__constant__ RcpTable c_rcp = make_rcp();
+
+__device__ __forceinline__ void welford_step_i(Welford &w, float v, int i) {
+    const float delta = __fsub_rn(v, w.m);
+    w.c = static_cast<float>(i + 1);
+    w.m = __fmaf_rn(delta, c_rcp.v[i], w.m);
+    w.s = __fmaf_rn(delta, __fsub_rn(v, w.m), w.s);
+}
+
+// bf16 rounding of a pair through the packed RNE conversion (the same value as the bit-level rounding on every
+// non-NaN input)
+__device__ __forceinline__ float2 r16x2(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const uint32_t u = *reinterpret_cast<const uint32_t *>(&h);
+    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+}
+
 __device__ __forceinline__ void ln_merge(Welford w, int64_t K, float &mu, float &var, float *red);
+
+// wcombine of two states that each hold C values: the count C + C and its correctly rounded reciprocal are
+// compile-time constants (C is the same in every lane), so the division of the merge becomes a product
+template <int C>
+__device__ __forceinline__ Welford wcombine_n(Welford own, Welford oth) {
+    constexpr float count = static_cast<float>(2 * C);
+    constexpr float coef = 1.0f / count;  // evaluated at compile time in IEEE arithmetic: div.rn's value
+    const float delta = __fsub_rn(own.m, oth.m);
+    const float n_a = __fmul_rn(oth.c, coef);
+    const float n_b = __fmul_rn(own.c, coef);
+    Welford r;
+    r.m = __fmaf_rn(n_a, oth.m, __fmul_rn(n_b, own.m));
+    r.s = __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), oth.c), n_b, __fadd_rn(oth.s, own.s));
+    r.c = count;
+    return r;
+}
+
+template <int N>  // values per thread (4 * K / 512)
+__device__ __forceinline__ void ln_merge_n(Welford w, int64_t K, float &mu, float &var, float *red) {
+#define WF_SHFL_MERGE(OFF, C)                                   \
+    {                                                           \
+        Welford o;                                              \
+        o.m = __shfl_down_sync(0xFFFFFFFFu, w.m, OFF);          \
+        o.s = __shfl_down_sync(0xFFFFFFFFu, w.s, OFF);          \
+        o.c = __shfl_down_sync(0xFFFFFFFFu, w.c, OFF);          \
+        w = wcombine_n<C>(w, o);                                \
+    }
+    WF_SHFL_MERGE(16, N) WF_SHFL_MERGE(8, 2 * N) WF_SHFL_MERGE(4, 4 * N) WF_SHFL_MERGE(2, 8 * N)
+    WF_SHFL_MERGE(1, 16 * N)
+#undef WF_SHFL_MERGE
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        red[warp * 3 + 0] = w.m;
+        red[warp * 3 + 1] = w.s;
+        red[warp * 3 + 2] = w.c;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        Welford w0{red[0], red[1], red[2]}, w1{red[3], red[4], red[5]}, w2{red[6], red[7], red[8]},
+            w3{red[9], red[10], red[11]};
+        w0 = wcombine_n<32 * N>(w0, w2);
+        w1 = wcombine_n<32 * N>(w1, w3);
+        w0 = wcombine_n<64 * N>(w0, w1);
+        red[12] = w0.m;
+        red[13] = __fdiv_rn(w0.s, static_cast<float>(K));
+    }
+    __syncthreads();
+    mu = red[12];
+    var = red[13];
+}
+
+template <int N>
+__device__ __forceinline__ void ln_stats_n(const float *v, int64_t K, float &mu, float &var, float *red) {
+    Welford w{0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < N; ++i) welford_step_i(w, v[i], i);
+    ln_merge_n<N>(w, K, mu, var, red);
+}
 
 __device__ __forceinline__ void ln_stats(const float *v, int nv, int64_t K, float &mu, float &var, float *red) {
     Welford w{0.f, 0.f, 0.f};
-    for (int i = 0; i < nv; ++i) welford_step(w, v[i]);
+#pragma unroll
+    for (int i = 0; i < nv; ++i) welford_step_i(w, v[i], i);
     ln_merge(w, K, mu, var, red);
 }
 
@@ -124,10 +210,10 @@ __device__ __forceinline__ void ln_stats_strided(const float *p, int nvec, int64
     Welford w{0.f, 0.f, 0.f};
     for (int j = 0; j < nvec; ++j) {
         const float4 v = *reinterpret_cast<const float4 *>(p + 512 * j);
-        welford_step(w, v.x);
-        welford_step(w, v.y);
-        welford_step(w, v.z);
-        welford_step(w, v.w);
+        welford_step_i(w, v.x, 4 * j);
+        welford_step_i(w, v.y, 4 * j + 1);
+        welford_step_i(w, v.z, 4 * j + 2);
+        welford_step_i(w, v.w, 4 * j + 3);
     }
     ln_merge(w, K, mu, var, red);
 }
@@ -163,39 +249,82 @@ __device__ __forceinline__ void ln_merge(Welford w, int64_t K, float &mu, float 
 }
 
 // ------------------------------------------------------------------------------------------------- kernel A
-// LayerNorm (no affine) + modulate, one row per CTA of 128 threads (fused_kernels.py:219-232 _lnmod):
+// LayerNorm (no affine) + modulate, one row at a time per CTA of 128 threads (fused_kernels.py:219-232 _lnmod):
 // x = R16((x - mu) * rsqrt.approx(var + eps)); out = R16(R16(x * s1) + shift). K % 512 == 0, NV = K / 512.
+// Persistent: CTA b handles rows b, b + gridDim.x, ...; the next row's x is loaded into registers while the current
+// row is reduced and written, so every thread keeps a row's loads in flight.
 template <int NV>
 __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *__restrict__ x,
                                                           const __nv_bfloat16 *__restrict__ s1,
                                                           const __nv_bfloat16 *__restrict__ sh,
-                                                          __nv_bfloat16 *__restrict__ out, int64_t K,
+                                                          __nv_bfloat16 *__restrict__ out, int64_t rows, int64_t K,
                                                           int64_t rows_per_group, float eps) {
     __shared__ float red[16];
-    const int64_t row = blockIdx.x;
     const int t = threadIdx.x;
-    const __nv_bfloat16 *xr = x + row * K;
-    float v[NV * 4];
+    int64_t row = blockIdx.x;
+    if (row >= rows) return;
+    uint2 raw[NV];
 #pragma unroll
-    for (int j = 0; j < NV; ++j) unpack4(__ldg(reinterpret_cast<const uint2 *>(xr) + t + 128 * j), v + 4 * j);
-    float mu, var;
-    ln_stats(v, NV * 4, K, mu, var, red);
-    const float rstd = rsqrt_approx(__fadd_rn(var, eps));
-    const int64_t goff = (row / rows_per_group) * K;
+    for (int j = 0; j < NV; ++j) raw[j] = __ldg(reinterpret_cast<const uint2 *>(x + row * K) + t + 128 * j);
+    uint2 sraw[NV], hraw[NV];
+    int64_t cached_group = -1;
+    for (; row < rows; row += gridDim.x) {
+        float v[NV * 4];
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        const int64_t c = static_cast<int64_t>(t + 128 * j) * 4;
-        float s[4], h[4];
-        unpack4(__ldg(reinterpret_cast<const uint2 *>(s1 + goff + c)), s);
-        unpack4(__ldg(reinterpret_cast<const uint2 *>(sh + goff + c)), h);
-        float o[4];
+        for (int j = 0; j < NV; ++j) unpack4(raw[j], v + 4 * j);
+        const int64_t nrow = row + gridDim.x;
+        if (nrow < rows) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float n = r16(__fmul_rn(__fsub_rn(v[4 * j + k], mu), rstd));
-            o[k] = __fadd_rn(r16(__fmul_rn(n, s[k])), h[k]);
+            for (int j = 0; j < NV; ++j) raw[j] = __ldg(reinterpret_cast<const uint2 *>(x + nrow * K) + t + 128 * j);
         }
-        *reinterpret_cast<uint2 *>(out + row * K + c) = make_uint2(pack2(o[0], o[1]), pack2(o[2], o[3]));
+        // the modulation rows of this row's group (kept while consecutive rows stay in one group)
+        const int64_t group = static_cast<int64_t>(static_cast<uint32_t>(row) / static_cast<uint32_t>(rows_per_group));
+        if (group != cached_group) {
+            cached_group = group;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                sraw[j] = __ldg(reinterpret_cast<const uint2 *>(s1 + group * K) + t + 128 * j);
+                hraw[j] = __ldg(reinterpret_cast<const uint2 *>(sh + group * K) + t + 128 * j);
+            }
+        }
+        float mu, var;
+        ln_stats_n<NV * 4>(v, K, mu, var, red);
+        const float rstd = rsqrt_approx(__fadd_rn(var, eps));
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int64_t c = static_cast<int64_t>(t + 128 * j) * 4;
+            float sv[4], h[4];
+            unpack4(sraw[j], sv);
+            unpack4(hraw[j], h);
+            float o[4];
+#pragma unroll
+            for (int k = 0; k < 4; k += 2) {
+                const float2 n = r16x2(__fmul_rn(__fsub_rn(v[4 * j + k], mu), rstd),
+                                       __fmul_rn(__fsub_rn(v[4 * j + k + 1], mu), rstd));
+                const float2 tt = r16x2(__fmul_rn(n.x, sv[k]), __fmul_rn(n.y, sv[k + 1]));
+                o[k] = __fadd_rn(tt.x, h[k]);
+                o[k + 1] = __fadd_rn(tt.y, h[k + 1]);
+            }
+            *reinterpret_cast<uint2 *>(out + row * K + c) = make_uint2(pack2(o[0], o[1]), pack2(o[2], o[3]));
+        }
+        __syncthreads();  // red[] is reused by the next row's statistics
     }
+}
+
+// resident CTAs per SM of a kernel (cached per kernel and device) times the SMs: a persistent grid's width
+template <auto KERN>
+int persistent_grid(int threads, size_t smem, int64_t items) {
+    auto kern = KERN;
+    static int occ[64] = {0};  // one cache per kernel: KERN is a template parameter
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int o = (dev >= 0 && dev < 64) ? occ[dev] : 0;
+    if (o == 0) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, threads, smem) != cudaSuccess || o < 1) o = 1;
+        if (dev >= 0 && dev < 64) occ[dev] = o;
+    }
+    const int64_t g = std::min<int64_t>(items, static_cast<int64_t>(o) * device_sm_count());
+    return static_cast<int>(std::max<int64_t>(g, 1));
 }
 
 // ------------------------------------------------------------------------------------------------- RMSNorm-128
@@ -232,44 +361,81 @@ __global__ void __launch_bounds__(256) rms128_kernel(const __nv_bfloat16 *__rest
 // reproduction of comfy_kitchen's rope kernel): lane t owns values t, t+32, t+64, t+96; squares summed by fma from
 // 0 in that order, pairwise lane tree, rr = rsqrt.approx(sum / 128 + eps), n = R16((x * rr) * w); then the pairs
 // (d, d + 64) rotate: y0 = R16(fma(f00, lo, f01 * hi)), y1 = R16(fma(f10, lo, f11 * hi)). Rotations f[token, d] are
-// float32 2x2 with element strides (s_tok, s_d, s_i, s_j). One row per warp, grid-strided.
+// float32 2x2 with element strides (s_tok, s_d, s_i, s_j).
+// One (batch, token) per warp: its rotations are read once for all its heads; the heads' rows are loaded four at a
+// time before any of them is reduced, so each warp keeps several loads in flight.
+template <bool F4>
+__device__ __forceinline__ void load_rot(const float *fd, int64_t s_i, int64_t s_j, float r[4]) {
+    if constexpr (F4) {
+        const float4 q = __ldg(reinterpret_cast<const float4 *>(fd));
+        r[0] = q.x; r[1] = q.y; r[2] = q.z; r[3] = q.w;
+    } else {
+        r[0] = __ldg(fd); r[1] = __ldg(fd + s_j); r[2] = __ldg(fd + s_i); r[3] = __ldg(fd + s_i + s_j);
+    }
+}
+
+constexpr int kRopeHeads = 16;  // head rows staged per warp at a time (4 KB)
+
+template <bool F4>
 __global__ void __launch_bounds__(256) rms_rope_kernel(const __nv_bfloat16 *__restrict__ x,
                                                        const float *__restrict__ f, const void *__restrict__ w,
-                                                       int wdt, __nv_bfloat16 *__restrict__ out, int64_t n_rows,
+                                                       int wdt, __nv_bfloat16 *__restrict__ out, int64_t n_tok,
                                                        int64_t heads, int64_t tokens, float eps, int64_t s_tok,
                                                        int64_t s_d, int64_t s_i, int64_t s_j) {
-    const int lane = threadIdx.x & 31;
+    // One (batch, token) per warp at a time: up to 16 of its head rows (4 KB) are copied into shared memory with
+    // 16-byte cp.async, the reduction reads the lane layout its order needs (t, t+32, t+64, t+96) from there, the
+    // results go back in place and leave with 16-byte stores; the token's rotations are read once for all its heads.
+    __shared__ __align__(16) __nv_bfloat16 stage[8][kRopeHeads * 128];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    __nv_bfloat16 *buf = stage[wid];
     float wv[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) wv[k] = load_w(w, wdt, lane + 32 * k);
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-    for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n_rows;
-         r += warps) {
-        const __nv_bfloat16 *xr = x + r * 128;
-        float v[4];
+    for (int64_t bt = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + wid; bt < n_tok; bt += warps) {
+        const int64_t tok = bt % tokens;
+        float rot[2][4];
+        load_rot<F4>(f + tok * s_tok + lane * s_d, s_i, s_j, rot[0]);
+        load_rot<F4>(f + tok * s_tok + (lane + 32) * s_d, s_i, s_j, rot[1]);
+        for (int64_t h0 = 0; h0 < heads; h0 += kRopeHeads) {
+            const int nh = static_cast<int>(heads - h0 < kRopeHeads ? heads - h0 : kRopeHeads);
+            const int chunks = nh * 16;  // 16-byte chunks of the nh rows
+            const uint4 *src = reinterpret_cast<const uint4 *>(x + (bt * heads + h0) * 128);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = __bfloat162float(xr[lane + 32 * k]);
-        float a = __fmul_rn(v[0], v[0]);
-        a = __fmaf_rn(v[1], v[1], a);
-        a = __fmaf_rn(v[2], v[2], a);
-        a = __fmaf_rn(v[3], v[3], a);
+            for (int i = 0; i < kRopeHeads / 2; ++i)
+                if (lane + 32 * i < chunks) cp_async16(reinterpret_cast<uint4 *>(buf) + lane + 32 * i, src + lane + 32 * i);
+            cp_async_commit();
+            cp_async_wait<0>();
+            __syncwarp();
+            for (int hh = 0; hh < nh; ++hh) {
+                __nv_bfloat16 *rowb = buf + hh * 128;
+                float v[4];
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xFFFFFFFFu, a, off));
-        a = __shfl_sync(0xFFFFFFFFu, a, 0);
-        const float rr = rsqrt_approx(__fadd_rn(__fmul_rn(a, 0.0078125f), eps));
-        float n[4];
+                for (int k = 0; k < 4; ++k) v[k] = __bfloat162float(rowb[lane + 32 * k]);
+                float a = __fmul_rn(v[0], v[0]);
+                a = __fmaf_rn(v[1], v[1], a);
+                a = __fmaf_rn(v[2], v[2], a);
+                a = __fmaf_rn(v[3], v[3], a);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) n[k] = r16(__fmul_rn(__fmul_rn(v[k], rr), wv[k]));
-        const int64_t tok = (r / heads) % tokens;
-        __nv_bfloat16 *orow = out + r * 128;
+                for (int off = 16; off >= 1; off >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xFFFFFFFFu, a, off));
+                a = __shfl_sync(0xFFFFFFFFu, a, 0);
+                const float rr = rsqrt_approx(__fadd_rn(__fmul_rn(a, 0.0078125f), eps));
+                const float2 n01 = r16x2(__fmul_rn(__fmul_rn(v[0], rr), wv[0]), __fmul_rn(__fmul_rn(v[1], rr), wv[1]));
+                const float2 n23 = r16x2(__fmul_rn(__fmul_rn(v[2], rr), wv[2]), __fmul_rn(__fmul_rn(v[3], rr), wv[3]));
+                const float n[4] = {n01.x, n01.y, n23.x, n23.y};
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {  // d = lane (+ 32): pairs (n[p], n[p + 2])
-            const int d = lane + 32 * p;
-            const float *fd = f + tok * s_tok + d * s_d;
-            const float f00 = __ldg(fd), f01 = __ldg(fd + s_j), f10 = __ldg(fd + s_i), f11 = __ldg(fd + s_i + s_j);
-            const float lo = n[p], hi = n[p + 2];
-            orow[d] = __float2bfloat16_rn(__fmaf_rn(f00, lo, __fmul_rn(f01, hi)));
-            orow[d + 64] = __float2bfloat16_rn(__fmaf_rn(f10, lo, __fmul_rn(f11, hi)));
+                for (int p = 0; p < 2; ++p) {  // d = lane (+ 32): pairs (n[p], n[p + 2]); this lane's own slots
+                    const float lo = n[p], hi = n[p + 2];
+                    rowb[lane + 32 * p] = __float2bfloat16_rn(__fmaf_rn(rot[p][0], lo, __fmul_rn(rot[p][1], hi)));
+                    rowb[lane + 32 * p + 64] = __float2bfloat16_rn(__fmaf_rn(rot[p][2], lo, __fmul_rn(rot[p][3], hi)));
+                }
+            }
+            __syncwarp();
+            uint4 *dst = reinterpret_cast<uint4 *>(out + (bt * heads + h0) * 128);
+#pragma unroll
+            for (int i = 0; i < kRopeHeads / 2; ++i)
+                if (lane + 32 * i < chunks) dst[lane + 32 * i] = reinterpret_cast<const uint4 *>(buf)[lane + 32 * i];
+            __syncwarp();
         }
     }
 }
@@ -439,7 +605,8 @@ extern "C" WF_API int wf_modulate(const void *x, const void *s1, const void *shi
 
 extern "C" WF_API int wf_ln_modulate(const void *x, const void *s1, const void *shift, void *out, int64_t rows,
                                     int64_t K, int64_t rows_per_group, float eps, wf_stream_t stream) {
-    if (rows < 0 || K <= 0 || K % 512 != 0 || K > 512 * 16 || rows_per_group <= 0) return WF_ERR_ARG;
+    if (rows < 0 || rows > INT32_MAX || K <= 0 || K % 512 != 0 || K > 512 * 16 || rows_per_group <= 0)
+        return WF_ERR_ARG;
     if (rows == 0) return WF_OK;
     if (!x || !s1 || !shift || !out || !al(x, 8) || !al(s1, 8) || !al(shift, 8) || !al(out, 8)) return WF_ERR_ARG;
     int rc = check_device();
@@ -449,18 +616,15 @@ extern "C" WF_API int wf_ln_modulate(const void *x, const void *s1, const void *
     auto S = static_cast<const __nv_bfloat16 *>(s1);
     auto H = static_cast<const __nv_bfloat16 *>(shift);
     auto O = static_cast<__nv_bfloat16 *>(out);
-    const unsigned g = static_cast<unsigned>(rows);
+#define WF_LN(NV)                                                                                    \
+    case NV: {                                                                                       \
+        const int g = persistent_grid<ln_modulate_kernel<NV>>(128, 0, rows);                         \
+        ln_modulate_kernel<NV><<<g, 128, 0, s>>>(X, S, H, O, rows, K, rows_per_group, eps);          \
+        break;                                                                                       \
+    }
     switch (K / 512) {
-        case 1: ln_modulate_kernel<1><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
-        case 2: ln_modulate_kernel<2><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
-        case 3: ln_modulate_kernel<3><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
-        case 4: ln_modulate_kernel<4><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
-        case 5: ln_modulate_kernel<5><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
-        case 6: ln_modulate_kernel<6><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
-        case 8: ln_modulate_kernel<8><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
-        case 10: ln_modulate_kernel<10><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
-        case 12: ln_modulate_kernel<12><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
-        case 16: ln_modulate_kernel<16><<<g, 128, 0, s>>>(X, S, H, O, K, rows_per_group, eps); break;
+        WF_LN(1) WF_LN(2) WF_LN(3) WF_LN(4) WF_LN(5) WF_LN(6) WF_LN(8) WF_LN(10) WF_LN(12) WF_LN(16)
+#undef WF_LN
         default: return WF_ERR_UNSUPPORTED;
     }
     return static_cast<int>(cudaGetLastError());
@@ -484,13 +648,23 @@ extern "C" WF_API int wf_rms_rope128(const void *x, const float *freqs, int64_t 
     if (batch < 0 || tokens < 0 || heads < 0 || w_dtype < WF_F16 || w_dtype > WF_F32) return WF_ERR_ARG;
     const int64_t n_rows = batch * tokens * heads;
     if (n_rows == 0) return WF_OK;
-    if (!x || !freqs || !w || !out || !al(x, 2) || !al(out, 2) || !al(freqs, 4) || !al(w, dtype_size(w_dtype)))
+    if (!x || !freqs || !w || !out || !al(x, 16) || !al(out, 16) || !al(freqs, 4) || !al(w, dtype_size(w_dtype)))
         return WF_ERR_ARG;
     int rc = check_device();
     if (rc != WF_OK) return rc;
-    rms_rope_kernel<<<grid_for(n_rows, 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __nv_bfloat16 *>(x), freqs, w, w_dtype, static_cast<__nv_bfloat16 *>(out), n_rows, heads,
-        tokens, eps, f_stride_token, f_stride_d, f_stride_i, f_stride_j);
+    const int64_t n_tok = batch * tokens;
+    const bool f4 = f_stride_j == 1 && f_stride_i == 2 && f_stride_d % 4 == 0 && f_stride_token % 4 == 0 &&
+                    al(freqs, 16);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (f4) {
+        rms_rope_kernel<true><<<persistent_grid<rms_rope_kernel<true>>(256, 0, (n_tok + 7) / 8), 256, 0, s>>>(
+            static_cast<const __nv_bfloat16 *>(x), freqs, w, w_dtype, static_cast<__nv_bfloat16 *>(out), n_tok, heads,
+            tokens, eps, f_stride_token, f_stride_d, f_stride_i, f_stride_j);
+    } else {
+        rms_rope_kernel<false><<<persistent_grid<rms_rope_kernel<false>>(256, 0, (n_tok + 7) / 8), 256, 0, s>>>(
+            static_cast<const __nv_bfloat16 *>(x), freqs, w, w_dtype, static_cast<__nv_bfloat16 *>(out), n_tok, heads,
+            tokens, eps, f_stride_token, f_stride_d, f_stride_i, f_stride_j);
+    }
     return static_cast<int>(cudaGetLastError());
 }
 
