@@ -31,7 +31,11 @@ sys.path.insert(0, REPO)
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from the ncu captures summarised in
 # profiles/ (None until captured). Keyed by workload; scaled to the bench's launch as described in the profile.
-NCU_TRAFFIC = {"sweep": None, "q8": None, "q4k": None, "w8a8": None, "prologue": None}
+NCU_TRAFFIC = {
+    # profiles/dequant_q4k_sweep.md: one-block capture (221.20 MB read + 729.71 MB written) x 36 blocks
+    "sweep": 34_232_680_000,
+    "q8": None, "q4k": None, "w8a8": None, "prologue": None,
+}
 
 Q4K_TS, Q8_TS = 144, 34
 
