@@ -22,6 +22,7 @@
 
 #include <cuda.h>
 
+#include <cstdlib>
 #include <mutex>
 
 namespace wf {
@@ -348,6 +349,224 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     }
 }
 
+// ---------------------------------------------------------------------------------------------- 2-SM kernel
+// The same GEMM with one 256 x 256 output tile per pair of CTAs (a cluster of 2 on neighbouring SMs):
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32) issued by one thread of the even CTA reads rows 0..127 of the
+// A tile and columns 0..127 of the B tile from the even CTA's shared memory and the other halves from the odd CTA's
+// (same offsets); each CTA's tensor memory holds its 128 accumulator rows x 256 columns. Per CTA a stage is 32 KB
+// (128 rows of xq + 128 rows of wq), so 6 stages fit and each SM pulls a third less from L2 than the 1-CTA kernel.
+// Each CTA's TMA loads count their bytes on the even CTA's full barrier (the .cta_group::2 form); the even CTA's
+// MMA thread signals both CTAs' empty / accumulator-ready barriers with one plain commit per CTA, and both CTAs'
+// epilogues release an accumulator on the even CTA's barrier.
+constexpr int S2 = 6;                       // stages
+constexpr int A2_STAGE = 128 * BK;          // 16 KB: this CTA's 128 rows of xq
+constexpr int B2_STAGE = 128 * BK;          // 16 KB: this CTA's 128 rows of wq
+constexpr int STAGE2 = A2_STAGE + B2_STAGE; // 32 KB
+constexpr int SMEM2_BYTES = S2 * STAGE2 + 1024 + 256 + 2 * BN * 4;
+constexpr uint32_t kIdesc2 = (2u << 4) | (1u << 7) | (1u << 10) | ((256u >> 3) << 17) | ((256u >> 4) << 24);
+constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;  // clears the CTA-rank bit of a cluster shared address
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                                 uint32_t leader_mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(leader_mbar)
+        : "memory");
+}
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(kIdesc2), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_mbar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_mbar)
+                 : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                     const float *__restrict__ xs, const float *__restrict__ ws, __nv_bfloat16 *__restrict__ y,
+                     int32_t *__restrict__ acc_out, int M, int N, int K) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + S2 * STAGE2);
+    float *ws_smem = reinterpret_cast<float *>(ring + S2 * STAGE2 + 256);
+    // bars: full[0..5] (used in the even CTA), empty[0..5], tmem_full[0..1], tmem_empty[0..1] (even CTA), drain,
+    // ws_ready[0..1]
+    __shared__ uint32_t s_tmem_base;
+    __shared__ int s_abort;
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S2), tfull0 = smem_u32(bars + 2 * S2),
+                   tempty0 = smem_u32(bars + 2 * S2 + 2), drain = smem_u32(bars + 2 * S2 + 4),
+                   wsrdy0 = smem_u32(bars + 2 * S2 + 5);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const uint32_t peer = rank ^ 1u;
+
+    const int tiles_m = (M + 255) / 256, tiles_n = (N + 255) / 256;
+    const int n_tiles = tiles_m * tiles_n;
+    const int kb_count = (K + BK - 1) / BK;
+    const int cluster_id = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int s = 0; s < S2; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull0 + 8 * b, 1);
+            mbar_init(tempty0 + 8 * b, 2 * EPI_THREADS);
+            mbar_init(wsrdy0 + 8 * b, EPI_THREADS);
+        }
+        mbar_init(drain, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 9) {  // the MMA warp of each CTA allocates (the pair's allocation: same warp, same offset)
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(&s_tmem_base)), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    cluster_sync();  // barriers initialised and tensor memory allocated in both CTAs
+    fence_after();
+    const uint32_t tmem_base = s_tmem_base;
+    volatile int *abort_flag = &s_abort;
+
+    if (warp == 8) {
+        // ------------------------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_a)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_b)) : "memory");
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = cluster_id; tile < n_tiles && ok; tile += n_clusters) {
+                const int m0 = (tile % tiles_m) * 256 + static_cast<int>(rank) * 128;
+                const int n0 = (tile / tiles_m) * 256 + static_cast<int>(rank) * 128;
+                for (int kb = 0; kb < kb_count; ++kb) {
+                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, abort_flag, 1)) { ok = false; break; }
+                    const uint32_t leader_full = (full0 + 8 * stage) & kPeerBitMask;
+                    if (rank == 0) mbar_expect_tx(full0 + 8 * stage, 2 * STAGE2);
+                    const uint32_t a_dst = smem_u32(ring + stage * STAGE2);
+                    tma_load_2d_pair(a_dst, &tma_a, kb * BK, m0, leader_full);
+                    tma_load_2d_pair(a_dst + A2_STAGE, &tma_b, kb * BK, n0, leader_full);
+                    if (++stage == S2) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok) {  // let issued copies land before this CTA can leave
+                const uint64_t t0 = global_ns();
+                while (global_ns() - t0 < 200000ull) {
+                }
+            }
+        }
+    } else if (warp == 9) {
+        // ------------------------------------------------------------------------------------ MMA issuer (even CTA)
+        if (lane == 0 && rank == 0) {
+            const uint32_t empty_peer = map_to_rank(empty0, peer), tfull_peer = map_to_rank(tfull0, peer);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int tile = cluster_id; tile < n_tiles && ok; tile += n_clusters) {
+                if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, abort_flag, 2)) { ok = false; break; }
+                fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < kb_count; ++kb) {
+                    if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, 2)) { ok = false; break; }
+                    fence_after();
+                    const uint32_t a_addr = smem_u32(ring + stage * STAGE2);
+                    const uint32_t b_addr = a_addr + A2_STAGE;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 32; ++kk)
+                        mma_i8_pair(d_tmem, smem_desc(a_addr + 32 * kk), smem_desc(b_addr + 32 * kk),
+                                    (kb | kk) != 0 ? 1u : 0u);
+                    mma_commit_pair(empty0 + 8 * stage);       // this CTA's stage is free ...
+                    mma_commit_pair(empty_peer + 8 * stage);   // ... and the other CTA's
+                    if (++stage == S2) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                mma_commit_pair(tfull0 + 8 * acc);
+                mma_commit_pair(tfull_peer + 8 * acc);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+            mma_commit_pair(drain);
+            const uint64_t t0 = global_ns();
+            while (!mbar_try(drain, 0) && global_ns() - t0 < kWaitLimitNs) {
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------------------------ epilogue (warps 0-7)
+        const int quarter = warp & 3, half = warp >> 2;
+        const uint32_t tempty_leader = map_to_rank(tempty0, 0);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = cluster_id; tile < n_tiles; tile += n_clusters) {
+            const int m0 = (tile % tiles_m) * 256 + static_cast<int>(rank) * 128, n0 = (tile / tiles_m) * 256;
+            float *ws_s = ws_smem + acc * BN;
+            {
+                const int c = static_cast<int>(threadIdx.x);
+                ws_s[c] = (n0 + c < N) ? __ldg(ws + n0 + c) : 0.f;
+            }
+            mbar_arrive(wsrdy0 + 8 * acc);
+            if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, 3)) break;
+            fence_after();
+            if (!mbar_wait(wsrdy0 + 8 * acc, acc_phase, abort_flag, 3)) break;
+            const int row = m0 + quarter * 32 + lane;
+            const bool row_ok = row < M;
+            const float xsr = row_ok ? __ldg(xs + row) : 0.f;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN + half * 128);
+            uint32_t ra[32], rb[32];
+            tmem_ld32(taddr, ra);
+            tmem_wait32(ra);
+            tmem_ld32(taddr + 32, rb);
+            if (row_ok) store_chunk(ra, ws_s, half * 128, xsr, y, acc_out, row, n0 + half * 128, N);
+            tmem_wait32(rb);
+            tmem_ld32(taddr + 64, ra);
+            if (row_ok) store_chunk(rb, ws_s, half * 128 + 32, xsr, y, acc_out, row, n0 + half * 128 + 32, N);
+            tmem_wait32(ra);
+            tmem_ld32(taddr + 96, rb);
+            if (row_ok) store_chunk(ra, ws_s, half * 128 + 64, xsr, y, acc_out, row, n0 + half * 128 + 64, N);
+            tmem_wait32(rb);
+            if (row_ok) store_chunk(rb, ws_s, half * 128 + 96, xsr, y, acc_out, row, n0 + half * 128 + 96, N);
+            fence_before();
+            mbar_arrive_cluster(tempty_leader + 8 * acc);  // the pair's accumulator may be overwritten
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    cluster_sync();  // no CTA leaves (or frees tensor memory) while the pair's MMAs may still use it
+    fence_after();
+    if (warp == 9) {
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
 // ---------------------------------------------------------------------------------------------- host
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -364,6 +583,15 @@ EncodeTiled encoder() {
             fn = reinterpret_cast<EncodeTiled>(p);
     });
     return fn;
+}
+
+// WEIGHTFERRY_W8A8_1SM=1 keeps every problem on the one-CTA kernel (the pair kernel is used for m > 128 otherwise)
+bool use_pair_kernel() {
+    static const bool pair = [] {
+        const char *v = getenv("WEIGHTFERRY_W8A8_1SM");
+        return !(v != nullptr && v[0] == '1');
+    }();
+    return pair;
 }
 
 // a [rows, K] int8 K-major matrix as a TMA map with boxes of box_rows x 128 bytes, 128-byte swizzle, zero fill
@@ -396,10 +624,42 @@ int w8a8_gemm_launch(const int8_t *xq, const int8_t *wq, const float *xs, const 
     CUtensorMap ma, mb;
     if ((rc = make_map(&ma, xq, static_cast<int>(M), static_cast<int>(K), BM)) != WF_OK) return rc;
     if ((rc = make_map(&mb, wq, static_cast<int>(N), static_cast<int>(K), BN)) != WF_OK) return rc;
-    static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (dev < 0 || dev >= 64) return WF_ERR_DEVICE;
+    if (M > BM && use_pair_kernel()) {
+        // pairs of CTAs, 256 x 256 tiles: each CTA loads 128 rows of xq and 128 rows of wq per stage
+        CUtensorMap mb2;
+        if ((rc = make_map(&mb2, wq, static_cast<int>(N), static_cast<int>(K), 128)) != WF_OK) return rc;
+        static int clusters[64] = {0};
+        if (clusters[dev] == 0) {
+            cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 SMEM2_BYTES);
+            if (e != cudaSuccess) return static_cast<int>(e);
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(2 * device_sm_count(), 1, 1);
+            cfg.blockDim = dim3(THREADS, 1, 1);
+            cfg.dynamicSmemBytes = SMEM2_BYTES;
+            cudaLaunchAttribute attr;
+            attr.id = cudaLaunchAttributeClusterDimension;
+            attr.val.clusterDim.x = 2;
+            attr.val.clusterDim.y = 1;
+            attr.val.clusterDim.z = 1;
+            cfg.attrs = &attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            e = cudaOccupancyMaxActiveClusters(&n, w8a8_gemm_2sm_kernel, &cfg);
+            if (e != cudaSuccess) return static_cast<int>(e);
+            clusters[dev] = std::max(n, 1);
+        }
+        const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+        const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, clusters[dev]));
+        w8a8_gemm_2sm_kernel<<<grid, THREADS, SMEM2_BYTES, stream>>>(ma, mb2, xs, ws, y, acc_out, static_cast<int>(M),
+                                                                    static_cast<int>(N), static_cast<int>(K));
+        return static_cast<int>(cudaGetLastError());
+    }
+    static bool attr_set[64] = {false};
+    if (!attr_set[dev]) {
         cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              SMEM_BYTES);
         if (e != cudaSuccess) return static_cast<int>(e);
