@@ -13,7 +13,9 @@
 //   warps 0..7  epilogue: warp w reads TMEM lanes 32(w%4)..+31 (one output row per thread), columns
 //               128(w/4)..+127, with tcgen05.ld (the next 32 columns in flight while the current ones are
 //               converted), y = bf16_rn((float(acc) * x_s[m]) * w_s[n]) (two float32 products, each rounded to
-//               nearest), w_s of the tile staged in shared memory, optional raw int32 copy, 16-byte stores.
+//               nearest; w_s read with warp-uniform loads). Each 32 x 32 bf16 chunk goes to a 2 KB shared-memory
+//               buffer of the warp (64-byte swizzle, two per warp) and leaves with one TMA tensor store, which
+//               also clips rows >= M and columns >= N; the optional raw int32 copy is written directly.
 // Every mbarrier wait is bounded in time (about 2 s): on expiry the CTA records an error code (read with
 // wf_w8a8_gemm_status), stops issuing work, waits (bounded) for its own copies and MMAs in flight, frees its tensor
 // memory and returns. Every TMA load here is a plain per-CTA load of this GPU's own memory.
@@ -35,7 +37,8 @@ constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
 constexpr int THREADS = 320;
 constexpr int EPI_THREADS = 256;
 constexpr int TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + 2 * BN * 4;  // ring, slack, barriers, w_s
+constexpr int OUT_BYTES = 8 * 2 * 2048;  // per epilogue warp two 32 x 32 bf16 output chunks
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 + 256;  // ring, output chunks, slack, barriers
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 // instruction descriptor of kind::i8: D int32 (bits 4-5 = 2), A and B signed int8 (bits 7-9, 10-12 = 1), both
@@ -62,6 +65,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t a) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {  // an arrive on a barrier anywhere in the cluster
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
     uint32_t ok;
@@ -153,50 +159,133 @@ __device__ __forceinline__ void tmem_wait32(uint32_t (&r)[32]) {
                  : "memory");
 }
 
-// 32 accumulators of one row -> bf16 (and the optional int32 copy); col0 is the first column, cols >= N skipped
-__device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], const float *ws_s, int cbase, float xsr,
-                                            __nv_bfloat16 *y, int32_t *acc_out, int row, int col0, int N) {
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// w_s of 32 output columns starting at col0 (a multiple of 32; N is a multiple of 8, so each group of 8 columns is
+// wholly inside or wholly outside [0, N)); same address in every lane
+struct Ws32 {
+    float4 v[8];
+};
+__device__ __forceinline__ void load_ws32(Ws32 &w, const float *__restrict__ ws, int col0, int N) {
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-        const int col = col0 + 8 * g;
-        if (col >= N) break;
-        const float4 w0 = *reinterpret_cast<const float4 *>(ws_s + cbase + 8 * g);
-        const float4 w1 = *reinterpret_cast<const float4 *>(ws_s + cbase + 8 * g + 4);
-        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        uint32_t packed[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float a0 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[8 * g + 2 * j])), xsr), wv[2 * j]);
-            const float a1 =
-                __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[8 * g + 2 * j + 1])), xsr), wv[2 * j + 1]);
-            __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
-            packed[j] = *reinterpret_cast<uint32_t *>(&h);
-        }
-        const size_t off = static_cast<size_t>(row) * N + col;
-        *reinterpret_cast<uint4 *>(y + off) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        if (acc_out != nullptr) {
-            int4 *dst = reinterpret_cast<int4 *>(acc_out + off);
-            dst[0] = make_int4(r[8 * g], r[8 * g + 1], r[8 * g + 2], r[8 * g + 3]);
-            dst[1] = make_int4(r[8 * g + 4], r[8 * g + 5], r[8 * g + 6], r[8 * g + 7]);
+        if (col0 + 8 * g < N) {
+            w.v[2 * g] = __ldg(reinterpret_cast<const float4 *>(ws + col0 + 8 * g));
+            w.v[2 * g + 1] = __ldg(reinterpret_cast<const float4 *>(ws + col0 + 8 * g + 4));
+        } else {
+            w.v[2 * g] = w.v[2 * g + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
 }
 
+// 32 accumulators of this lane's row -> bf16 in the warp's chunk buffer `buf` (32 rows x 64 bytes, 64-byte swizzle:
+// the 16-byte piece j of row r sits at piece j ^ ((r >> 1) & 3)), then one TMA store of the 32 x 32 chunk whose
+// top-left element is (row0, col0). The buffer is reused every second chunk: lane 0 first waits until the store
+// issued from it two chunks ago has read it.
+__device__ __forceinline__ void emit_chunk(const uint32_t (&r)[32], const Ws32 &w, float xsr, uint32_t buf, int lane,
+                                           const CUtensorMap *tma_y, int row0, int col0) {
+    uint32_t p[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const float4 wv = w.v[j >> 1];
+        const float w0 = (j & 1) ? wv.z : wv.x, w1 = (j & 1) ? wv.w : wv.y;
+        const float a0 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[2 * j])), xsr), w0);
+        const float a1 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[2 * j + 1])), xsr), w1);
+        __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
+        p[j] = *reinterpret_cast<uint32_t *>(&h);
+    }
+    if (lane == 0) bulk_wait_read1();
+    __syncwarp();
+    const uint32_t row_addr = buf + 64u * static_cast<uint32_t>(lane);
+    const uint32_t sw = (static_cast<uint32_t>(lane) >> 1) & 3u;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row_addr + 16u * (static_cast<uint32_t>(j) ^ sw)),
+                     "r"(p[4 * j]), "r"(p[4 * j + 1]), "r"(p[4 * j + 2]), "r"(p[4 * j + 3])
+                     : "memory");
+    fence_async_smem();  // the generic-proxy writes become visible to the TMA engine
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(tma_y, buf, col0, row0);
+        bulk_commit();
+    }
+}
+
+// the raw int32 accumulators of this lane's row (debug copy), columns >= N skipped
+__device__ __forceinline__ void store_acc_chunk(const uint32_t (&r)[32], int32_t *acc_out, int row, int col0, int N) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const int col = col0 + 8 * g;
+        if (col >= N) break;
+        int4 *dst = reinterpret_cast<int4 *>(acc_out + static_cast<size_t>(row) * N + col);
+        dst[0] = make_int4(r[8 * g], r[8 * g + 1], r[8 * g + 2], r[8 * g + 3]);
+        dst[1] = make_int4(r[8 * g + 4], r[8 * g + 5], r[8 * g + 6], r[8 * g + 7]);
+    }
+}
+
+// One epilogue warp's share of an accumulator tile: 32 rows (TMEM lanes of taddr) x 128 columns from col0, four
+// 32-column tcgen05.ld with the next one in flight while the current chunk is converted and stored. The accumulator
+// is released (tcgen05 fence, then an arrive on `release`, a cluster address when PAIR) as soon as its last
+// columns are in registers. `chunk` counts this warp's chunks and picks the buffer.
+template <bool PAIR>
+__device__ __forceinline__ void epilogue_rows(uint32_t taddr, uint32_t release, const float *__restrict__ ws,
+                                              float xsr, uint32_t out_smem, uint32_t &chunk, int lane,
+                                              const CUtensorMap *tma_y, int32_t *acc_out, int row0, int col0,
+                                              int M, int N) {
+    const int row = row0 + lane;
+    const bool dbg = acc_out != nullptr && row < M;
+    uint32_t ra[32], rb[32];
+    Ws32 w;
+    load_ws32(w, ws, col0, N);
+    tmem_ld32(taddr, ra);
+    tmem_wait32(ra);
+    tmem_ld32(taddr + 32, rb);
+    emit_chunk(ra, w, xsr, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0);
+    if (dbg) store_acc_chunk(ra, acc_out, row, col0, N);
+    load_ws32(w, ws, col0 + 32, N);
+    tmem_wait32(rb);
+    tmem_ld32(taddr + 64, ra);
+    emit_chunk(rb, w, xsr, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0 + 32);
+    if (dbg) store_acc_chunk(rb, acc_out, row, col0 + 32, N);
+    load_ws32(w, ws, col0 + 64, N);
+    tmem_wait32(ra);
+    tmem_ld32(taddr + 96, rb);
+    emit_chunk(ra, w, xsr, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0 + 64);
+    if (dbg) store_acc_chunk(ra, acc_out, row, col0 + 64, N);
+    load_ws32(w, ws, col0 + 96, N);
+    tmem_wait32(rb);
+    fence_before();
+    if (PAIR)
+        mbar_arrive_cluster(release);  // the accumulator may be overwritten
+    else
+        mbar_arrive(release);
+    emit_chunk(rb, w, xsr, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0 + 96);
+    if (dbg) store_acc_chunk(rb, acc_out, row, col0 + 96, N);
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
 w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                 const float *__restrict__ xs, const float *__restrict__ ws, __nv_bfloat16 *__restrict__ y,
-                 int32_t *__restrict__ acc_out, int M, int N, int K) {
+                 const __grid_constant__ CUtensorMap tma_y, const float *__restrict__ xs,
+                 const float *__restrict__ ws, int32_t *__restrict__ acc_out, int M, int N, int K) {
     extern __shared__ uint8_t smem_raw[];
-    // 1024-byte aligned ring (the 128-byte swizzle pattern repeats every 8 rows of 128 bytes)
+    // 1024-byte aligned ring (the 128-byte swizzle pattern repeats every 8 rows of 128 bytes), then the epilogue
+    // warps' output chunks (4 KB per warp), then the barriers
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + STAGES * STAGE_BYTES);
-    float *ws_smem = reinterpret_cast<float *>(ring + STAGES * STAGE_BYTES + 256);  // 2 x BN w_s of a tile
-    // bars: full[0..3], empty[0..3], tmem_full[0..1], tmem_empty[0..1], drain, ws_ready[0..1]
+    uint8_t *out_chunks = ring + STAGES * STAGE_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(out_chunks + OUT_BYTES);
+    // bars: full[0..3], empty[0..3], tmem_full[0..1], tmem_empty[0..1], drain
     __shared__ uint32_t s_tmem_base;
     __shared__ int s_abort;
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), tfull0 = smem_u32(bars + 2 * STAGES),
-                   tempty0 = smem_u32(bars + 2 * STAGES + 2), drain = smem_u32(bars + 2 * STAGES + 4),
-                   wsrdy0 = smem_u32(bars + 2 * STAGES + 5);
+                   tempty0 = smem_u32(bars + 2 * STAGES + 2), drain = smem_u32(bars + 2 * STAGES + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
@@ -212,7 +301,6 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull0 + 8 * b, 1);
             mbar_init(tempty0 + 8 * b, EPI_THREADS);
-            mbar_init(wsrdy0 + 8 * b, EPI_THREADS);
         }
         mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -302,43 +390,25 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     } else {
         // ------------------------------------------------------------------------------------ epilogue (warps 0-7)
         const int quarter = warp & 3, half = warp >> 2;
+        const uint32_t out_smem = smem_u32(out_chunks + warp * 4096);
+        if (threadIdx.x == 0)
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_y)) : "memory");
         int acc = 0;
-        uint32_t acc_phase = 0;
+        uint32_t acc_phase = 0, chunk = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
             const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
-            // this tile's w_s into shared memory, buffer `acc`: every epilogue thread has finished the tile that last
-            // used it (they arrived on the other buffer's barrier after it, and this thread waited there)
-            float *ws_s = ws_smem + acc * BN;
-            {
-                const int c = static_cast<int>(threadIdx.x);  // 0 .. 255
-                ws_s[c] = (n0 + c < N) ? __ldg(ws + n0 + c) : 0.f;
-            }
-            mbar_arrive(wsrdy0 + 8 * acc);
+            const int row0 = m0 + quarter * 32;
+            const float xsr = row0 + lane < M ? __ldg(xs + row0 + lane) : 0.f;
             if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, 3)) break;
             fence_after();
-            if (!mbar_wait(wsrdy0 + 8 * acc, acc_phase, abort_flag, 3)) break;
-            const int row = m0 + quarter * 32 + lane;
-            const bool row_ok = row < M;
-            const float xsr = row_ok ? __ldg(xs + row) : 0.f;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + half * 128);
-            uint32_t ra[32], rb[32];
-            tmem_ld32(taddr, ra);
-            tmem_wait32(ra);
-            tmem_ld32(taddr + 32, rb);
-            if (row_ok) store_chunk(ra, ws_s, half * 128, xsr, y, acc_out, row, n0 + half * 128, N);
-            tmem_wait32(rb);
-            tmem_ld32(taddr + 64, ra);
-            if (row_ok) store_chunk(rb, ws_s, half * 128 + 32, xsr, y, acc_out, row, n0 + half * 128 + 32, N);
-            tmem_wait32(ra);
-            tmem_ld32(taddr + 96, rb);
-            if (row_ok) store_chunk(ra, ws_s, half * 128 + 64, xsr, y, acc_out, row, n0 + half * 128 + 64, N);
-            tmem_wait32(rb);
-            if (row_ok) store_chunk(rb, ws_s, half * 128 + 96, xsr, y, acc_out, row, n0 + half * 128 + 96, N);
-            fence_before();
-            mbar_arrive(tempty0 + 8 * acc);  // this accumulator may be overwritten
+            epilogue_rows<false>(taddr, tempty0 + 8 * acc, ws, xsr, out_smem, chunk, lane, &tma_y, acc_out, row0,
+                                 n0 + half * 128, M, N);
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
+        if (lane == 0) bulk_wait_all();  // this warp's output stores have finished with its shared memory
+        __syncwarp();
     }
     fence_before();
     __syncthreads();
@@ -362,7 +432,7 @@ constexpr int S2 = 6;                       // stages
 constexpr int A2_STAGE = 128 * BK;          // 16 KB: this CTA's 128 rows of xq
 constexpr int B2_STAGE = 128 * BK;          // 16 KB: this CTA's 128 rows of wq
 constexpr int STAGE2 = A2_STAGE + B2_STAGE; // 32 KB
-constexpr int SMEM2_BYTES = S2 * STAGE2 + 1024 + 256 + 2 * BN * 4;
+constexpr int SMEM2_BYTES = S2 * STAGE2 + OUT_BYTES + 1024 + 256;
 constexpr uint32_t kIdesc2 = (2u << 4) | (1u << 7) | (1u << 10) | ((256u >> 3) << 17) | ((256u >> 4) << 24);
 constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;  // clears the CTA-rank bit of a cluster shared address
 
@@ -378,9 +448,6 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
 }
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int c0, int c1,
                                                  uint32_t leader_mbar) {
@@ -405,19 +472,17 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_mbar) {
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                     const float *__restrict__ xs, const float *__restrict__ ws, __nv_bfloat16 *__restrict__ y,
-                     int32_t *__restrict__ acc_out, int M, int N, int K) {
+                     const __grid_constant__ CUtensorMap tma_y, const float *__restrict__ xs,
+                     const float *__restrict__ ws, int32_t *__restrict__ acc_out, int M, int N, int K) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + S2 * STAGE2);
-    float *ws_smem = reinterpret_cast<float *>(ring + S2 * STAGE2 + 256);
-    // bars: full[0..5] (used in the even CTA), empty[0..5], tmem_full[0..1], tmem_empty[0..1] (even CTA), drain,
-    // ws_ready[0..1]
+    uint8_t *out_chunks = ring + S2 * STAGE2;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(out_chunks + OUT_BYTES);
+    // bars: full[0..5] (used in the even CTA), empty[0..5], tmem_full[0..1], tmem_empty[0..1] (even CTA), drain
     __shared__ uint32_t s_tmem_base;
     __shared__ int s_abort;
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S2), tfull0 = smem_u32(bars + 2 * S2),
-                   tempty0 = smem_u32(bars + 2 * S2 + 2), drain = smem_u32(bars + 2 * S2 + 4),
-                   wsrdy0 = smem_u32(bars + 2 * S2 + 5);
+                   tempty0 = smem_u32(bars + 2 * S2 + 2), drain = smem_u32(bars + 2 * S2 + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     const uint32_t peer = rank ^ 1u;
@@ -436,7 +501,6 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull0 + 8 * b, 1);
             mbar_init(tempty0 + 8 * b, 2 * EPI_THREADS);
-            mbar_init(wsrdy0 + 8 * b, EPI_THREADS);
         }
         mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -521,41 +585,26 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
         // ------------------------------------------------------------------------------------ epilogue (warps 0-7)
         const int quarter = warp & 3, half = warp >> 2;
         const uint32_t tempty_leader = map_to_rank(tempty0, 0);
+        const uint32_t out_smem = smem_u32(out_chunks + warp * 4096);
+        if (threadIdx.x == 0)
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_y)) : "memory");
         int acc = 0;
-        uint32_t acc_phase = 0;
+        uint32_t acc_phase = 0, chunk = 0;
         for (int tile = cluster_id; tile < n_tiles; tile += n_clusters) {
             const int m0 = (tile % tiles_m) * 256 + static_cast<int>(rank) * 128, n0 = (tile / tiles_m) * 256;
-            float *ws_s = ws_smem + acc * BN;
-            {
-                const int c = static_cast<int>(threadIdx.x);
-                ws_s[c] = (n0 + c < N) ? __ldg(ws + n0 + c) : 0.f;
-            }
-            mbar_arrive(wsrdy0 + 8 * acc);
+            const int row0 = m0 + quarter * 32;
+            const float xsr = row0 + lane < M ? __ldg(xs + row0 + lane) : 0.f;
             if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, 3)) break;
             fence_after();
-            if (!mbar_wait(wsrdy0 + 8 * acc, acc_phase, abort_flag, 3)) break;
-            const int row = m0 + quarter * 32 + lane;
-            const bool row_ok = row < M;
-            const float xsr = row_ok ? __ldg(xs + row) : 0.f;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + half * 128);
-            uint32_t ra[32], rb[32];
-            tmem_ld32(taddr, ra);
-            tmem_wait32(ra);
-            tmem_ld32(taddr + 32, rb);
-            if (row_ok) store_chunk(ra, ws_s, half * 128, xsr, y, acc_out, row, n0 + half * 128, N);
-            tmem_wait32(rb);
-            tmem_ld32(taddr + 64, ra);
-            if (row_ok) store_chunk(rb, ws_s, half * 128 + 32, xsr, y, acc_out, row, n0 + half * 128 + 32, N);
-            tmem_wait32(ra);
-            tmem_ld32(taddr + 96, rb);
-            if (row_ok) store_chunk(ra, ws_s, half * 128 + 64, xsr, y, acc_out, row, n0 + half * 128 + 64, N);
-            tmem_wait32(rb);
-            if (row_ok) store_chunk(rb, ws_s, half * 128 + 96, xsr, y, acc_out, row, n0 + half * 128 + 96, N);
-            fence_before();
-            mbar_arrive_cluster(tempty_leader + 8 * acc);  // the pair's accumulator may be overwritten
+            // the pair's accumulator is released on the even CTA's barrier
+            epilogue_rows<true>(taddr, tempty_leader + 8 * acc, ws, xsr, out_smem, chunk, lane, &tma_y, acc_out, row0,
+                                n0 + half * 128, M, N);
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
     }
     fence_before();
     __syncthreads();
@@ -608,21 +657,36 @@ int make_map(CUtensorMap *map, const void *base, int rows, int K, int box_rows) 
     return r == CUDA_SUCCESS ? WF_OK : WF_ERR_ARG;
 }
 
+// y [rows, N] bf16 row-major as a TMA store map with 32 x 32 boxes and 64-byte swizzle (N % 8 == 0, base 16-aligned)
+int make_out_map(CUtensorMap *map, void *base, int rows, int N) {
+    EncodeTiled enc = encoder();
+    if (enc == nullptr) return WF_ERR_DEVICE;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(N) * 2};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? WF_OK : WF_ERR_ARG;
+}
+
 }  // namespace
 
 int w8a8_gemm_launch(const int8_t *xq, const int8_t *wq, const float *xs, const float *ws, __nv_bfloat16 *y,
                      int32_t *acc_out, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
     if (M <= 0 || N <= 0 || K <= 0) return (M == 0 || N == 0) ? WF_OK : WF_ERR_ARG;
     if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return WF_ERR_ARG;
-    if (K % 16 != 0 || N % 8 != 0) return WF_ERR_ARG;  // TMA row pitch and 16-byte output stores
+    if (K % 16 != 0 || N % 8 != 0) return WF_ERR_ARG;  // TMA row pitches of xq, wq and y
     auto al = [](const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
     if (!xq || !wq || !xs || !ws || !y || !al(xq, 16) || !al(wq, 16) || !al(ws, 16) || !al(xs, 4) || !al(y, 16) ||
         (acc_out && !al(acc_out, 16)))
         return WF_ERR_ARG;
     int rc = check_device();
     if (rc != WF_OK) return rc;
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, my;
     if ((rc = make_map(&ma, xq, static_cast<int>(M), static_cast<int>(K), BM)) != WF_OK) return rc;
+    if ((rc = make_out_map(&my, y, static_cast<int>(M), static_cast<int>(N))) != WF_OK) return rc;
     if ((rc = make_map(&mb, wq, static_cast<int>(N), static_cast<int>(K), BN)) != WF_OK) return rc;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -654,7 +718,7 @@ int w8a8_gemm_launch(const int8_t *xq, const int8_t *wq, const float *xs, const 
         }
         const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
         const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, clusters[dev]));
-        w8a8_gemm_2sm_kernel<<<grid, THREADS, SMEM2_BYTES, stream>>>(ma, mb2, xs, ws, y, acc_out, static_cast<int>(M),
+        w8a8_gemm_2sm_kernel<<<grid, THREADS, SMEM2_BYTES, stream>>>(ma, mb2, my, xs, ws, acc_out, static_cast<int>(M),
                                                                     static_cast<int>(N), static_cast<int>(K));
         return static_cast<int>(cudaGetLastError());
     }
@@ -667,7 +731,7 @@ int w8a8_gemm_launch(const int8_t *xq, const int8_t *wq, const float *xs, const 
     }
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, device_sm_count()));
-    w8a8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, xs, ws, y, acc_out, static_cast<int>(M),
+    w8a8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, my, xs, ws, acc_out, static_cast<int>(M),
                                                             static_cast<int>(N), static_cast<int>(K));
     return static_cast<int>(cudaGetLastError());
 }

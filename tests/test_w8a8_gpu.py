@@ -60,6 +60,31 @@ def test_gemm_exact_accumulators(cuda, m, n, k):
     xq, wq, xs, ws = _operands(m, n, k, seed=m * 7 + n * 3 + k)
     y, acc = _gemm(xq, wq, xs, ws)
     _check(xq, wq, xs, ws, y, acc)
+    y2, _ = _gemm(xq, wq, xs, ws, with_acc=False)
+    assert torch_equal(y, y2)
+
+
+def torch_equal(a, b):
+    import torch
+    return torch.equal(a, b)
+
+
+@pytest.mark.parametrize("m,n", [(300, 520), (129, 264), (1, 8), (255, 2056)])
+def test_gemm_output_bounds(cuda, m, n):
+    """The tile stores are clipped at row m and column n: a y that ends inside a larger buffer leaves the bytes
+    after it untouched."""
+    import torch
+    ext = wf("_ext")
+    k = 64
+    xq, wq, xs, ws = _operands(m, n, k, seed=m + n)
+    buf = torch.full((m * n + 4096,), 7.0, dtype=torch.bfloat16, device="cuda")
+    y = buf[:m * n].view(m, n)
+    rc = ext.lib().wf_w8a8_gemm(xq.data_ptr(), wq.data_ptr(), xs.data_ptr(), ws.data_ptr(), y.data_ptr(), None,
+                                m, n, k, ext.stream_of(xq.device))
+    ext.check(rc, "wf_w8a8_gemm")
+    torch.cuda.synchronize()
+    assert bool((buf[m * n:] == 7.0).all()), "the GEMM wrote past the end of y"
+    _check(xq, wq, xs, ws, y, None)
 
 
 def test_gemm_extreme_values(cuda):
