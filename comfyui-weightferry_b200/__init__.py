@@ -5,11 +5,10 @@ installs the GGUF dequantisation patch and the fused Cosmos / Anima block when C
 classes are present. Outside ComfyUI (tests, benchmarks) importing it installs nothing.
 
 Modules: ``enhancers`` (gguf_dequant, fused_kernels, fused_int8, fused_block, sage_fused -- the reference's
-entry points over the CUDA kernels), ``streaming`` (slot ring with dequant-on-arrival, profiler, tensor-parallel
-block stack), ``core`` (switches, pinned host buffers), ``_ext`` (the C-ABI binding)."""
+entry points over the CUDA kernels), ``streaming`` (the ⚡ DiT Layer Streaming node ``WeightFerryDiT``, slot ring
+with dequant-on-arrival, profiler, tensor-parallel block stack), ``core`` (switches, pinned host buffers), ``_ext`` (the C-ABI binding)."""
 
-NODE_CLASS_MAPPINGS = {}
-NODE_DISPLAY_NAME_MAPPINGS = {}
+from .streaming.dit_node import NODE_CLASS_MAPPINGS, NODE_DISPLAY_NAME_MAPPINGS  # noqa: E402,F401
 
 
 def _install_at_import():

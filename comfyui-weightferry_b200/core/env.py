@@ -17,6 +17,8 @@ DEFAULTS = {
     "WEIGHTFERRY_SLOTS": None,             # GPU slots of the block-streaming ring (None: the node's option)
     "WEIGHTFERRY_PREFETCH_PRIORITY": None,  # CUDA priority of the transfer stream (lower = higher)
     "WEIGHTFERRY_PROFILE": None,           # 1: CUDA-event timeline of the streaming pipeline
+    "WEIGHTFERRY_AUTO": None,              # 1: the streaming node chooses resident blocks as with auto_config
+    "WEIGHTFERRY_AUTO_HEADROOM_MB": "1536",  # VRAM auto_config leaves for activations
     "WEIGHTFERRY_SETTINGS_FILE": None,
 }
 

@@ -1,0 +1,399 @@
+"""The ⚡ DiT Layer Streaming node over this package's slot ring with dequantisation on arrival (the reference's
+streaming/dit_node.py:38-455, WeightFerryDiT.apply_streaming).
+
+``WeightFerryDiT().apply_streaming(model, ...)`` keeps the reference's signature, option strings and return value
+``(MODEL,)``. ``model`` is a ComfyUI ModelPatcher (``clone()``, ``model.diffusion_model``, ``load_device``) or, outside
+ComfyUI, the diffusion model itself (an ``nn.Module``). On a CUDA model whose diffusion model has a block list
+(``blocks`` / ``transformer_blocks`` / ``layers`` / ``block``, the reference's streaming/common.py:125-144) it
+
+1. keeps blocks 0 .. resident_blocks-1 where they are and streams the others; ``auto_config`` picks the resident count
+   from the usable VRAM the way streaming/auto_config.py:15-85 does, and streams nothing when the model fits;
+2. captures every streamed block into one exact-size pinned host buffer (core/tiers/pinned.py) with the 256-byte
+   aligned flat layout of streaming/common.py:87-120. A GGUF weight (ComfyUI-GGUF's GGMLTensor: ``tensor_type``,
+   ``tensor_shape``) travels as its packed bytes and is dequantised on arrival, with the intermediate precision its
+   layer would use (``dequant_dtype``: None -> f16, "target" -> the compute dtype), so the slot holds the bits the
+   layer's own dequantisation gives; a GGUF weight carrying LoRA patches, or of a type or precision the kernels do not
+   take, travels packed and its layer dequantises it per use as before. The parameters are then bound to the host
+   bytes (the reference's rest binding, dit_node.py:331-339), which frees their GPU memory;
+3. builds the slot ring (streaming/state.py: ``prefetch_slots`` GPU slots, copy and dequant streams, events) and hooks
+   every streamed block: before it runs, its parameters are bound to its slot (a dequantised GGUF weight is marked as
+   a plain tensor for the block's duration: ComfyUI-GGUF's ``dequantize_tensor`` then returns it as it is); after it,
+   the slot is released, the block ``prefetch_slots`` ahead is prefetched and the rest binding comes back;
+4. brackets every forward of the diffusion model (the reference's streaming_diffusion_model_wrapper,
+   dit_node.py:414-455) with begin_forward / end_forward, starting the first transfers before the resident blocks
+   run, and captures again when something else rebound the streamed parameters (a ComfyUI model load).
+
+Options of the reference that select parts outside the quantized-weight path -- chunk streaming, the SSD tier,
+self-managed resident blocks, SageAttention, the fp8 storage host format, the RAM / VRAM budgets -- are accepted and
+logged as not used here. "Single Buffer (Synchronous)" issues each block's transfer when the block starts (no
+look-ahead)."""
+
+import torch
+
+from ..core import env as _env
+from ..core.tiers.pinned import PinnedHost, release_all
+from ..utils.logging import log_info, log_warn
+from .state import _GGUF_GEOMETRY, BlockLayout, ParamSpec, _StreamState
+
+# option values of the node (the reference's streaming/common.py:89-96 and dit_node.py:61-65): kept as they are,
+# since saved workflows carry them
+BUFFER_DOUBLE = "Double Buffer (Async Prefetch, Recommended)"
+BUFFER_SINGLE = "Single Buffer (Synchronous)"
+TIERING_RAM = "RAM (all streamed blocks pinned in RAM)"
+TIERING_AUTO = "Auto (GPU / RAM / SSD)"
+RESIDENT_MODE_COMFY = "ComfyUI (Dynamic VRAM)"
+RESIDENT_MODE_SELF = "Self-managed (fixed on GPU)"
+HOST_FORMAT_BAKED = "Compute dtype, LoRA baked (fast with LoRA)"
+HOST_FORMAT_STORAGE = "Storage dtype (fp8), LoRA on GPU (half transfer)"
+
+_BLOCK_LIST_ATTRS = ("blocks", "transformer_blocks", "layers", "block")
+_STATE_ATTR = "_weightferry_stream_state"
+_MID_CODE = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
+
+
+def _blocks(dit):
+    """The first non-empty ModuleList among the block-list attribute names, else []."""
+    for name in _BLOCK_LIST_ATTRS:
+        lst = getattr(dit, name, None)
+        if isinstance(lst, torch.nn.ModuleList) and len(lst) > 0:
+            return lst
+    return []
+
+
+def _param_owner(blk, name):
+    mod_name, _, _ = name.rpartition(".")
+    return blk.get_submodule(mod_name) if mod_name else blk
+
+
+def _raw(t):
+    """The plain tensor under a parameter (a GGMLTensor or Parameter subclass becomes a torch.Tensor view)."""
+    t = t.detach()
+    return t if type(t) is torch.Tensor else t.as_subclass(torch.Tensor)
+
+
+def _nbytes(t):
+    return t.numel() * t.element_size()
+
+
+def _gguf_mid(module, compute_dtype):
+    """The dequantisation's intermediate precision code for a layer's ``dequant_dtype``, or None when the kernels do
+    not take it (ComfyUI-GGUF: None -> f16, "target" -> the requested dtype, else a torch dtype)."""
+    dd = getattr(module, "dequant_dtype", None)
+    if dd == "target":
+        dd = compute_dtype
+    if dd is None:
+        return 0
+    return _MID_CODE.get(dd) if isinstance(dd, torch.dtype) else None
+
+
+def param_spec(name, p, module, compute_dtype):
+    """(ParamSpec, dequantised-on-arrival?) for one parameter of a streamed block."""
+    raw = _raw(p)
+    qtype = getattr(p, "tensor_type", None)
+    try:
+        qtype = None if qtype is None else int(qtype)
+    except (TypeError, ValueError):
+        qtype = None
+    if qtype in _GGUF_GEOMETRY and raw.dtype == torch.uint8 and not getattr(p, "patches", None):
+        mid = _gguf_mid(module, compute_dtype)
+        shape = tuple(int(s) for s in getattr(p, "tensor_shape", raw.shape))
+        if mid is not None:
+            try:
+                spec = ParamSpec(name, shape, qtype=qtype, mid=mid)
+            except ValueError:
+                spec = None
+            if spec is not None and spec.packed_bytes == _nbytes(raw):
+                return spec, True
+    return ParamSpec(name, tuple(raw.shape), dtype=raw.dtype), False
+
+
+def block_specs_of(blk, compute_dtype=torch.bfloat16):
+    """The streamed layout of one block: a ParamSpec per parameter (named_parameters order) and which of them are
+    dequantised on arrival."""
+    specs, deq = [], []
+    for name, p in blk.named_parameters():
+        sp, d = param_spec(name, p, _param_owner(blk, name), compute_dtype)
+        specs.append(sp)
+        deq.append(d)
+    return specs, deq
+
+
+def _same_layout(a, b):
+    return [(s.name, s.shape, s.qtype, s.dtype, s.mid) for s in a] == [(s.name, s.shape, s.qtype, s.dtype, s.mid)
+                                                                       for s in b]
+
+
+def auto_resident(num_blocks, block_bytes, slot_bytes, nonblock_bytes, usable, headroom, prefetch_slots, is_double):
+    """Resident block count for the usable VRAM (the reference's _auto_config, streaming/auto_config.py:56-77): None
+    when the whole model fits with the headroom (no streaming), else the blocks that fit beside the non-block weights,
+    the slots and the headroom, at least 1 and at most num_blocks - 1."""
+    fit_all = num_blocks * block_bytes + nonblock_bytes + headroom
+    if fit_all <= usable:
+        return None
+    slots = (max(2, int(prefetch_slots)) if is_double else 2) * slot_bytes
+    resident = int((usable - headroom - nonblock_bytes - slots) // max(1, block_bytes))
+    return max(1, min(num_blocks - 1, resident))
+
+
+class _PageableHost:
+    """A plain (pageable) host buffer with PinnedHost's interface, for pin_memory=False."""
+
+    def __init__(self, nbytes):
+        self.nbytes = int(nbytes)
+        self.tensor = torch.empty(self.nbytes, dtype=torch.uint8)
+
+    def release(self):
+        self.tensor = None
+
+
+class _NodeState:
+    """One streaming configuration of a diffusion model: the captured blocks, their rest binding and the slot ring."""
+
+    def __init__(self, owner, dit, stream_idx, device, pin_memory, num_slots, lookahead, compute_dtype):
+        self.owner = owner
+        self.dit = dit
+        self.stream_idx = list(stream_idx)
+        self.device = torch.device(device)
+        self.pin_memory = pin_memory
+        self.num_slots = num_slots
+        self.lookahead = lookahead
+        self.compute_dtype = compute_dtype
+        self.handles = []
+        self.holders = []
+        self.entries = []   # per streamed block: [(param, name, dequantised?, rest tensor, tensor_type)]
+        self.ring = None
+        self.captures = 0
+
+    # ------------------------------------------------------------------------------------------------ capture
+    def capture(self):
+        """Every streamed block into its host buffer, parameters bound to it, and a new slot ring."""
+        self.drop_ring()
+        blocks = _blocks(self.dit)
+        streamed = [blocks[i] for i in self.stream_idx]
+        specs, deq = block_specs_of(streamed[0], self.compute_dtype)
+        for i, blk in zip(self.stream_idx[1:], streamed[1:]):
+            other, _ = block_specs_of(blk, self.compute_dtype)
+            if not _same_layout(specs, other):
+                raise ValueError(f"streamed block {i} has another parameter layout than block {self.stream_idx[0]}")
+        layout = BlockLayout(specs, compute_dtype=self.compute_dtype)
+        holder_cls = PinnedHost if self.pin_memory else _PageableHost
+        flats = []
+        for blk in streamed:
+            holder = holder_cls(layout.flat_bytes)
+            flat = holder.tensor
+            entries = []
+            params = dict(blk.named_parameters())
+            for sp, d, off in zip(specs, deq, layout.offsets):
+                p = params[sp.name]
+                raw = _raw(p)
+                dst = flat[off:off + sp.packed_bytes]
+                dst.copy_(raw.reshape(-1).view(torch.uint8))
+                rest = dst.view(raw.dtype).view(raw.shape)
+                entries.append((p, sp.name, d, rest, getattr(p, "tensor_type", None)))
+            self.holders.append(holder)
+            flats.append(flat)
+            self.entries.append(entries)
+        # the rest binding: between uses the streamed parameters are the host bytes (their GPU copies are freed)
+        for entries in self.entries:
+            for p, _name, _d, rest, _tt in entries:
+                p.data = rest
+        self.ring = _StreamState(self.device, flats, layout, num_slots=self.num_slots)
+        self.ring.lookahead = self.lookahead
+        self.layout = layout
+        self.captures += 1
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+
+    def bindings_intact(self):
+        for entries in self.entries:
+            for p, _name, _d, rest, _tt in entries:
+                if p.data_ptr() != rest.data_ptr():
+                    return False
+        return bool(self.entries)
+
+    def drop_ring(self):
+        self.ring = None
+        self.entries = []
+        release_all(self.holders)
+        self.holders = []
+
+    # ------------------------------------------------------------------------------------------------ hooks
+    def install_hooks(self):
+        blocks = _blocks(self.dit)
+        for k, i in enumerate(self.stream_idx):
+            self.handles.append(blocks[i].register_forward_pre_hook(self._make_pre(k)))
+            self.handles.append(blocks[i].register_forward_hook(self._make_post(k)))
+        self.handles.append(self.dit.register_forward_pre_hook(self._dit_pre))
+        self.handles.append(self.dit.register_forward_hook(self._dit_post))
+
+    def _make_pre(self, k):
+        def pre(module, args):
+            if self.ring is None:
+                return
+            views = self.ring.acquire(k)
+            for p, name, d, _rest, _tt in self.entries[k]:
+                p.data = views[name]
+                if d:
+                    p.tensor_type = None  # a plain tensor while the block runs: used as it is
+        return pre
+
+    def _make_post(self, k):
+        def post(module, args, output):
+            if self.ring is None:
+                return
+            self.ring.release(k)
+            for p, _name, d, rest, tt in self.entries[k]:
+                p.data = rest
+                if d:
+                    p.tensor_type = tt
+        return post
+
+    def _dit_pre(self, module, args):
+        if getattr(self.dit, _STATE_ATTR, None) is not self:
+            return
+        if self.ring is None or not self.bindings_intact():
+            log_info("DiT Layer Streaming: the streamed weights were rebound; capturing them again.")
+            self.capture()
+        self.ring.begin_forward()
+        if self.lookahead:
+            self.ring.prefetch_first_slots()
+
+    def _dit_post(self, module, args, output):
+        if self.ring is not None:
+            self.ring.end_forward()
+
+    # ------------------------------------------------------------------------------------------------ teardown
+    def teardown(self):
+        """Hooks off; the streamed parameters back on the GPU as plain copies of their host bytes."""
+        for h in self.handles:
+            h.remove()
+        self.handles = []
+        for entries in self.entries:
+            for p, _name, d, rest, tt in entries:
+                p.data = rest.to(self.device)
+                if d:
+                    p.tensor_type = tt
+        self.drop_ring()
+        if getattr(self.dit, _STATE_ATTR, None) is self:
+            setattr(self.dit, _STATE_ATTR, None)
+
+
+def teardown(dit):
+    """Undo apply_streaming on a diffusion model (the reference's streaming/teardown.py for one model)."""
+    st = getattr(dit, _STATE_ATTR, None)
+    if st is not None:
+        st.teardown()
+
+
+class WeightFerryDiT:
+    """⚡ DiT Layer Streaming (low VRAM)."""
+
+    @classmethod
+    def INPUT_TYPES(cls):
+        return {
+            "required": {
+                "model": ("MODEL",),
+                "enabled": ("BOOLEAN", {"default": True}),
+                "pin_memory": ("BOOLEAN", {"default": True}),
+                "buffer_mode": ([BUFFER_DOUBLE, BUFFER_SINGLE], {"default": BUFFER_DOUBLE}),
+                "resident_blocks": ("INT", {"default": 8, "min": 0, "max": 256, "step": 1}),
+                "sage_attention": ("BOOLEAN", {"default": False}),
+                "host_format": ([HOST_FORMAT_BAKED, HOST_FORMAT_STORAGE], {"default": HOST_FORMAT_BAKED}),
+                "tiering": ([TIERING_RAM, TIERING_AUTO], {"default": TIERING_RAM}),
+                "ram_budget_gb": ("FLOAT", {"default": 0.0, "min": 0.0, "max": 512.0, "step": 0.5}),
+                "resident_mode": ([RESIDENT_MODE_COMFY, RESIDENT_MODE_SELF], {"default": RESIDENT_MODE_COMFY}),
+                "sage_pv_fp16": ("BOOLEAN", {"default": False}),
+                "auto_config": ("BOOLEAN", {"default": True}),
+                "prefetch_slots": ("INT", {"default": 3, "min": 2, "max": 6, "step": 1}),
+                "vram_budget_gb": ("FLOAT", {"default": 0.0, "min": 0.0, "max": 512.0, "step": 0.5}),
+            }
+        }
+
+    RETURN_TYPES = ("MODEL",)
+    RETURN_NAMES = ("model",)
+    FUNCTION = "apply_streaming"
+    CATEGORY = "WeightFerry/streaming"
+    TITLE = "⚡ DiT Layer Streaming (low VRAM)"
+
+    def apply_streaming(self, model, enabled: bool = True, pin_memory: bool = True, buffer_mode: str = BUFFER_DOUBLE,
+                        resident_blocks: int = 8, sage_attention: bool = False, host_format: str = HOST_FORMAT_BAKED,
+                        prefetch_slots: int = 3, resident_mode: str = RESIDENT_MODE_COMFY, tiering: str = TIERING_RAM,
+                        ram_budget_gb: float = 0.0, auto_config: bool = False, sage_pv_fp16: bool = False,
+                        vram_budget_gb: float = 0.0):
+        if not enabled:
+            log_info("DiT Layer Streaming: Disabled, passing original model.")
+            return (model,)
+        unused = [n for n, on in (("sage_attention", sage_attention), ("sage_pv_fp16", sage_pv_fp16),
+                                  ("host_format=storage", host_format == HOST_FORMAT_STORAGE),
+                                  ("resident_mode=self", resident_mode == RESIDENT_MODE_SELF),
+                                  ("tiering=auto", tiering == TIERING_AUTO), ("ram_budget_gb", ram_budget_gb > 0),
+                                  ("vram_budget_gb", vram_budget_gb > 0)) if on]
+        if unused:
+            log_info(f"DiT Layer Streaming: not used by this build: {', '.join(unused)}.")
+
+        if isinstance(model, torch.nn.Module) and not hasattr(model, "model"):
+            patcher, dit = model, model
+        else:
+            patcher = model.clone() if hasattr(model, "clone") else model
+            dit = getattr(getattr(patcher, "model", None), "diffusion_model", None)
+        if dit is None:
+            log_warn("DiT Layer Streaming: Model has no 'diffusion_model', skipping.")
+            return (model,)
+        device = getattr(patcher, "load_device", None)
+        if device is None:
+            first = next(dit.parameters(), None)
+            device = first.device if first is not None else torch.device("cpu")
+        device = torch.device(device)
+        if device.type != "cuda":
+            log_warn("DiT Layer Streaming: Device is not CUDA, skipping.")
+            return (patcher,)
+        blocks = _blocks(dit)
+        if len(blocks) == 0:
+            log_warn(f"DiT Layer Streaming: no transformer block list ({', '.join(_BLOCK_LIST_ATTRS)}) on "
+                     f"{type(dit).__name__}, skipping.")
+            return (patcher,)
+        num_blocks = len(blocks)
+        is_double = "Double Buffer" in buffer_mode
+        compute_dtype = getattr(getattr(patcher, "model", None), "manual_cast_dtype", None) or torch.bfloat16
+
+        if auto_config or _env.get("WEIGHTFERRY_AUTO") == "1":
+            auto = self._auto(dit, blocks, device, prefetch_slots, is_double, compute_dtype)
+            if auto is None:
+                log_info("DiT Layer Streaming [auto]: the whole model fits in VRAM; streaming not used.")
+                return (patcher,)
+            resident_blocks = auto
+        resident_k = max(1, min(num_blocks, int(resident_blocks)))
+        stream_idx = list(range(resident_k, num_blocks))
+        if not stream_idx:
+            log_info("DiT Layer Streaming: All blocks resident, no streaming offload registered.")
+            return (patcher,)
+
+        teardown(dit)  # an earlier configuration of this model (the reference's _teardown(dit, "re-load"))
+        num_slots = max(2, int(prefetch_slots)) if is_double else 2
+        st = _NodeState(object(), dit, stream_idx, device, pin_memory, num_slots, is_double, compute_dtype)
+        st.capture()
+        st.install_hooks()
+        setattr(dit, _STATE_ATTR, st)
+        n_deq = sum(1 for _p, _n, d, _r, _t in st.entries[0] if d)
+        log_info(f"DiT Layer Streaming: {resident_k}/{num_blocks} resident, {len(stream_idx)} streaming blocks, "
+                 f"pin_memory={pin_memory}, double_buffer={is_double}, slots={st.ring.num_slots}; per block "
+                 f"{st.layout.flat_bytes / 1024 ** 2:.1f} MB host, {n_deq} GGUF weights dequantised on arrival.")
+        return (patcher,)
+
+    @staticmethod
+    def _auto(dit, blocks, device, prefetch_slots, is_double, compute_dtype):
+        block_ids = {id(p) for blk in blocks for p in blk.parameters()}
+        block_bytes = max(sum(_nbytes(_raw(p)) for p in blk.parameters()) for blk in blocks)
+        nonblock = sum(_nbytes(_raw(p)) for p in dit.parameters() if id(p) not in block_ids)
+        specs, _ = block_specs_of(blocks[-1], compute_dtype)
+        lay = BlockLayout(specs, compute_dtype=compute_dtype)
+        free, _total = torch.cuda.mem_get_info(device)
+        stats = torch.cuda.memory_stats(device)
+        cached = stats.get("reserved_bytes.all.current", 0) - stats.get("active_bytes.all.current", 0)
+        headroom = int(_env.get("WEIGHTFERRY_AUTO_HEADROOM_MB")) * 1024 ** 2
+        return auto_resident(len(blocks), block_bytes, lay.flat_bytes + lay.weight_bytes, nonblock, free + cached,
+                             headroom, prefetch_slots, is_double)
+
+
+NODE_CLASS_MAPPINGS = {"WeightFerryDiT": WeightFerryDiT}
+NODE_DISPLAY_NAME_MAPPINGS = {"WeightFerryDiT": WeightFerryDiT.TITLE}

@@ -37,13 +37,16 @@ _DTYPE_CODE = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 
 
 class ParamSpec:
-    """One parameter of a streamed block: GGUF-quantised (qtype, logical shape) or plain (dtype, shape)."""
+    """One parameter of a streamed block: GGUF-quantised (qtype, logical shape) or plain (dtype, shape). ``mid`` is
+    the intermediate precision of the dequantisation (0 f16 -- ComfyUI-GGUF's default --, 1 bf16, 2 f32), the one
+    the layer's own dequantisation would use, so that the slot holds the same bits."""
 
-    def __init__(self, name, shape, qtype=None, dtype=None):
+    def __init__(self, name, shape, qtype=None, dtype=None, mid=0):
         self.name = name
         self.shape = tuple(int(s) for s in shape)
         self.qtype = None if qtype is None else int(qtype)
         self.dtype = dtype
+        self.mid = int(mid)
         n = 1
         for s in self.shape:
             n *= s
@@ -109,6 +112,7 @@ class _StreamState:
         self.slot_views = [self._bind_views(i) for i in range(self.num_slots)]
         self._tasks = [self._build_tasks(i) for i in range(self.num_slots)]
         self.issued = [False] * self.num_stream
+        self.lookahead = True  # False: a block's transfer is issued when it starts (single buffer), not ahead
         want_prof = profile if profile is not None else _env.get("WEIGHTFERRY_PROFILE") == "1"
         self.profiler = _StreamProfiler(self.num_stream, layout.flat_bytes) if want_prof else None
 
@@ -130,7 +134,8 @@ class _StreamState:
         return out
 
     def _build_tasks(self, slot):
-        """Per GGML type: the prebuilt wf_dequant_task table of this slot (packed bytes -> weights)."""
+        """Per (GGML type, intermediate precision): the prebuilt wf_dequant_task table of this slot (packed bytes ->
+        weights)."""
         lay = self.layout
         groups = {}
         flat_ptr = self.slot_flats[slot].data_ptr()
@@ -139,14 +144,14 @@ class _StreamState:
         for p, off in zip(lay.specs, lay.offsets):
             if p.qtype is None:
                 continue
-            groups.setdefault(p.qtype, []).append((flat_ptr + off, w_ptr + lay.w_offsets[qi], p.numel))
+            groups.setdefault((p.qtype, p.mid), []).append((flat_ptr + off, w_ptr + lay.w_offsets[qi], p.numel))
             qi += 1
         tables = []
-        for qt, items in groups.items():
+        for (qt, mid), items in groups.items():
             arr = (_ext.DequantTask * len(items))()
             for i, (s, d, n) in enumerate(items):
                 arr[i].src, arr[i].dst, arr[i].n_values = s, d, n
-            tables.append((qt, arr, len(items)))
+            tables.append((qt, mid, arr, len(items)))
         return tables
 
     def slot_of(self, s_idx):
@@ -168,8 +173,8 @@ class _StreamState:
             self.transferred_events[s_idx].record(cs)
         ds.wait_event(self.transferred_events[s_idx])
         code = _DTYPE_CODE[self.layout.compute_dtype]
-        for qt, arr, n in self._tasks[slot_idx]:
-            rc = self._lib.wf_dequant_gguf_batch(arr, n, qt, 0, code, ds.cuda_stream)
+        for qt, mid, arr, n in self._tasks[slot_idx]:
+            rc = self._lib.wf_dequant_gguf_batch(arr, n, qt, mid, code, ds.cuda_stream)
             if rc:
                 _ext.check(rc, "wf_dequant_gguf_batch")
         if prof is not None:
@@ -222,7 +227,7 @@ class _StreamState:
         slot = self.slot_of(s_idx)
         self.computed_events[slot].record(compute)
         nxt = s_idx + self.num_slots
-        if nxt < self.num_stream and not self.issued[nxt]:
+        if self.lookahead and nxt < self.num_stream and not self.issued[nxt]:
             self.issue_prefetch(nxt)
         if self.profiler is not None:
             self.profiler.add_cpu(time.perf_counter() - t0)

@@ -1,0 +1,189 @@
+"""The streaming node end to end on the GPU, in the reference's test shape (tests/test_streaming.py: the streamed
+result bit for bit equal to the un-streamed one, in several modes): a small GGUF DiT -- Q8_0 and Q4_K weights, F32
+norms and biases, one layer with dequant_dtype "target" -- built on a stand-in of ComfyUI-GGUF's ops module whose
+dequantisation is this package's patch. Un-streamed, every layer dequantises its weight per use; streamed, the node
+dequantises each block once on arrival into its slot. Both must give the same bits, across forwards, slot counts,
+buffer modes and resident counts, and teardown must hand back a working resident model."""
+
+import numpy as np
+import pytest
+
+from conftest import wf
+import fake_gguf_ops as fg
+
+pytestmark = pytest.mark.gpu
+
+DIM, HID, N_BLOCKS = 256, 1024, 5
+
+
+def _packed(qt, n_values, rng):
+    vpb, ts = (32, 34) if qt == 8 else (256, 144)
+    nb = n_values // vpb
+    raw = rng.integers(0, 256, size=(nb, ts), dtype=np.uint8)
+    if qt == 8:
+        raw[:, 0:2] = (np.abs(rng.standard_normal(nb)) * 0.002).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    else:
+        for off in (0, 2):
+            raw[:, off:off + 2] = rng.uniform(0, 0.01, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    return raw.reshape(-1)
+
+
+def _dit(torch, seed=7, plain=False):
+    rng = np.random.default_rng(seed)
+    F = torch.nn.functional
+
+    class Block(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.norm = torch.nn.Module()
+            self.norm.weight = fg.plain_param(torch.from_numpy(1 + 0.02 * rng.standard_normal(DIM)).float(), "cuda")
+            if plain:
+                self.up = torch.nn.Linear(DIM, HID, device="cuda", dtype=torch.bfloat16)
+                self.down = torch.nn.Linear(HID, DIM, device="cuda", dtype=torch.bfloat16)
+            else:
+                self.up = fg.Linear(fg.gguf_param(_packed(8, HID * DIM, rng), 8, (HID, DIM), "cuda"),
+                                    fg.plain_param(torch.from_numpy(0.01 * rng.standard_normal(HID)).float(), "cuda"))
+                self.down = fg.Linear(fg.gguf_param(_packed(12, DIM * HID, rng), 12, (DIM, HID), "cuda"),
+                                      dequant_dtype="target")
+
+        def forward(self, x):
+            h = F.layer_norm(x, (DIM,), weight=self.norm.weight.to(x.dtype))
+            return x + self.down(F.gelu(self.up(h)))
+
+    class DiT(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.blocks = torch.nn.ModuleList([Block() for _ in range(N_BLOCKS)])
+
+        def forward(self, x):
+            for b in self.blocks:
+                x = b(x)
+            return x
+
+    return DiT()
+
+
+class _Patcher:
+    """The ModelPatcher surface the node uses: clone(), model.diffusion_model, load_device."""
+
+    def __init__(self, dit, torch):
+        self.model = type("Model", (), {})()
+        self.model.diffusion_model = dit
+        self.load_device = torch.device("cuda", 0)
+        self._torch = torch
+
+    def clone(self):
+        return _Patcher(self.model.diffusion_model, self._torch)
+
+
+@pytest.fixture()
+def gguf_patch(cuda):
+    gd = wf("enhancers.gguf_dequant")
+    fg.register()
+    assert gd.install(force=True)
+    yield gd
+    gd.uninstall()
+    fg.unregister()
+
+
+def _x(torch):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    return torch.randn((2, 64, DIM), device="cuda", generator=g).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("opts", [dict(resident_blocks=1), dict(resident_blocks=1, prefetch_slots=2),
+                                  dict(resident_blocks=2, prefetch_slots=4),
+                                  dict(resident_blocks=1, buffer_mode="Single Buffer (Synchronous)"),
+                                  dict(resident_blocks=1, pin_memory=False)])
+def test_streamed_gguf_dit_is_bit_exact(gguf_patch, opts):
+    import torch
+    dn = wf("streaming.dit_node")
+    dit = _dit(torch)
+    x = _x(torch)
+    with torch.inference_mode():
+        ref = dit(x)
+        gguf_patch.stats(reset=True)
+        (patcher,) = dn.WeightFerryDiT().apply_streaming(_Patcher(dit, torch), **opts)
+        st = dit._weightferry_stream_state
+        assert st is not None and patcher.model.diffusion_model is dit
+        n_res = opts["resident_blocks"]
+        assert st.stream_idx == list(range(n_res, N_BLOCKS))
+        # rest binding: the streamed weights wait in host memory between uses
+        assert all(not p.is_cuda for i in st.stream_idx for p in dit.blocks[i].parameters())
+        assert all(p.is_cuda for i in range(n_res) for p in dit.blocks[i].parameters())
+        out1 = dit(x)
+        out2 = dit(x)
+        torch.cuda.synchronize()
+        used = gguf_patch.stats()["used"]
+    assert torch.equal(out1, ref) and torch.equal(out2, ref)
+    # only the resident blocks dequantised per use (2 GGUF weights each, 2 forwards)
+    assert used == 2 * 2 * n_res
+    assert all(not p.is_cuda for i in st.stream_idx for p in dit.blocks[i].parameters())
+    dn.teardown(dit)
+    assert dit._weightferry_stream_state is None
+    assert all(p.is_cuda for p in dit.parameters())
+    with torch.inference_mode():
+        assert torch.equal(dit(x), ref)
+
+
+def test_streamed_slot_weights_are_the_layers_dequantisation(gguf_patch):
+    """Inside a streamed block the bound weights are exactly what the layer's own dequantisation gives."""
+    import torch
+    dn = wf("streaming.dit_node")
+    gd = gguf_patch
+    dit = _dit(torch, seed=11)
+    want = {}
+    for i, blk in enumerate(dit.blocks):
+        want[i] = (gd.dequantize(blk.up.weight.data, 8, (HID, DIM), None, torch.bfloat16),
+                   gd.dequantize(blk.down.weight.data, 12, (DIM, HID), torch.bfloat16, torch.bfloat16))
+    seen = {}
+
+    def grab(i):
+        def hook(module, args):
+            seen[i] = (module.up.get_weight(module.up.weight, torch.bfloat16).clone(),
+                       module.down.get_weight(module.down.weight, torch.bfloat16).clone())
+        return hook
+
+    dn.WeightFerryDiT().apply_streaming(_Patcher(dit, torch), resident_blocks=1, prefetch_slots=2)
+    hs = [dit.blocks[i].register_forward_pre_hook(grab(i)) for i in range(N_BLOCKS)]  # after the node's hooks
+    with torch.inference_mode():
+        dit(_x(torch))
+    torch.cuda.synchronize()
+    for h in hs:
+        h.remove()
+    for i in range(N_BLOCKS):
+        assert torch.equal(seen[i][0], want[i][0]) and torch.equal(seen[i][1], want[i][1]), i
+    dn.teardown(dit)
+
+
+def test_rebinding_triggers_a_new_capture(gguf_patch):
+    """Weights moved by someone else (a model load) are captured again at the next forward."""
+    import torch
+    dn = wf("streaming.dit_node")
+    dit = _dit(torch, seed=5)
+    x = _x(torch)
+    with torch.inference_mode():
+        ref = dit(x)
+        dn.WeightFerryDiT().apply_streaming(_Patcher(dit, torch), resident_blocks=1)
+        st = dit._weightferry_stream_state
+        for p in dit.blocks[3].parameters():
+            p.data = p.data.to("cuda")
+        out = dit(x)
+    torch.cuda.synchronize()
+    assert st.captures == 2 and torch.equal(out, ref)
+    dn.teardown(dit)
+
+
+def test_streamed_plain_bf16_dit(cuda):
+    """A model without GGUF weights streams its bf16 parameters as they are."""
+    import torch
+    dn = wf("streaming.dit_node")
+    dit = _dit(torch, seed=9, plain=True)
+    x = _x(torch)
+    with torch.inference_mode():
+        ref = dit(x)
+        dn.WeightFerryDiT().apply_streaming(dit, resident_blocks=2, prefetch_slots=2)
+        out = dit(x)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    dn.teardown(dit)
