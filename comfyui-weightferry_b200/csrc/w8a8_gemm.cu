@@ -16,6 +16,11 @@
 //               nearest; w_s read with warp-uniform loads). Each 32 x 32 bf16 chunk goes to a 2 KB shared-memory
 //               buffer of the warp (64-byte swizzle, two per warp) and leaves with one TMA tensor store, which
 //               also clips rows >= M and columns >= N; the optional raw int32 copy is written directly.
+// The residual variant (wf_w8a8_gemm_residual) adds the block's gated residual in the same epilogue:
+// out = bf16_rn(float(x[m, n]) + float(gate[m / rows_per_group, n]) * float(y)) with y the bf16 value above (one
+// float32 product and one float32 sum, each rounded to nearest) -- the bits of the GEMM followed by PyTorch's bf16
+// addcmul(x, gate, y). Each lane bulk-prefetches its row's residual span into L2 while the tile's MMAs run; residual
+// and gate then come in with plain 16-byte loads, one 32-column chunk ahead of its TMEM read. out may be x.
 // Every mbarrier wait is bounded in time (about 2 s): on expiry the CTA records an error code (read with
 // wf_w8a8_gemm_status), stops issuing work, waits (bounded) for its own copies and MMAs in flight, frees its tensor
 // memory and returns. Every TMA load here is a plain per-CTA load of this GPU's own memory.
@@ -186,12 +191,51 @@ __device__ __forceinline__ void load_ws32(Ws32 &w, const float *__restrict__ ws,
     }
 }
 
+// the block's residual operand of the residual epilogue (resid == nullptr: the plain GEMM)
+struct ResidualArgs {
+    const __nv_bfloat16 *resid;  // [M, N] row-major
+    const __nv_bfloat16 *gate;   // [ceil(M / rows_per_group), N] row-major
+    int rows_per_group;
+};
+
+// 32 residual and gate values of this lane's row (row < M) at columns col0 .. col0 + 31 (16-byte groups past N are 0)
+struct Res32 {
+    uint4 r[4], g[4];
+};
+__device__ __forceinline__ void load_res32(Res32 &v, const ResidualArgs &res, int row, int col0, int M, int N) {
+    const size_t rbase = static_cast<size_t>(row) * N, gbase = static_cast<size_t>(row / res.rows_per_group) * N;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int col = col0 + 8 * q;
+        if (row < M && col < N) {
+            v.r[q] = __ldg(reinterpret_cast<const uint4 *>(res.resid + rbase + col));
+            v.g[q] = __ldg(reinterpret_cast<const uint4 *>(res.gate + gbase + col));
+        } else {
+            v.r[q] = v.g[q] = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+}
+
+// bf16x2 -> two floats (exact)
+__device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
+
+// this lane's residual span of a tile (128 columns from col0, clipped at N) into L2 ahead of its use
+__device__ __forceinline__ void prefetch_res_l2(const ResidualArgs &res, int row, int col0, int M, int N) {
+    if (row >= M || col0 >= N) return;
+    const uint32_t bytes = static_cast<uint32_t>(min(128, N - col0)) * 2u;  // a multiple of 16 (N % 8 == 0)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(res.resid + static_cast<size_t>(row) * N + col0),
+                 "r"(bytes)
+                 : "memory");
+}
+
 // 32 accumulators of this lane's row -> bf16 in the warp's chunk buffer `buf` (32 rows x 64 bytes, 64-byte swizzle:
 // the 16-byte piece j of row r sits at piece j ^ ((r >> 1) & 3)), then one TMA store of the 32 x 32 chunk whose
 // top-left element is (row0, col0). The buffer is reused every second chunk: lane 0 first waits until the store
 // issued from it two chunks ago has read it.
-__device__ __forceinline__ void emit_chunk(const uint32_t (&r)[32], const Ws32 &w, float xsr, uint32_t buf, int lane,
-                                           const CUtensorMap *tma_y, int row0, int col0) {
+template <bool RES>
+__device__ __forceinline__ void emit_chunk(const uint32_t (&r)[32], const Ws32 &w, float xsr, const Res32 &rv,
+                                           uint32_t buf, int lane, const CUtensorMap *tma_y, int row0, int col0) {
     uint32_t p[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -200,7 +244,17 @@ __device__ __forceinline__ void emit_chunk(const uint32_t (&r)[32], const Ws32 &
         const float a0 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[2 * j])), xsr), w0);
         const float a1 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[2 * j + 1])), xsr), w1);
         __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
-        p[j] = *reinterpret_cast<uint32_t *>(&h);
+        uint32_t y2 = *reinterpret_cast<uint32_t *>(&h);
+        if (RES) {
+            const uint4 rq = rv.r[j >> 2], gq = rv.g[j >> 2];
+            const uint32_t rw = (j & 3) == 0 ? rq.x : (j & 3) == 1 ? rq.y : (j & 3) == 2 ? rq.z : rq.w;
+            const uint32_t gw = (j & 3) == 0 ? gq.x : (j & 3) == 1 ? gq.y : (j & 3) == 2 ? gq.z : gq.w;
+            const float o0 = __fadd_rn(bf_lo(rw), __fmul_rn(bf_lo(gw), bf_lo(y2)));
+            const float o1 = __fadd_rn(bf_hi(rw), __fmul_rn(bf_hi(gw), bf_hi(y2)));
+            __nv_bfloat162 o = __floats2bfloat162_rn(o0, o1);
+            y2 = *reinterpret_cast<uint32_t *>(&o);
+        }
+        p[j] = y2;
     }
     if (lane == 0) bulk_wait_read1();
     __syncwarp();
@@ -235,46 +289,53 @@ __device__ __forceinline__ void store_acc_chunk(const uint32_t (&r)[32], int32_t
 // 32-column tcgen05.ld with the next one in flight while the current chunk is converted and stored. The accumulator
 // is released (tcgen05 fence, then an arrive on `release`, a cluster address when PAIR) as soon as its last
 // columns are in registers. `chunk` counts this warp's chunks and picks the buffer.
-template <bool PAIR>
+template <bool PAIR, bool RES>
 __device__ __forceinline__ void epilogue_rows(uint32_t taddr, uint32_t release, const float *__restrict__ ws,
                                               float xsr, uint32_t out_smem, uint32_t &chunk, int lane,
-                                              const CUtensorMap *tma_y, int32_t *acc_out, int row0, int col0,
-                                              int M, int N) {
+                                              const CUtensorMap *tma_y, int32_t *acc_out, const ResidualArgs &res,
+                                              int row0, int col0, int M, int N) {
     const int row = row0 + lane;
     const bool dbg = acc_out != nullptr && row < M;
     uint32_t ra[32], rb[32];
     Ws32 w;
+    Res32 rv;
     load_ws32(w, ws, col0, N);
+    if (RES) load_res32(rv, res, row, col0, M, N);
     tmem_ld32(taddr, ra);
     tmem_wait32(ra);
     tmem_ld32(taddr + 32, rb);
-    emit_chunk(ra, w, xsr, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0);
+    emit_chunk<RES>(ra, w, xsr, rv, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0);
     if (dbg) store_acc_chunk(ra, acc_out, row, col0, N);
     load_ws32(w, ws, col0 + 32, N);
+    if (RES) load_res32(rv, res, row, col0 + 32, M, N);
     tmem_wait32(rb);
     tmem_ld32(taddr + 64, ra);
-    emit_chunk(rb, w, xsr, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0 + 32);
+    emit_chunk<RES>(rb, w, xsr, rv, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0 + 32);
     if (dbg) store_acc_chunk(rb, acc_out, row, col0 + 32, N);
     load_ws32(w, ws, col0 + 64, N);
+    if (RES) load_res32(rv, res, row, col0 + 64, M, N);
     tmem_wait32(ra);
     tmem_ld32(taddr + 96, rb);
-    emit_chunk(ra, w, xsr, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0 + 64);
+    emit_chunk<RES>(ra, w, xsr, rv, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0 + 64);
     if (dbg) store_acc_chunk(ra, acc_out, row, col0 + 64, N);
     load_ws32(w, ws, col0 + 96, N);
+    if (RES) load_res32(rv, res, row, col0 + 96, M, N);
     tmem_wait32(rb);
     fence_before();
     if (PAIR)
         mbar_arrive_cluster(release);  // the accumulator may be overwritten
     else
         mbar_arrive(release);
-    emit_chunk(rb, w, xsr, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0 + 96);
+    emit_chunk<RES>(rb, w, xsr, rv, out_smem + 2048u * (chunk++ & 1u), lane, tma_y, row0, col0 + 96);
     if (dbg) store_acc_chunk(rb, acc_out, row, col0 + 96, N);
 }
 
+template <bool RES>
 __global__ void __launch_bounds__(THREADS, 1)
 w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                  const __grid_constant__ CUtensorMap tma_y, const float *__restrict__ xs,
-                 const float *__restrict__ ws, int32_t *__restrict__ acc_out, int M, int N, int K) {
+                 const float *__restrict__ ws, int32_t *__restrict__ acc_out, ResidualArgs res, int M, int N,
+                 int K) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned ring (the 128-byte swizzle pattern repeats every 8 rows of 128 bytes), then the epilogue
     // warps' output chunks (4 KB per warp), then the barriers
@@ -399,12 +460,13 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
             const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
             const int row0 = m0 + quarter * 32;
             const float xsr = row0 + lane < M ? __ldg(xs + row0 + lane) : 0.f;
+            if (RES) prefetch_res_l2(res, row0 + lane, n0 + half * 128, M, N);
             if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, 3)) break;
             fence_after();
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + half * 128);
-            epilogue_rows<false>(taddr, tempty0 + 8 * acc, ws, xsr, out_smem, chunk, lane, &tma_y, acc_out, row0,
-                                 n0 + half * 128, M, N);
+            epilogue_rows<false, RES>(taddr, tempty0 + 8 * acc, ws, xsr, out_smem, chunk, lane, &tma_y, acc_out, res,
+                                      row0, n0 + half * 128, M, N);
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
         if (lane == 0) bulk_wait_all();  // this warp's output stores have finished with its shared memory
@@ -470,10 +532,12 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_mbar) {
                  : "memory");
 }
 
+template <bool RES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_y, const float *__restrict__ xs,
-                     const float *__restrict__ ws, int32_t *__restrict__ acc_out, int M, int N, int K) {
+                     const float *__restrict__ ws, int32_t *__restrict__ acc_out, ResidualArgs res, int M, int N,
+                     int K) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *out_chunks = ring + S2 * STAGE2;
@@ -594,13 +658,14 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
             const int m0 = (tile % tiles_m) * 256 + static_cast<int>(rank) * 128, n0 = (tile / tiles_m) * 256;
             const int row0 = m0 + quarter * 32;
             const float xsr = row0 + lane < M ? __ldg(xs + row0 + lane) : 0.f;
+            if (RES) prefetch_res_l2(res, row0 + lane, n0 + half * 128, M, N);
             if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, 3)) break;
             fence_after();
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + half * 128);
             // the pair's accumulator is released on the even CTA's barrier
-            epilogue_rows<true>(taddr, tempty_leader + 8 * acc, ws, xsr, out_smem, chunk, lane, &tma_y, acc_out, row0,
-                                n0 + half * 128, M, N);
+            epilogue_rows<true, RES>(taddr, tempty_leader + 8 * acc, ws, xsr, out_smem, chunk, lane, &tma_y, acc_out,
+                                     res, row0, n0 + half * 128, M, N);
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
         if (lane == 0) bulk_wait_all();
@@ -671,34 +736,19 @@ int make_out_map(CUtensorMap *map, void *base, int rows, int N) {
     return r == CUDA_SUCCESS ? WF_OK : WF_ERR_ARG;
 }
 
-}  // namespace
-
-int w8a8_gemm_launch(const int8_t *xq, const int8_t *wq, const float *xs, const float *ws, __nv_bfloat16 *y,
-                     int32_t *acc_out, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
-    if (M <= 0 || N <= 0 || K <= 0) return (M == 0 || N == 0) ? WF_OK : WF_ERR_ARG;
-    if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return WF_ERR_ARG;
-    if (K % 16 != 0 || N % 8 != 0) return WF_ERR_ARG;  // TMA row pitches of xq, wq and y
-    auto al = [](const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
-    if (!xq || !wq || !xs || !ws || !y || !al(xq, 16) || !al(wq, 16) || !al(ws, 16) || !al(xs, 4) || !al(y, 16) ||
-        (acc_out && !al(acc_out, 16)))
-        return WF_ERR_ARG;
-    int rc = check_device();
-    if (rc != WF_OK) return rc;
-    CUtensorMap ma, mb, my;
-    if ((rc = make_map(&ma, xq, static_cast<int>(M), static_cast<int>(K), BM)) != WF_OK) return rc;
-    if ((rc = make_out_map(&my, y, static_cast<int>(M), static_cast<int>(N))) != WF_OK) return rc;
-    if ((rc = make_map(&mb, wq, static_cast<int>(N), static_cast<int>(K), BN)) != WF_OK) return rc;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return WF_ERR_DEVICE;
+// one launch of the pair kernel (m > 128) or the one-CTA kernel, with or without the residual epilogue
+template <bool RES>
+int launch(const CUtensorMap &ma, const void *wq, const CUtensorMap &my, const float *xs, const float *ws,
+           int32_t *acc_out, const ResidualArgs &res, int64_t M, int64_t N, int64_t K, int dev, cudaStream_t stream) {
+    int rc;
     if (M > BM && use_pair_kernel()) {
         // pairs of CTAs, 256 x 256 tiles: each CTA loads 128 rows of xq and 128 rows of wq per stage
         CUtensorMap mb2;
         if ((rc = make_map(&mb2, wq, static_cast<int>(N), static_cast<int>(K), 128)) != WF_OK) return rc;
         static int clusters[64] = {0};
         if (clusters[dev] == 0) {
-            cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 SMEM2_BYTES);
+            cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_2sm_kernel<RES>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
             if (e != cudaSuccess) return static_cast<int>(e);
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(2 * device_sm_count(), 1, 1);
@@ -712,28 +762,58 @@ int w8a8_gemm_launch(const int8_t *xq, const int8_t *wq, const float *xs, const 
             cfg.attrs = &attr;
             cfg.numAttrs = 1;
             int n = 0;
-            e = cudaOccupancyMaxActiveClusters(&n, w8a8_gemm_2sm_kernel, &cfg);
+            e = cudaOccupancyMaxActiveClusters(&n, w8a8_gemm_2sm_kernel<RES>, &cfg);
             if (e != cudaSuccess) return static_cast<int>(e);
             clusters[dev] = std::max(n, 1);
         }
         const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
         const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, clusters[dev]));
-        w8a8_gemm_2sm_kernel<<<grid, THREADS, SMEM2_BYTES, stream>>>(ma, mb2, my, xs, ws, acc_out, static_cast<int>(M),
-                                                                    static_cast<int>(N), static_cast<int>(K));
+        w8a8_gemm_2sm_kernel<RES><<<grid, THREADS, SMEM2_BYTES, stream>>>(
+            ma, mb2, my, xs, ws, acc_out, res, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
         return static_cast<int>(cudaGetLastError());
     }
+    CUtensorMap mb;
+    if ((rc = make_map(&mb, wq, static_cast<int>(N), static_cast<int>(K), BN)) != WF_OK) return rc;
     static bool attr_set[64] = {false};
     if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel<RES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              SMEM_BYTES);
         if (e != cudaSuccess) return static_cast<int>(e);
         attr_set[dev] = true;
     }
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, device_sm_count()));
-    w8a8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, my, xs, ws, acc_out, static_cast<int>(M),
-                                                            static_cast<int>(N), static_cast<int>(K));
+    w8a8_gemm_kernel<RES><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, my, xs, ws, acc_out, res, static_cast<int>(M),
+                                                                 static_cast<int>(N), static_cast<int>(K));
     return static_cast<int>(cudaGetLastError());
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+}  // namespace
+
+int w8a8_gemm_launch(const int8_t *xq, const int8_t *wq, const float *xs, const float *ws, __nv_bfloat16 *y,
+                     int32_t *acc_out, const __nv_bfloat16 *resid, const __nv_bfloat16 *gate, int64_t rows_per_group,
+                     int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0) return (M == 0 || N == 0) ? WF_OK : WF_ERR_ARG;
+    if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return WF_ERR_ARG;
+    if (K % 16 != 0 || N % 8 != 0) return WF_ERR_ARG;  // TMA row pitches of xq, wq and y
+    if (!xq || !wq || !xs || !ws || !y || !aligned(xq, 16) || !aligned(wq, 16) || !aligned(ws, 16) ||
+        !aligned(xs, 4) || !aligned(y, 16) || (acc_out && !aligned(acc_out, 16)))
+        return WF_ERR_ARG;
+    const bool res_on = resid != nullptr;
+    if (res_on && (!gate || !aligned(resid, 16) || !aligned(gate, 16) || rows_per_group <= 0)) return WF_ERR_ARG;
+    int rc = check_device();
+    if (rc != WF_OK) return rc;
+    CUtensorMap ma, my;
+    if ((rc = make_map(&ma, xq, static_cast<int>(M), static_cast<int>(K), BM)) != WF_OK) return rc;
+    if ((rc = make_out_map(&my, y, static_cast<int>(M), static_cast<int>(N))) != WF_OK) return rc;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return WF_ERR_DEVICE;
+    ResidualArgs res{resid, gate, static_cast<int>(std::min<int64_t>(rows_per_group, 1 << 30))};
+    return res_on ? launch<true>(ma, wq, my, xs, ws, acc_out, res, M, N, K, dev, stream)
+                  : launch<false>(ma, wq, my, xs, ws, acc_out, res, M, N, K, dev, stream);
 }
 
 int w8a8_gemm_status(int *status) {
@@ -752,8 +832,17 @@ int w8a8_gemm_status(int *status) {
 
 extern "C" WF_API int wf_w8a8_gemm(const int8_t *xq, const int8_t *wq, const float *xs, const float *ws, void *y,
                                   int32_t *acc_dbg, int64_t m, int64_t n, int64_t k, wf_stream_t stream) {
-    return wf::w8a8_gemm_launch(xq, wq, xs, ws, static_cast<__nv_bfloat16 *>(y), acc_dbg, m, n, k,
-                                reinterpret_cast<cudaStream_t>(stream));
+    return wf::w8a8_gemm_launch(xq, wq, xs, ws, static_cast<__nv_bfloat16 *>(y), acc_dbg, nullptr, nullptr, 1, m, n,
+                                k, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" WF_API int wf_w8a8_gemm_residual(const int8_t *xq, const int8_t *wq, const float *xs, const float *ws,
+                                           const void *resid, const void *gate, int64_t rows_per_group, void *out,
+                                           int64_t m, int64_t n, int64_t k, wf_stream_t stream) {
+    if (resid == nullptr) return WF_ERR_ARG;
+    return wf::w8a8_gemm_launch(xq, wq, xs, ws, static_cast<__nv_bfloat16 *>(out), nullptr,
+                                static_cast<const __nv_bfloat16 *>(resid), static_cast<const __nv_bfloat16 *>(gate),
+                                rows_per_group, m, n, k, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" WF_API int wf_w8a8_gemm_status(int *status) {

@@ -203,17 +203,51 @@ def _int8_linear_shared(x, weight, bias):
     return out if x.dim() == 2 else out.reshape(*x.shape[:-1], q["n"])
 
 
-def _int8_linear_residual(x, weight, bias, res):
-    """x_res + gate * linear(x) for the block's residual x_res (B, T, H, W, D) / (B, N, D) and gate (B, T, 1, 1, D) /
-    (B, 1, D) (reference :212-268): the GEMM, then the residual as PyTorch's addcmul in bf16 (the reference fuses it
-    into kitchen's epilogue with the same bits). None when not possible."""
-    xr, gate = res["x"], res["gate"]
-    out = _int8_linear_shared(x, weight, bias)
+def gemm_residual(x_q, w_q, x_s, ws, resid, gate, rows_per_group, out=None):
+    """out = bf16(resid + gate[row // rows_per_group] * bf16((float(x_q @ w_q^T) * x_s) * ws)) in one launch: the
+    GEMM's epilogue adds the gated residual (the bits of gemm() followed by torch.addcmul in bf16). resid / out
+    [m, n] bf16, gate [groups, n] bf16, all contiguous; out may be resid."""
+    m, k = x_q.shape
+    n = w_q.shape[0]
     if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x_q.device)
+    with torch.cuda.device(x_q.device):
+        rc = _ext.lib().wf_w8a8_gemm_residual(x_q.data_ptr(), w_q.data_ptr(), x_s.data_ptr(), ws.data_ptr(),
+                                              resid.data_ptr(), gate.data_ptr(), int(rows_per_group), out.data_ptr(),
+                                              m, n, k, _ext.stream_of(x_q.device))
+    _ext.check(rc, "wf_w8a8_gemm_residual")
+    return out
+
+
+def _int8_linear_residual(x, weight, bias, res):
+    """x_res + gate * linear(x) for the block's residual x_res (B, T, H, W, D) and gate (B, T, 1, 1, D), or x_res
+    (B, N, D) and gate (B, 1, D) (reference :212-268): one GEMM whose epilogue adds the gated residual, over all the
+    (batch, frame) groups at once (each row takes its group's gate row; the reference launches once per group, or once
+    for all rows when the gates are equal). None when not possible (the caller runs the plain linear and the block
+    its addcmul)."""
+    xr, gate = res["x"], res["gate"]
+    q = _int8_quantised(x, weight, bias)
+    if q is None:
         return None
-    if out.shape[-1] != xr.shape[-1] or xr.dtype != out.dtype:
+    m, n = q["m"], q["n"]
+    D = xr.shape[-1]
+    if xr.dim() == 5:
+        B, T, H, W, _ = xr.shape
+        if not xr.is_contiguous() or tuple(gate.shape) != (B, T, 1, 1, D):
+            return None
+        groups, rows = B * T, H * W
+    elif xr.dim() == 3:
+        groups, rows, _ = xr.shape
+        if not xr.is_contiguous() or tuple(gate.shape) != (groups, 1, D):
+            return None
+    else:
         return None
-    return torch.addcmul(xr, gate, out.view(xr.shape))
+    if n != D or m != groups * rows or xr.dtype != q["dtype"] or gate.dtype != q["dtype"] or not xr.is_cuda:
+        return None
+    g2 = gate.reshape(groups, D).contiguous()
+    out = torch.empty_like(xr)
+    gemm_residual(q["x_q"], q["w_q"], q["x_s"], q["ws"], xr.view(m, D), g2, rows, out=out.view(m, D))
+    return out if x.dim() == 2 else out.view(*q["shape"][:-1], n)
 
 
 def _pending_for(input):

@@ -131,6 +131,18 @@ WF_API int wf_quant_rows(const void *x, const void *s1, const void *shift, const
 WF_API int wf_w8a8_gemm(const int8_t *xq, const int8_t *wq, const float *xs, const float *ws, void *y,
                         int32_t *acc_dbg, int64_t m, int64_t n, int64_t k, wf_stream_t stream);
 
+/* The W8A8 linear with the block's gated residual in its epilogue:
+ *   out[r, c] = bf16_rn(float(resid[r, c]) + float(gate[r / rows_per_group, c]) * float(y[r, c]))
+ * with y[r, c] the bf16 value wf_w8a8_gemm computes (one float32 product, one float32 sum, each rounded to nearest:
+ * the bits of wf_w8a8_gemm followed by PyTorch's bf16 addcmul(resid, gate, y)). resid and out [m, n] bf16 and gate
+ * [ceil(m / rows_per_group), n] bf16, all row-major and 16-byte aligned; rows_per_group >= 1 (the rows of one
+ * (batch, frame) group; m or more: one gate row for all rows). out may be resid (in place). Operand rules otherwise
+ * as wf_w8a8_gemm. Replaces comfy_kitchen's cutlass_int8_dequant_residual as the reference calls it, once per
+ * group or once for all rows when the gates are equal (enhancers/fused_int8.py:212-268). */
+WF_API int wf_w8a8_gemm_residual(const int8_t *xq, const int8_t *wq, const float *xs, const float *ws,
+                                 const void *resid, const void *gate, int64_t rows_per_group, void *out, int64_t m,
+                                 int64_t n, int64_t k, wf_stream_t stream);
+
 /* Status word of the GEMM kernel: 0, or the code of a pipeline wait that ran out of time (the kernel then stopped
  * early and its output is incomplete). Reading it synchronises the device and clears it. No reference counterpart
  * (the reference's GEMM is a closed library call); it is this library's failure report. */

@@ -159,3 +159,78 @@ def test_int8_linear_entry_points(cuda):
     finally:
         fs._tls.qkv = None
         fi._clear_pre()
+
+
+def _gemm_residual(xq, wq, xs, ws, resid, gate, rpg, out):
+    ext = wf("_ext")
+    m, k = xq.shape
+    n = wq.shape[0]
+    rc = ext.lib().wf_w8a8_gemm_residual(xq.data_ptr(), wq.data_ptr(), xs.data_ptr(), ws.data_ptr(),
+                                         resid.data_ptr(), gate.data_ptr(), rpg, out.data_ptr(), m, n, k,
+                                         ext.stream_of(xq.device))
+    ext.check(rc, "wf_w8a8_gemm_residual")
+    return out
+
+
+@pytest.mark.parametrize("m,n,k,rpg", [(300, 520, 272, 100), (1024, 2048, 2048, 256), (64, 512, 256, 64),
+                                       (257, 264, 64, 1000), (2048, 512, 4096, 7)])
+def test_gemm_residual_equals_gemm_then_addcmul(cuda, m, n, k, rpg):
+    """The residual epilogue gives exactly the plain GEMM followed by PyTorch's bf16 addcmul with each row's gate row,
+    also written in place over the residual."""
+    import torch
+    xq, wq, xs, ws = _operands(m, n, k, seed=m + 3 * n + k)
+    g = torch.Generator(device="cuda").manual_seed(m * n)
+    resid = torch.randn((m, n), device="cuda", generator=g).to(torch.bfloat16)
+    groups = (m + rpg - 1) // rpg
+    gate = (torch.randn((groups, n), device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    y, _ = _gemm(xq, wq, xs, ws, with_acc=False)
+    rows_gate = gate[torch.arange(m, device="cuda") // rpg]
+    want = torch.addcmul(resid, rows_gate, y)
+    assert torch.equal(want, (resid.float() + rows_gate.float() * y.float()).to(torch.bfloat16))
+    out = _gemm_residual(xq, wq, xs, ws, resid, gate, rpg, torch.empty_like(resid))
+    inplace = resid.clone()
+    _gemm_residual(xq, wq, xs, ws, inplace, gate, rpg, inplace)
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    assert torch.equal(inplace, want)
+
+
+def test_gemm_residual_rejections(cuda):
+    import torch
+    ext = wf("_ext")
+    t = torch.zeros(1 << 16, dtype=torch.int8, device="cuda")
+    p = t.data_ptr()
+    st = ext.stream_of(t.device)
+    L = ext.lib()
+    assert L.wf_w8a8_gemm_residual(p, p, p, p, None, p, 1, p, 16, 16, 32, st) == -1      # no residual
+    assert L.wf_w8a8_gemm_residual(p, p, p, p, p, None, 1, p, 16, 16, 32, st) == -1      # no gate
+    assert L.wf_w8a8_gemm_residual(p, p, p, p, p, p, 0, p, 16, 16, 32, st) == -1         # rows_per_group
+    assert L.wf_w8a8_gemm_residual(p, p, p, p, p + 2, p, 1, p, 16, 16, 32, st) == -1     # resid alignment
+    assert L.wf_w8a8_gemm_residual(p, p, p, p, p, p + 8, 1, p, 16, 16, 32, st) == -1     # gate alignment
+
+
+@pytest.mark.parametrize("five_d", [True, False])
+def test_int8_linear_residual_entry_point(cuda, five_d):
+    """_int8_linear_residual (the reference's residual sub-layer output) equals the plain int8 linear followed by the
+    block's addcmul, for the block's (B, T, H, W, D) layout and the row layout (B, N, D)."""
+    import torch
+    fi = wf("enhancers.fused_int8")
+    fs = wf("enhancers.fused_state")
+    g = torch.Generator(device="cuda").manual_seed(21)
+    B, T, H, W, D, k = 2, 2, 8, 16, 512, 768
+    x = torch.randn((B, T, H, W, k) if five_d else (B, T * H * W, k), device="cuda", generator=g).to(torch.bfloat16)
+    wq = torch.randint(-127, 128, (D, k), dtype=torch.int16, device="cuda", generator=g).to(torch.int8)
+    ws = torch.rand(D, device="cuda", generator=g) * 1e-3
+    xr = torch.randn((*x.shape[:-1], D), device="cuda", generator=g).to(torch.bfloat16)
+    gshape = (B, T, 1, 1, D) if five_d else (B, 1, D)
+    gate = (torch.randn(gshape, device="cuda", generator=g) * 0.3).to(torch.bfloat16)
+    fs._tls.qkv = {}
+    try:
+        out = fi._int8_linear_residual(x, (wq, ws), None, {"x": xr, "gate": gate})
+        plain = fi._int8_linear_shared(x, (wq, ws), None)
+    finally:
+        fs._tls.qkv = None
+    assert out is not None and out.shape == xr.shape
+    want = torch.addcmul(xr, gate, plain.view(xr.shape))
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
