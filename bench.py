@@ -34,7 +34,9 @@ sys.path.insert(0, REPO)
 NCU_TRAFFIC = {
     # profiles/dequant_q4k_sweep.md: one-block capture (221.20 MB read + 729.71 MB written) x 36 blocks
     "sweep": 34_232_680_000,
-    "q8": None, "q4k": None, "w8a8": None, "prologue": None,
+    # profiles/w8a8_gemm.md: one configs[2] launch, 34.17 MB read + 87.15 MB written (the rest of Y still in L2)
+    "w8a8": 121_317_632,
+    "q8": None, "q4k": None, "prologue": None,
 }
 
 Q4K_TS, Q8_TS = 144, 34
@@ -916,7 +918,8 @@ def finish_w8a8(torch, args, world, rank, dist, r):
             "config": r["config"],
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
                          "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC.get("w8a8"), "peak_source": src,
-                         "kernel": "w8a8_gemm_kernel"},
+                         "kernel": ("w8a8_gemm_kernel" if os.environ.get("WEIGHTFERRY_W8A8_1SM") == "1"
+                                    else "w8a8_gemm_2sm_kernel")},
             "cpu_baseline": cpu, "e2e": r["e2e"], "gpu_launches": r["gpu_launches"], "clocks": r["clk"],
             "gemm_status": r["gemm_status"]}), flush=True)
     if dist is not None:
