@@ -562,6 +562,202 @@ __global__ void __launch_bounds__(128) quant_rows_kernel(const __nv_bfloat16 *__
     }
 }
 
+// v = the pending operation of the chunk (pre 1: the GELU table, pre 2: bf16(bf16(v * s1) + shift)), v bf16 in and out
+template <int PRE, int NCH>
+__device__ __forceinline__ void quant_pre(uint4 (&v)[NCH], const __nv_bfloat16 *__restrict__ s1,
+                                          const __nv_bfloat16 *__restrict__ sh, const __nv_bfloat16 *__restrict__ gelu,
+                                          int64_t goff, int lane) {
+    if constexpr (PRE == 2) {
+        const uint4 *sr = reinterpret_cast<const uint4 *>(s1 + goff);
+        const uint4 *hr = reinterpret_cast<const uint4 *>(sh + goff);
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) {
+            const uint4 sv = __ldg(sr + 32 * j + lane), hv = __ldg(hr + 32 * j + lane);
+            const uint32_t xs[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+            const uint32_t ss[4] = {sv.x, sv.y, sv.z, sv.w}, hs[4] = {hv.x, hv.y, hv.z, hv.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float a = r16(__fadd_rn(r16(__fmul_rn(bf_lo(xs[k]), bf_lo(ss[k]))), bf_lo(hs[k])));
+                const float b = r16(__fadd_rn(r16(__fmul_rn(bf_hi(xs[k]), bf_hi(ss[k]))), bf_hi(hs[k])));
+                o[k] = (__float_as_uint(a) >> 16) | (__float_as_uint(b) & 0xFFFF0000u);
+            }
+            v[j] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    } else if constexpr (PRE == 1) {
+        const uint16_t *tab = reinterpret_cast<const uint16_t *>(gelu);
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) {
+            const uint32_t xs[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+            uint32_t o[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                o[k] = static_cast<uint32_t>(__ldg(tab + (xs[k] & 0xFFFFu))) |
+                       (static_cast<uint32_t>(__ldg(tab + (xs[k] >> 16))) << 16);
+            v[j] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
+template <int NCH>
+__device__ __forceinline__ float chunk_amax(const uint4 (&v)[NCH]) {
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) {
+        const uint32_t xs[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) amax = fmaxf(amax, fmaxf(fabsf(bf_lo(xs[k])), fabsf(bf_hi(xs[k]))));
+    }
+    return amax;
+}
+
+// clamp(rint(bf16(v / sb)), -128, 127) of the four values of two bf16 pairs, as four bytes. The bf16 rounding of
+// the quotients is one cvt.rn.bf16x2 per pair (the reference's integer rounding gives the same value for every finite
+// or infinite quotient; a NaN becomes -128 either way). The bounds are integers, so clamping first gives
+// rint-then-clamp's value, and the round to the nearest (even) integer is the float addition of 1.5 * 2^23, whose
+// low mantissa byte is then the two's-complement int8 (exact for |y| <= 2^22).
+__device__ __forceinline__ uint32_t quant_quad(uint32_t xa, uint32_t xb, float sb) {
+    __nv_bfloat162 ta = __floats2bfloat162_rn(div_full(bf_lo(xa), sb), div_full(bf_hi(xa), sb));
+    __nv_bfloat162 tb = __floats2bfloat162_rn(div_full(bf_lo(xb), sb), div_full(bf_hi(xb), sb));
+    const uint32_t ua = *reinterpret_cast<uint32_t *>(&ta), ub = *reinterpret_cast<uint32_t *>(&tb);
+    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+    const uint32_t r0 = __float_as_uint(__fadd_rn(fminf(fmaxf(bf_lo(ua), -128.0f), 127.0f), kMagic));
+    const uint32_t r1 = __float_as_uint(__fadd_rn(fminf(fmaxf(bf_hi(ua), -128.0f), 127.0f), kMagic));
+    const uint32_t r2 = __float_as_uint(__fadd_rn(fminf(fmaxf(bf_lo(ub), -128.0f), 127.0f), kMagic));
+    const uint32_t r3 = __float_as_uint(__fadd_rn(fminf(fmaxf(bf_hi(ub), -128.0f), 127.0f), kMagic));
+    return __byte_perm(__byte_perm(r0, r1, 0x0040), __byte_perm(r2, r3, 0x0040), 0x5410);
+}
+
+template <int NCH>
+__device__ __forceinline__ void quant_store(const uint4 (&v)[NCH], float sb, uint2 *qr, int lane) {
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) qr[32 * j + lane] = make_uint2(quant_quad(v[j].x, v[j].y, sb),
+                                                                  quant_quad(v[j].z, v[j].w, sb));
+}
+
+// The quantiser without rotation or layer norm (pre 0 / 1 / 2) for K = 256 * NCH * WPR: the row in registers as packed
+// bf16 (WPR warps per row; lane l of the row's warp w holds the 8 values at 8 * (32 * (NCH * w + j) + l) .. +7,
+// j < NCH), all of the row's 16-byte loads issued before the first is used, the absmax by shuffles (and, with
+// WPR > 1, across the row's warps through shared memory), 8-byte int8 stores. With one warp per row and NCH <= 8 the
+// warp walks several rows and the loads of its next row are in flight while the current one is converted. The same
+// arithmetic as quant_rows_kernel above: the pending operation rounded to bf16 as there, amax = min(max |v|,
+// 3.38953139e38), scale = max(amax / 127, 1e-30) (div.full), q = clamp(rint(bf16(v / bf16(scale)))) -- every v is
+// already a bf16 value here, so the reference's bf16 rounding of v before the division is the identity.
+template <int PRE, int NCH, int WPR>
+__global__ void __launch_bounds__(256) quant_rows_reg_kernel(const __nv_bfloat16 *__restrict__ x,
+                                                             const __nv_bfloat16 *__restrict__ s1,
+                                                             const __nv_bfloat16 *__restrict__ sh,
+                                                             const __nv_bfloat16 *__restrict__ gelu,
+                                                             int8_t *__restrict__ q, float *__restrict__ scale_out,
+                                                             int64_t rows, int64_t rows_per_group) {
+    constexpr int K = 256 * NCH * WPR;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if constexpr (WPR == 1 && NCH <= 8) {
+        const int64_t nw = static_cast<int64_t>(gridDim.x) * 8;
+        int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+        uint4 v[NCH], nx[NCH];
+        if (row < rows) {
+#pragma unroll
+            for (int j = 0; j < NCH; ++j) nx[j] = __ldg(reinterpret_cast<const uint4 *>(x + row * K) + 32 * j + lane);
+        }
+        for (; row < rows; row += nw) {
+#pragma unroll
+            for (int j = 0; j < NCH; ++j) v[j] = nx[j];
+            const int64_t nrow = row + nw;
+            if (nrow < rows) {
+#pragma unroll
+                for (int j = 0; j < NCH; ++j)
+                    nx[j] = __ldg(reinterpret_cast<const uint4 *>(x + nrow * K) + 32 * j + lane);
+            }
+            quant_pre<PRE, NCH>(v, s1, sh, gelu, (row / rows_per_group) * K, lane);
+            float amax = chunk_amax<NCH>(v);
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+            amax = fminf(amax, 3.38953139e38f);
+            const float scale = fmaxf(div_full(amax, 127.0f), 1.0e-30f);
+            if (lane == 0) scale_out[row] = scale;
+            quant_store<NCH>(v, r16(scale), reinterpret_cast<uint2 *>(q + row * K), lane);
+        }
+    } else {
+        constexpr int ROWS_PER_CTA = 8 / WPR;
+        __shared__ float red[8];
+        const int seg = warp % WPR;  // this warp's segment of its row
+        const int64_t n_groups = (rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
+        for (int64_t rg = blockIdx.x; rg < n_groups; rg += gridDim.x) {
+            const int64_t row = rg * ROWS_PER_CTA + warp / WPR;
+            const bool live = row < rows;
+            uint4 v[NCH];
+            const int64_t off = static_cast<int64_t>(seg) * (K / WPR);  // element offset of the segment in the row
+            float amax = 0.f;
+            if (live) {
+                const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * K + off);
+#pragma unroll
+                for (int j = 0; j < NCH; ++j) v[j] = __ldg(xr + 32 * j + lane);
+                quant_pre<PRE, NCH>(v, s1, sh, gelu, (row / rows_per_group) * K + off, lane);
+                amax = chunk_amax<NCH>(v);
+            }
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+            if constexpr (WPR > 1) {
+                if (lane == 0) red[warp] = amax;
+                __syncthreads();
+                const int w0 = warp - seg;
+#pragma unroll
+                for (int w = 0; w < WPR; ++w) amax = fmaxf(amax, red[w0 + w]);
+                __syncthreads();  // red is written again by the next row group
+            }
+            if (live) {
+                amax = fminf(amax, 3.38953139e38f);
+                const float scale = fmaxf(div_full(amax, 127.0f), 1.0e-30f);
+                if (lane == 0 && seg == 0) scale_out[row] = scale;
+                quant_store<NCH>(v, r16(scale), reinterpret_cast<uint2 *>(q + row * K + off), lane);
+            }
+        }
+    }
+}
+
+template <int PRE, int NCH, int WPR>
+int launch_quant_reg(const void *x, const void *s1, const void *sh, const void *gelu, int8_t *q, float *sc,
+                     int64_t rows, int64_t rpg, cudaStream_t s) {
+    auto kern = quant_rows_reg_kernel<PRE, NCH, WPR>;
+    static int per_sm = 0;
+    if (per_sm == 0) {
+        int n = 0;
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 256, 0);
+        if (e != cudaSuccess) return static_cast<int>(e);
+        per_sm = std::max(n, 1);
+    }
+    const int64_t groups = (rows + (8 / WPR) - 1) / (8 / WPR);
+    // the pipelined variant walks about two rows per warp; the others one row group per CTA while they fit
+    const int64_t want = (WPR == 1 && NCH <= 8) ? (groups + 1) / 2 : groups;
+    const int grid = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(device_sm_count()) * per_sm));
+    kern<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(s1),
+                              static_cast<const __nv_bfloat16 *>(sh), static_cast<const __nv_bfloat16 *>(gelu), q,
+                              sc, rows, rpg);
+    return static_cast<int>(cudaGetLastError());
+}
+
+// The register kernel's (NCH, WPR) for K, or false: one warp per row up to K = 6144, eight from K = 8192 to 32768.
+template <int PRE>
+bool quant_reg_dispatch(int64_t K, const void *x, const void *s1, const void *sh, const void *gelu, int8_t *q,
+                        float *sc, int64_t rows, int64_t rpg, cudaStream_t s, int *rc) {
+#define WF_QR(N, W) do { *rc = launch_quant_reg<PRE, N, W>(x, s1, sh, gelu, q, sc, rows, rpg, s); return true; } while (0)
+    if (K % 256 != 0) return false;
+    switch (K / 256) {
+        case 1: WF_QR(1, 1); case 2: WF_QR(2, 1); case 3: WF_QR(3, 1); case 4: WF_QR(4, 1); case 5: WF_QR(5, 1);
+        case 6: WF_QR(6, 1); case 8: WF_QR(8, 1); case 10: WF_QR(10, 1); case 12: WF_QR(12, 1);
+        case 16: WF_QR(16, 1); case 20: WF_QR(20, 1); case 24: WF_QR(24, 1);
+        default: break;
+    }
+    if (K % 2048 != 0) return false;
+    switch (K / 2048) {
+        case 4: WF_QR(4, 8); case 5: WF_QR(5, 8); case 6: WF_QR(6, 8); case 8: WF_QR(8, 8); case 10: WF_QR(10, 8);
+        case 12: WF_QR(12, 8); case 16: WF_QR(16, 8);
+        default: return false;
+    }
+#undef WF_QR
+}
+
 template <int PRE, bool ROT>
 int launch_quant(const void *x, const void *s1, const void *sh, const void *gelu, int8_t *q, float *sc, int64_t rows,
                  int64_t K, int64_t rpg, float eps, cudaStream_t s) {
@@ -682,6 +878,15 @@ extern "C" WF_API int wf_quant_rows(const void *x, const void *s1, const void *s
     int rc = check_device();
     if (rc != WF_OK) return rc;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (!rotate && pre != 3 && al(x, 16) && al(q, 8) && (pre != 2 || (al(s1, 16) && al(shift, 16)))) {
+        bool done = false;
+        switch (pre) {
+            case 0: done = quant_reg_dispatch<0>(K, x, s1, shift, gelu_table, q, scale, rows, rows_per_group, s, &rc); break;
+            case 1: done = quant_reg_dispatch<1>(K, x, s1, shift, gelu_table, q, scale, rows, rows_per_group, s, &rc); break;
+            default: done = quant_reg_dispatch<2>(K, x, s1, shift, gelu_table, q, scale, rows, rows_per_group, s, &rc); break;
+        }
+        if (done) return rc;
+    }
 #define WF_Q(P, R) return launch_quant<P, R>(x, s1, shift, gelu_table, q, scale, rows, K, rows_per_group, eps, s)
     if (rotate) {
         switch (pre) { case 0: WF_Q(0, true); case 1: WF_Q(1, true); case 2: WF_Q(2, true); default: WF_Q(3, true); }

@@ -259,3 +259,38 @@ def test_fused_c_abi_rejections(cuda):
     assert L.wf_modulate(p, p, p, p, 4, 1001, 1, st) == -1              # d not a multiple of 8
     assert L.wf_quant_rows(p, None, None, None, p, p, 4, 1000, 1, 0.0, 0, 1, st) == -1  # rotate needs K % 256
     assert L.wf_quant_rows(p, None, None, None, p, p, 4, 1024, 1, 0.0, 2, 0, st) == -1  # modulate needs s1 / shift
+
+
+@pytest.mark.parametrize("pre", [0, 1, 2])
+@pytest.mark.parametrize("k", [256, 768, 1280, 2048, 5120, 6144, 8192, 20480, 1000])
+def test_quant_rows_register_kernel_matches_shared_kernel(cuda, pre, k):
+    """The register-resident quantiser (16-byte aligned operands, K = 256 * n for the sizes it takes) and the
+    shared-memory one (any K % 4 == 0; reached here through an x that is only 8-byte aligned) give the same bits."""
+    import torch
+    ext = wf("_ext")
+    L = ext.lib()
+    g = torch.Generator(device="cuda").manual_seed(k + pre)
+    rows, rpg = 37, 5
+    groups = (rows + rpg - 1) // rpg
+    base = (torch.randn((rows * k + 8,), device="cuda", generator=g) * 3).to(torch.bfloat16)
+    x_al = base[:rows * k].clone()                                    # 16-byte aligned
+    x_al[3 * k:4 * k] = 0                                             # an all-zero row
+    x_mis = base[4:4 + rows * k]                                      # 8-byte aligned only
+    x_mis.copy_(x_al)
+    s1 = (1 + 0.1 * torch.randn((groups * k,), device="cuda", generator=g)).to(torch.bfloat16)
+    sh = (0.1 * torch.randn((groups * k,), device="cuda", generator=g)).to(torch.bfloat16)
+    gelu = wf("enhancers.fused_int8")._gelu_table(torch.device("cuda")) if pre == 1 else None
+    outs = []
+    for x in (x_al, x_mis):
+        q = torch.empty((rows, k), dtype=torch.int8, device="cuda")
+        sc = torch.empty((rows,), dtype=torch.float32, device="cuda")
+        rc = L.wf_quant_rows(x.data_ptr(), s1.data_ptr() if pre == 2 else None, sh.data_ptr() if pre == 2 else None,
+                             gelu.data_ptr() if pre == 1 else None, q.data_ptr(), sc.data_ptr(), rows, k, rpg, 0.0,
+                             pre, 0, ext.stream_of(x.device))
+        ext.check(rc, "wf_quant_rows")
+        outs.append((q, sc))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1].view(torch.int32), outs[1][1].view(torch.int32))
+    if pre != 2:                                                      # (with modulate the row becomes the shift)
+        assert float(outs[0][1][3]) == pytest.approx(1e-30)
