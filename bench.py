@@ -272,6 +272,7 @@ def run_sweep(torch, args, world, rank, dist):
     value = total_out / (total_ms / 1e3) / 1e9
     del srcs, dsts
     torch.cuda.empty_cache()
+    mix = hbm_mix_probe(torch, lib, ext, dev, in_bytes, out_bytes, stream)
     e2e = None
     if not args.no_e2e:
         e2e = e2e_block(torch, gd, dev, args)
@@ -280,13 +281,37 @@ def run_sweep(torch, args, world, rank, dist):
     return {
         "value": value, "ms_per_step": total_ms / args.steps, "kern_ms": kern_ms,
         "alg_bytes_per_launch": (in_bytes + out_bytes) / launches_per_step, "clk": clk.summary(), "e2e": e2e,
-        "gpu_launches": launches,
+        "gpu_launches": launches, "mix_gbs": mix,
         "config": {"workload": "GGUF Q4_K -> bf16 sweep of a Cosmos-Predict2-14B checkpoint (configs[1])",
                    "blocks_per_rank": args.blocks, "tensors_per_rank": len(mine), "values_per_rank": n_values,
                    "in_bytes_per_rank": in_bytes, "out_bytes_per_rank": out_bytes, "mid_dtype": "f16",
                    "sharding": "by tensor, greedy bin-pack of an N x 36-block table, no communication",
                    "l2": "inputs larger than L2 (36 GB per rank per step); no flush"},
     }
+
+
+def hbm_mix_probe(torch, lib, ext, dev, in_bytes, out_bytes, stream):
+    """GB/s of wf_hbm_probe -- a plain streaming kernel that reads in_bytes and writes out_bytes with coalesced
+    16-byte accesses -- over buffers of the sweep's own sizes (mean of 3 launches after 1 untimed): the HBM rate this
+    read : write mix reaches, beside the copy-based peak. Runs after the timed region, on its freed memory."""
+    a = torch.empty(in_bytes // 16 * 16, dtype=torch.uint8, device=dev)
+    b = torch.empty(out_bytes // 16 * 16, dtype=torch.uint8, device=dev)
+
+    def go():
+        ext.check(lib.wf_hbm_probe(a.data_ptr(), a.numel(), b.data_ptr(), b.numel(), stream.cuda_stream),
+                  "wf_hbm_probe")
+
+    go()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(3):
+        go()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    gbs = 3 * (a.numel() + b.numel()) / (e0.elapsed_time(e1) / 1e3) / 1e9
+    del a, b
+    torch.cuda.empty_cache()
+    return gbs
 
 
 def e2e_block(torch, gd, dev, args):
@@ -883,6 +908,11 @@ def main():
                          else "dequant_kernel (single weight)"},
             "cpu_baseline": cpu, "e2e": r["e2e"], "gpu_launches": r["gpu_launches"], "clocks": r["clk"],
         }
+        if r.get("mix_gbs"):
+            # the copy-based peak assumes read = write; this traffic is write-heavy (in : out about 1 : 3.6), and a
+            # plain streaming kernel with the same byte counts (wf_hbm_probe) is the ceiling it is measured against too
+            line["roofline"]["mix_ceiling"] = {"gbs": round(r["mix_gbs"], 1), "frac": round(achieved / r["mix_gbs"], 4),
+                                               "probe": "wf_hbm_probe over the sweep's in / out byte counts"}
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()

@@ -96,6 +96,44 @@ __device__ __forceinline__ __half h_int(uint32_t v, float off) {
 // bit i (i = 0..3) of v moved to bit 0 of byte i
 __device__ __forceinline__ uint32_t spread4(uint32_t v) { return ((v & 0xFu) * 0x00204081u) & 0x01010101u; }
 
+// Q4_K / Q5_K: the scale and the min of sub-block `sub` (0..7) of a super-block, ds = f16(d * sc) and
+// dm = f16(dmin * mn) with the 6-bit sc / mn unpacked from the 12 scale bytes (gguf_dequant.py:170-185), splatted
+__device__ __forceinline__ void kq_scales(const uint8_t *blk, int sub, __half2 &ds, __half2 &dm) {
+    const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
+    const uint8_t *sc_b = blk + 4;
+    uint32_t sc, mn;
+    if (sub < 4) {
+        sc = sc_b[sub] & 63u;
+        mn = sc_b[4 + sub] & 63u;
+    } else {
+        const int j = sub - 4;
+        sc = (sc_b[8 + j] & 0xFu) | ((sc_b[j] >> 2) & 0x30u);
+        mn = (sc_b[8 + j] >> 4) | ((sc_b[4 + j] >> 2) & 0x30u);
+    }
+    ds = __half2half2(__hmul_rn(h_of_bits(dd), h_int(sc, 0.f)));
+    dm = __half2half2(__hmul_rn(h_of_bits(dd >> 16), h_int(mn, 0.f)));
+}
+
+// Q4_K / Q5_K: eight values from v0 of a super-block with their sub-block's (ds, dm): x = f16(f16(ds * q) - dm)
+template <int QT>
+__device__ __forceinline__ void decode8_kq(const uint8_t *blk, int v0, __half2 ds, __half2 dm, __half2 h[4]) {
+    const int sub = v0 >> 5;
+    constexpr int QS_OFF = (QT == 12) ? 16 : 48;
+    const uint2 b = *reinterpret_cast<const uint2 *>(blk + QS_OFF + (sub >> 1) * 32 + (v0 & 31));
+    const uint32_t sh = (sub & 1) * 4;
+    uint32_t lo = (b.x >> sh) & 0x0F0F0F0Fu, hi = (b.y >> sh) & 0x0F0F0F0Fu;
+    if constexpr (QT == 13) {
+        const uint2 hb = *reinterpret_cast<const uint2 *>(blk + 16 + (v0 & 31));
+        lo |= ((hb.x >> sub) & 0x01010101u) << 4;
+        hi |= ((hb.y >> sub) & 0x01010101u) << 4;
+    }
+    const __half2 bias = h2_bias(1024.0f);
+    bytes4_h2(lo, bias, h[0], h[1]);
+    bytes4_h2(hi, bias, h[2], h[3]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __hsub2_rn(__hmul2_rn(ds, h[i]), dm);
+}
+
 template <int QT>
 __device__ __forceinline__ void decode8_h(const uint8_t *blk, int v0, __half2 h[4]) {
     if constexpr (QT == 8) {  // Q8_0
@@ -128,34 +166,9 @@ __device__ __forceinline__ void decode8_h(const uint8_t *blk, int v0, __half2 h[
             for (int i = 0; i < 4; ++i) h[i] = __hadd2_rn(h[i], m);
         }
     } else if constexpr (QT == 12 || QT == 13) {  // Q4_K / Q5_K
-        const int sub = v0 >> 5;
-        const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
-        const uint8_t *sc_b = blk + 4;
-        uint32_t sc, mn;
-        if (sub < 4) {
-            sc = sc_b[sub] & 63u;
-            mn = sc_b[4 + sub] & 63u;
-        } else {
-            const int j = sub - 4;
-            sc = (sc_b[8 + j] & 0xFu) | ((sc_b[j] >> 2) & 0x30u);
-            mn = (sc_b[8 + j] >> 4) | ((sc_b[4 + j] >> 2) & 0x30u);
-        }
-        const __half2 ds = __half2half2(__hmul_rn(h_of_bits(dd), h_int(sc, 0.f)));
-        const __half2 dm = __half2half2(__hmul_rn(h_of_bits(dd >> 16), h_int(mn, 0.f)));
-        constexpr int QS_OFF = (QT == 12) ? 16 : 48;
-        const uint2 b = *reinterpret_cast<const uint2 *>(blk + QS_OFF + (sub >> 1) * 32 + (v0 & 31));
-        const uint32_t sh = (sub & 1) * 4;
-        uint32_t lo = (b.x >> sh) & 0x0F0F0F0Fu, hi = (b.y >> sh) & 0x0F0F0F0Fu;
-        if constexpr (QT == 13) {
-            const uint2 hb = *reinterpret_cast<const uint2 *>(blk + 16 + (v0 & 31));
-            lo |= ((hb.x >> sub) & 0x01010101u) << 4;
-            hi |= ((hb.y >> sub) & 0x01010101u) << 4;
-        }
-        const __half2 bias = h2_bias(1024.0f);
-        bytes4_h2(lo, bias, h[0], h[1]);
-        bytes4_h2(hi, bias, h[2], h[3]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) h[i] = __hsub2_rn(__hmul2_rn(ds, h[i]), dm);
+        __half2 ds, dm;
+        kq_scales(blk, v0 >> 5, ds, dm);
+        decode8_kq<QT>(blk, v0, ds, dm, h);
     } else if constexpr (QT == 14) {  // Q6_K
         const int hh = v0 >> 7, r = v0 & 127;
         const uint2 lo = lds8_any(blk + hh * 64 + (r & 63));
@@ -364,6 +377,31 @@ template <int QT, int MID, int OUT, bool ALIGNED, bool LORA>
 __device__ __forceinline__ void decode_chunk(const uint8_t *sbuf, void *dst_chunk, int valid_values,
                                              const float *diff_chunk, float sa) {
     constexpr int VPB = Fmt<QT>::VPB, TS = Fmt<QT>::TS;
+    if constexpr (MID == WF_F16 && !LORA && (QT == 12 || QT == 13)) {
+        // Q4_K / Q5_K: each thread decodes one 32-value sub-block's (ds, dm) into shared memory once per chunk
+        // (kChunkValues / 32 == kThreads), so the groups below read it with one load instead of unpacking the
+        // 6-bit scales again for every 8 values
+        static_assert(kChunkValues / 32 == kThreads, "one sub-block per thread");
+        __shared__ uint2 s_kq[kThreads];
+        const int sub_all = threadIdx.x;
+        if (32 * sub_all < valid_values) {
+            __half2 ds, dm;
+            kq_scales(sbuf + (sub_all / 8) * TS, sub_all % 8, ds, dm);
+            s_kq[sub_all] = make_uint2(*reinterpret_cast<uint32_t *>(&ds), *reinterpret_cast<uint32_t *>(&dm));
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < kGroupsPerThread; ++i) {
+            const int v = 8 * (threadIdx.x + i * kThreads);
+            if (v >= valid_values) break;
+            const uint2 sd = s_kq[v >> 5];
+            __half2 h[4];
+            decode8_kq<QT>(sbuf + (v / VPB) * TS, v % VPB, *reinterpret_cast<const __half2 *>(&sd.x),
+                           *reinterpret_cast<const __half2 *>(&sd.y), h);
+            store8_h<OUT, ALIGNED>(static_cast<uint8_t *>(dst_chunk) + static_cast<size_t>(v) * dtype_size(OUT), h);
+        }
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < kGroupsPerThread; ++i) {
         const int g = threadIdx.x + i * kThreads;

@@ -224,3 +224,26 @@ def test_c_abi_rejects_unaligned_output(cuda):
     d = torch.empty(64, dtype=torch.bfloat16, device="cuda")
     st = ext.stream_of(s.device)
     assert ext.lib().wf_dequant_gguf(s.data_ptr(), 34, d.data_ptr() + 1, 32, 8, 0, 1, st) == -1
+
+
+def test_hbm_probe_writes_its_pattern(cuda):
+    """The benchmark's mix probe (wf_hbm_probe) does the work it is timed for: out[j] = in[floor(j * r)] ^ j per
+    16-byte unit with r the 32.32 fixed-point in / out ratio, every output unit written."""
+    import torch
+    ext = wf("_ext")
+    L = ext.lib()
+    n_in, n_out = 9 * 1000 + 7, 32 * 1000 + 5           # about the Q4_K sweep's 9 : 32 mix, ragged tiles
+    a = torch.randint(0, 2**31 - 1, (n_in, 4), dtype=torch.int32, device="cuda")
+    b = torch.zeros((n_out, 4), dtype=torch.int32, device="cuda")
+    ext.check(L.wf_hbm_probe(a.data_ptr(), n_in * 16, b.data_ptr(), n_out * 16, ext.stream_of(a.device)), "probe")
+    torch.cuda.synchronize()
+    r = (n_in << 32) // n_out
+    j = np.arange(n_out, dtype=np.uint64)
+    idx = ((j * np.uint64(r)) >> np.uint64(32)).astype(np.int64)
+    want = a.cpu().numpy()[idx].copy()
+    want[:, 0] ^= np.arange(n_out, dtype=np.int64).astype(np.uint32).view(np.int32)
+    assert np.array_equal(b.cpu().numpy(), want)
+    p = a.data_ptr()
+    assert L.wf_hbm_probe(p, 32, p, 16, None) == -1      # reads larger than writes
+    assert L.wf_hbm_probe(p + 8, 16, p, 32, None) == -1  # alignment
+    assert L.wf_hbm_probe(p, 24, p, 32, None) == -1      # not a multiple of 16
