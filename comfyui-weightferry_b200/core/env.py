@@ -19,6 +19,12 @@ DEFAULTS = {
     "WEIGHTFERRY_PROFILE": None,           # 1: CUDA-event timeline of the streaming pipeline
     "WEIGHTFERRY_AUTO": None,              # 1: the streaming node chooses resident blocks as with auto_config
     "WEIGHTFERRY_AUTO_HEADROOM_MB": "1536",  # VRAM auto_config leaves for activations
+    "WEIGHTFERRY_TIERING": None,           # auto / ram: overrides the streaming node's tiering option
+    "WEIGHTFERRY_RAM_BUDGET_GB": None,     # pinned-RAM budget of the streamed blocks (None: the node's option)
+    "WEIGHTFERRY_RAM_MARGIN_GB": "6",      # RAM kept free when the budget is the available RAM
+    "WEIGHTFERRY_DISK_DIR": None,          # folder of the SSD tier's cache files (None: ComfyUI's / the system temp)
+    "WEIGHTFERRY_DISK_THREADS": None,      # SSD reader threads (None: the probe's fastest count)
+    "WEIGHTFERRY_SSD_LAYOUT": "interleave",  # which streamed blocks go to the SSD: interleave / tail
     "WEIGHTFERRY_SETTINGS_FILE": None,
 }
 

@@ -23,15 +23,24 @@ ComfyUI, the diffusion model itself (an ``nn.Module``). On a CUDA model whose di
    dit_node.py:414-455) with begin_forward / end_forward, starting the first transfers before the resident blocks
    run, and captures again when something else rebound the streamed parameters (a ComfyUI model load).
 
-Options of the reference that select parts outside the quantized-weight path -- chunk streaming, the SSD tier,
-self-managed resident blocks, SageAttention, the fp8 storage host format, the RAM / VRAM budgets -- are accepted and
-logged as not used here. "Single Buffer (Synchronous)" issues each block's transfer when the block starts (no
-look-ahead)."""
+With ``tiering`` "Auto (GPU / RAM / SSD)" (or WEIGHTFERRY_TIERING=auto) and a RAM budget (``ram_budget_gb`` or
+WEIGHTFERRY_RAM_BUDGET_GB; else the available RAM minus WEIGHTFERRY_RAM_MARGIN_GB), core/tiers/plan.plan_tiers splits
+the streamed blocks between pinned RAM and the SSD (the reference's tier planner, core/tiers/plan.py:60-151): the SSD
+blocks, interleaved among the others, are written to a cache file (O_DIRECT) and read back every forward by a
+DiskRing of pinned buffers and the uploader thread (streaming/ssd_uploader.py), which also dequantises them; their
+parameters rest on a mapping of the cache file.
+
+Options of the reference that select parts outside the quantized-weight path -- chunk streaming, self-managed
+resident blocks, SageAttention, the fp8 storage host format, the VRAM budget -- are accepted and logged as not used
+here. "Single Buffer (Synchronous)" issues each block's transfer when the block starts (no look-ahead)."""
 
 import torch
 
 from ..core import env as _env
+from ..core.tiers.cache_files import DiskBlockStore, default_cache_dir, new_cache_path
 from ..core.tiers.pinned import PinnedHost, release_all
+from ..core.tiers.plan import plan_tiers, ssd_positions
+from ..core.tiers.sources import DiskRing
 from ..utils.logging import log_info, log_warn
 from .state import _GGUF_GEOMETRY, BlockLayout, ParamSpec, _StreamState
 
@@ -149,8 +158,14 @@ class _PageableHost:
 class _NodeState:
     """One streaming configuration of a diffusion model: the captured blocks, their rest binding and the slot ring."""
 
-    def __init__(self, owner, dit, stream_idx, device, pin_memory, num_slots, lookahead, compute_dtype):
+    def __init__(self, owner, dit, stream_idx, device, pin_memory, num_slots, lookahead, compute_dtype,
+                 tiering_auto=False, ram_budget_bytes=None):
         self.owner = owner
+        self.tiering_auto = tiering_auto
+        self.ram_budget_bytes = ram_budget_bytes
+        self.tier_plan = None
+        self.store = None
+        self.disk_blocks = []
         self.dit = dit
         self.stream_idx = list(stream_idx)
         self.device = torch.device(device)
@@ -163,6 +178,7 @@ class _NodeState:
         self.entries = []   # per streamed block: [(param, name, dequantised?, rest tensor, tensor_type)]
         self.ring = None
         self.captures = 0
+        self.bound = set()  # streamed blocks whose parameters are bound to their slot (between pre and post hook)
 
     # ------------------------------------------------------------------------------------------------ capture
     def capture(self):
@@ -176,28 +192,55 @@ class _NodeState:
             if not _same_layout(specs, other):
                 raise ValueError(f"streamed block {i} has another parameter layout than block {self.stream_idx[0]}")
         layout = BlockLayout(specs, compute_dtype=self.compute_dtype)
+        self._plan_tiers(len(streamed), layout.flat_bytes)
+        disk_set = set(self.disk_blocks)
         holder_cls = PinnedHost if self.pin_memory else _PageableHost
-        flats = []
-        for blk in streamed:
-            holder = holder_cls(layout.flat_bytes)
-            flat = holder.tensor
-            entries = []
+        flats, pending = [], []
+        for b, blk in enumerate(streamed):
+            if b in disk_set:  # SSD tier: the block's flat bytes go to the cache file
+                flat = self.store.staging()
+                flats.append(None)
+            else:
+                holder = holder_cls(layout.flat_bytes)
+                self.holders.append(holder)
+                flat = holder.tensor
+                flats.append(flat)
+            flat.zero_()
             params = dict(blk.named_parameters())
+            block_params = []
             for sp, d, off in zip(specs, deq, layout.offsets):
                 p = params[sp.name]
                 raw = _raw(p)
-                dst = flat[off:off + sp.packed_bytes]
-                dst.copy_(raw.reshape(-1).view(torch.uint8))
-                rest = dst.view(raw.dtype).view(raw.shape)
+                flat[off:off + sp.packed_bytes].copy_(raw.reshape(-1).view(torch.uint8))
+                block_params.append((p, sp, d, off, raw.dtype, raw.shape))
+            if b in disk_set:
+                self.store.write_block(self.disk_blocks.index(b), flat)
+            pending.append(block_params)
+        ring = None
+        if self.store is not None:
+            self.store.finalize()
+            # the SSD-tier parameters rest on a mapping of the cache file (no RAM held for them)
+            mapped = torch.from_file(self.store.path, shared=True, size=self.store.stride * self.store.n_blocks,
+                                     dtype=torch.uint8)
+            for k, b in enumerate(self.disk_blocks):
+                flats_b = mapped[k * self.store.stride:k * self.store.stride + layout.flat_bytes]
+                pending[b] = [(p, sp, d, off, dt, sh, flats_b) for p, sp, d, off, dt, sh in pending[b]]
+            plan = self.tier_plan
+            ring = DiskRing(self.store, depth=max(2, plan["ring_depth"]), pin=self.pin_memory,
+                            threads=plan["disk_threads"])
+        for b, block_params in enumerate(pending):
+            entries = []
+            for item in block_params:
+                p, sp, d, off, dt, sh = item[:6]
+                src = item[6] if len(item) > 6 else flats[b]
+                rest = src[off:off + sp.packed_bytes].view(dt).view(sh)
                 entries.append((p, sp.name, d, rest, getattr(p, "tensor_type", None)))
-            self.holders.append(holder)
-            flats.append(flat)
             self.entries.append(entries)
         # the rest binding: between uses the streamed parameters are the host bytes (their GPU copies are freed)
         for entries in self.entries:
             for p, _name, _d, rest, _tt in entries:
                 p.data = rest
-        self.ring = _StreamState(self.device, flats, layout, num_slots=self.num_slots)
+        self.ring = _StreamState(self.device, flats, layout, num_slots=self.num_slots, ring=ring)
         self.ring.lookahead = self.lookahead
         self.layout = layout
         self.captures += 1
@@ -211,11 +254,34 @@ class _NodeState:
                     return False
         return bool(self.entries)
 
+    def _plan_tiers(self, num_stream, block_bytes):
+        """With tiering "Auto": how many streamed blocks go to the SSD (core/tiers/plan.plan_tiers), their positions
+        (interleaved) and the cache file that holds them."""
+        self.disk_blocks, self.tier_plan = [], None
+        if not self.tiering_auto:
+            return
+        plan = plan_tiers(num_stream, block_bytes, ram_budget_bytes=self.ram_budget_bytes, disk_dir=default_cache_dir())
+        self.tier_plan = plan
+        if plan["disk_error"] is not None:
+            log_warn(f"DiT Layer Streaming [tiers]: no SSD tier ({plan['disk_error']}); every block in RAM.")
+        if plan["disk_blocks"] <= 0:
+            return
+        self.disk_blocks = ssd_positions(num_stream, plan["disk_blocks"])
+        self.store = DiskBlockStore(new_cache_path(plan["disk_dir"]), block_bytes, len(self.disk_blocks))
+        log_info(f"DiT Layer Streaming [tiers]: {plan['ram_blocks']} streamed blocks in pinned RAM, "
+                 f"{plan['disk_blocks']} on the SSD ({self.store.path}), ring depth {plan['ring_depth']}, "
+                 f"{plan['disk_threads']} reader thread(s), drive {plan['disk_read_gbps']} GB/s.")
+
     def drop_ring(self):
+        if self.ring is not None:
+            self.ring.close()
         self.ring = None
         self.entries = []
         release_all(self.holders)
         self.holders = []
+        if self.store is not None:
+            self.store.delete()
+            self.store = None
 
     # ------------------------------------------------------------------------------------------------ hooks
     def install_hooks(self):
@@ -231,26 +297,38 @@ class _NodeState:
             if self.ring is None:
                 return
             views = self.ring.acquire(k)
+            self.bound.add(k)
             for p, name, d, _rest, _tt in self.entries[k]:
                 p.data = views[name]
                 if d:
                     p.tensor_type = None  # a plain tensor while the block runs: used as it is
         return pre
 
+    def _restore(self, k):
+        for p, _name, d, rest, tt in self.entries[k]:
+            p.data = rest
+            if d:
+                p.tensor_type = tt
+        self.bound.discard(k)
+
     def _make_post(self, k):
         def post(module, args, output):
             if self.ring is None:
                 return
             self.ring.release(k)
-            for p, _name, d, rest, tt in self.entries[k]:
-                p.data = rest
-                if d:
-                    p.tensor_type = tt
+            self._restore(k)
         return post
 
     def _dit_pre(self, module, args):
         if getattr(self.dit, _STATE_ATTR, None) is not self:
             return
+        if self.bound:
+            # the last forward stopped inside a streamed block (an exception skipped its post hook): its parameters
+            # go back to the host bytes (the reference restores the rest binding in a finally), and the GPU work it
+            # queued finishes before any slot is written again
+            for k in list(self.bound):
+                self._restore(k)
+            torch.cuda.synchronize(self.device)
         if self.ring is None or not self.bindings_intact():
             log_info("DiT Layer Streaming: the streamed weights were rebound; capturing them again.")
             self.capture()
@@ -326,7 +404,6 @@ class WeightFerryDiT:
         unused = [n for n, on in (("sage_attention", sage_attention), ("sage_pv_fp16", sage_pv_fp16),
                                   ("host_format=storage", host_format == HOST_FORMAT_STORAGE),
                                   ("resident_mode=self", resident_mode == RESIDENT_MODE_SELF),
-                                  ("tiering=auto", tiering == TIERING_AUTO), ("ram_budget_gb", ram_budget_gb > 0),
                                   ("vram_budget_gb", vram_budget_gb > 0)) if on]
         if unused:
             log_info(f"DiT Layer Streaming: not used by this build: {', '.join(unused)}.")
@@ -370,7 +447,12 @@ class WeightFerryDiT:
 
         teardown(dit)  # an earlier configuration of this model (the reference's _teardown(dit, "re-load"))
         num_slots = max(2, int(prefetch_slots)) if is_double else 2
-        st = _NodeState(object(), dit, stream_idx, device, pin_memory, num_slots, is_double, compute_dtype)
+        env_tiering = _env.get("WEIGHTFERRY_TIERING")
+        tiering_auto = (env_tiering == "auto") if env_tiering else tiering == TIERING_AUTO
+        env_budget = _env.get("WEIGHTFERRY_RAM_BUDGET_GB")
+        ram_budget_bytes = int(float(env_budget if env_budget else ram_budget_gb) * 1024 ** 3) or None
+        st = _NodeState(object(), dit, stream_idx, device, pin_memory, num_slots, is_double, compute_dtype,
+                        tiering_auto=tiering_auto, ram_budget_bytes=ram_budget_bytes)
         st.capture()
         st.install_hooks()
         setattr(dit, _STATE_ATTR, st)

@@ -90,6 +90,8 @@ class StreamedStack:
         return x_rows
 
     def close(self):
+        if self.state is not None:
+            self.state.close()
         release_all(self.holders)
         self.holders = []
         self.host_flats = []

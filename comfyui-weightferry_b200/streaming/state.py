@@ -80,11 +80,17 @@ class BlockLayout:
 class _StreamState:
     """GPU slots, transfer / dequant streams and events of one streamed block list (one owner, one device)."""
 
-    def __init__(self, device, host_flats, layout, num_slots=None, profile=None):
+    def __init__(self, device, host_flats, layout, num_slots=None, profile=None, ring=None):
         self.device = torch.device(device)
-        self.host_flats = host_flats          # per block: flat pinned uint8 tensor (DMA source)
+        self.host_flats = host_flats          # per block: flat pinned uint8 tensor (DMA source), None: SSD tier
         self.layout = layout
         self.num_stream = len(host_flats)
+        # SSD tier: the blocks without a host flat are read by `ring` (core/tiers/sources.DiskRing) in block order
+        disk = [s for s, f in enumerate(host_flats) if f is None]
+        self.disk_index = {s: k for k, s in enumerate(disk)}
+        if disk and (ring is None or ring.n != len(disk)):
+            raise ValueError(f"{len(disk)} blocks have no host flat; the SSD ring must serve exactly those")
+        self.ring = ring if disk else None
         if num_slots is None:
             env_slots = _env.get("WEIGHTFERRY_SLOTS")
             num_slots = int(env_slots) if env_slots else 3
@@ -115,6 +121,10 @@ class _StreamState:
         self.lookahead = True  # False: a block's transfer is issued when it starts (single buffer), not ahead
         want_prof = profile if profile is not None else _env.get("WEIGHTFERRY_PROFILE") == "1"
         self.profiler = _StreamProfiler(self.num_stream, layout.flat_bytes) if want_prof else None
+        self.uploader = None
+        if self.ring is not None:
+            from .ssd_uploader import _SsdUploader
+            self.uploader = _SsdUploader(self)
 
     # ------------------------------------------------------------------------------------------------ layout
     def _bind_views(self, slot):
@@ -172,24 +182,37 @@ class _StreamState:
                 prof.record(s_idx, "dma1", cs)
             self.transferred_events[s_idx].record(cs)
         ds.wait_event(self.transferred_events[s_idx])
-        code = _DTYPE_CODE[self.layout.compute_dtype]
-        for qt, mid, arr, n in self._tasks[slot_idx]:
-            rc = self._lib.wf_dequant_gguf_batch(arr, n, qt, mid, code, ds.cuda_stream)
-            if rc:
-                _ext.check(rc, "wf_dequant_gguf_batch")
+        self.dequant_slot(slot_idx, ds)
         if prof is not None:
             prof.record(s_idx, "ready", ds)
         self.ready_events[s_idx].record(ds)
+
+    def dequant_slot(self, slot_idx, stream):
+        """The slot's GGUF weights from its packed bytes: one batched launch per (type, precision) on ``stream``."""
+        code = _DTYPE_CODE[self.layout.compute_dtype]
+        for qt, mid, arr, n in self._tasks[slot_idx]:
+            rc = self._lib.wf_dequant_gguf_batch(arr, n, qt, mid, code, stream.cuda_stream)
+            if rc:
+                _ext.check(rc, "wf_dequant_gguf_batch")
 
     def issue_prefetch(self, s_idx):
         """Transfer + dequantisation of block s_idx into its slot, after that slot's last reader finished."""
         if self.profiler is not None:
             self.profiler.mark(s_idx, "cpu_issue")
         with torch.cuda.device(self.device):
-            self.materialize(s_idx, self.slot_of(s_idx))
+            if self.host_flats[s_idx] is None:
+                self.uploader.submit(s_idx, self.slot_of(s_idx))  # SSD tier: the uploader thread copies
+            else:
+                self.materialize(s_idx, self.slot_of(s_idx))
         self.issued[s_idx] = True
 
     def begin_forward(self):
+        if self.uploader is not None and (self.uploader.outstanding() or self.uploader.error is not None
+                                          or not self.ring.at_cycle_start() or self.ring.failed()):
+            # the previous forward stopped part way: finish the uploads it queued, then restart the SSD read cycle
+            self.uploader.drain()
+            self.ring.restart_if_needed(lambda msg: print(f"[streaming] {msg}", flush=True))
+            self.uploader.error = None
         self.issued = [False] * self.num_stream
         if self.profiler is not None:
             self.profiler.begin_forward(torch.cuda.current_stream(self.device))
@@ -212,6 +235,8 @@ class _StreamState:
         prof = self.profiler
         if prof is not None:
             prof.record(s_idx, "wait0", compute)
+        if self.host_flats[s_idx] is None:
+            self.uploader.wait(s_idx)  # ready[s] is recorded by the uploader thread
         compute.wait_event(self.ready_events[s_idx])
         if prof is not None:
             prof.record(s_idx, "start", compute)
@@ -231,6 +256,16 @@ class _StreamState:
             self.issue_prefetch(nxt)
         if self.profiler is not None:
             self.profiler.add_cpu(time.perf_counter() - t0)
+
+    def close(self):
+        """Stop the SSD tier's threads (uploader, ring readers) and release its buffers."""
+        if self.uploader is not None:
+            self.uploader.drain()
+            self.uploader.close()
+            self.uploader = None
+        if self.ring is not None:
+            self.ring.close()
+            self.ring = None
 
     def profile_summary(self):
         return None if self.profiler is None else self.profiler.summary()

@@ -5,6 +5,8 @@ dequantisation is this package's patch. Un-streamed, every layer dequantises its
 dequantises each block once on arrival into its slot. Both must give the same bits, across forwards, slot counts,
 buffer modes and resident counts, and teardown must hand back a working resident model."""
 
+import os
+
 import numpy as np
 import pytest
 
@@ -28,7 +30,7 @@ def _packed(qt, n_values, rng):
     return raw.reshape(-1)
 
 
-def _dit(torch, seed=7, plain=False):
+def _dit(torch, seed=7, plain=False, n_blocks=N_BLOCKS):
     rng = np.random.default_rng(seed)
     F = torch.nn.functional
 
@@ -46,14 +48,19 @@ def _dit(torch, seed=7, plain=False):
                 self.down = fg.Linear(fg.gguf_param(_packed(12, DIM * HID, rng), 12, (DIM, HID), "cuda"),
                                       dequant_dtype="target")
 
+        fail = False  # set on one block to make its forward raise once (a forward interrupted part way)
+
         def forward(self, x):
+            if self.fail:
+                self.fail = False
+                raise RuntimeError("interrupted")
             h = F.layer_norm(x, (DIM,), weight=self.norm.weight.to(x.dtype))
             return x + self.down(F.gelu(self.up(h)))
 
     class DiT(torch.nn.Module):
         def __init__(self):
             super().__init__()
-            self.blocks = torch.nn.ModuleList([Block() for _ in range(N_BLOCKS)])
+            self.blocks = torch.nn.ModuleList([Block() for _ in range(n_blocks)])
 
         def forward(self, x):
             for b in self.blocks:
@@ -187,3 +194,40 @@ def test_streamed_plain_bf16_dit(cuda):
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
     dn.teardown(dit)
+
+
+@pytest.mark.parametrize("n_blocks,budget_blocks,slots", [(9, 6, 3), (5, 1, 2)])
+def test_streamed_gguf_dit_with_ssd_tier(gguf_patch, tmp_path, monkeypatch, n_blocks, budget_blocks, slots):
+    """tiering "Auto" with a RAM budget of a few blocks: the planner puts streamed blocks on the SSD (a cache file
+    read back every forward through the DiskRing and the uploader thread, which dequantises them); the result equals
+    the un-streamed model's bit for bit, forward after forward, and after a forward that stopped part way."""
+    import torch
+    dn = wf("streaming.dit_node")
+    monkeypatch.setenv("WEIGHTFERRY_DISK_DIR", str(tmp_path))
+    dit = _dit(torch, seed=13, n_blocks=n_blocks)
+    x = _x(torch)
+    specs, _ = dn.block_specs_of(dit.blocks[1])
+    flat = wf("streaming.state").BlockLayout(specs).flat_bytes
+    with torch.inference_mode():
+        ref = dit(x)
+        dn.WeightFerryDiT().apply_streaming(_Patcher(dit, torch), resident_blocks=1, prefetch_slots=slots,
+                                            tiering=dn.TIERING_AUTO, ram_budget_gb=budget_blocks * flat / 1024 ** 3)
+        st = dit._weightferry_stream_state
+        plan = st.tier_plan
+        assert plan["disk_blocks"] > 0 and st.ring.ring is not None and st.ring.uploader is not None
+        assert plan["ram_blocks"] + plan["disk_blocks"] == n_blocks - 1
+        assert os.path.exists(st.store.path) and len(st.disk_blocks) == plan["disk_blocks"]
+        outs = [dit(x) for _ in range(3)]
+        # a forward that stops part way, after the SSD tier's first blocks were queued
+        dit.blocks[n_blocks - 2].fail = True
+        with pytest.raises(RuntimeError, match="interrupted"):
+            dit(x)
+        outs += [dit(x) for _ in range(2)]
+        torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o, ref)
+    path = st.store.path
+    dn.teardown(dit)
+    assert not os.path.exists(path)
+    with torch.inference_mode():
+        assert torch.equal(dit(x), ref)
