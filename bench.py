@@ -193,6 +193,20 @@ def barrier(torch, dist):
 
 
 # ----------------------------------------------------------------------------------------------------- CPU baseline
+def host_threads():
+    """Host threads this process may use: the oracle's OpenMP pool is set to this explicitly, since a torchrun launch
+    sets OMP_NUM_THREADS=1."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def use_all_host_threads(oracle):
+    """Set the oracle's OpenMP thread count for the calling thread to host_threads(); returns it."""
+    return int(oracle.set_threads(host_threads()))
+
+
 def cpu_baseline_sweep(seconds=10.0):
     """The oracle port (oracle/wf_oracle.c, OpenMP, all host threads) on one BASELINE configs[1] weight, Q4_K
     5120x13824 -> bf16 (mid float16), repeated for about `seconds`. Returns (out GB/s, threads, sample text)."""
@@ -202,7 +216,7 @@ def cpu_baseline_sweep(seconds=10.0):
     nb = n // 256
     raw = rng.integers(0, 256, size=(nb, Q4K_TS), dtype=np.uint8)
     raw[:, 0:4] = (rng.uniform(0, 0.01, (nb, 2)).astype(np.float16)).view(np.uint8)
-    threads = oracle.max_threads()
+    threads = use_all_host_threads(oracle)
     oracle.dequant_gguf(raw, n, 12, 0, 1)  # warm-up (page faults, thread pool)
     reps, t0 = 0, time.perf_counter()
     while True:
@@ -495,6 +509,8 @@ def cpu_baseline_w8a8(seconds=10.0):
     ws = (w_fp.abs().amax(dim=1) / 127.0).double()
     wq = torch.clamp(torch.round(w_fp / ws.float().view(-1, 1)), -127, 127).double()
     xb = x.view(torch.int16).numpy().view(np.uint16)
+    use_all_host_threads(oracle)
+    torch.set_num_threads(host_threads())
     reps, t0 = 0, time.perf_counter()
     while True:
         q, sc = oracle.quant_rows(xb, pre=0, rotate=False)
@@ -639,7 +655,7 @@ def cpu_baseline_stack(seconds=10.0):
 
 def finish_stack(torch, args, world, rank, dist, r):
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, threads, sample = cpu_baseline_stack(args.cpu_seconds)
         cpu = {"value": round(v, 2), "unit": "s/step", "cores": threads, "kind": "port", "sample": sample}
     if dist is not None:
@@ -757,6 +773,7 @@ def cpu_baseline_prologue(seconds=10.0):
     q = torch.randn((1, 32, 16, 128), generator=g).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     f = cb.rope3d_table(1, 64, 64).numpy()[:, :32]
     w = np.ones(128, dtype=np.float32)
+    threads = use_all_host_threads(oracle)
     reps, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds:
         oracle.ln_modulate(x, s1, sh, 512, 1e-6)
@@ -765,7 +782,7 @@ def cpu_baseline_prologue(seconds=10.0):
         reps += 1
     el = time.perf_counter() - t0
     nbytes = reps * (2 * 512 * 2048 * 2 + 2 * 2 * 32 * 16 * 128 * 2)
-    return nbytes / el / 1e9, oracle.max_threads(), f"{reps} x (512 rows of kernel A + 32 tokens of kernel B on q, k)"
+    return nbytes / el / 1e9, threads, f"{reps} x (512 rows of kernel A + 32 tokens of kernel B on q, k)"
 
 
 def finish_prologue(torch, args, world, rank, dist, r):
@@ -773,7 +790,7 @@ def finish_prologue(torch, args, world, rank, dist, r):
     a_rate = r["bytes_a"] / (r["a_ms"] / 1e3) / 1e9
     b_rate = r["bytes_b"] / (r["b_ms"] / 1e3) / 1e9
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, threads, sample = cpu_baseline_prologue(args.cpu_seconds)
         cpu = {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample}
     if dist is not None:
@@ -890,7 +907,7 @@ def main():
     achieved = r["alg_bytes_per_launch"] / (r["kern_ms"] / 1e3) / 1e9
     traffic = NCU_TRAFFIC.get(args.workload)
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline and args.workload in ("sweep", "q4k"):
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("sweep", "q4k"):
         gbs, threads, sample = cpu_baseline_sweep(args.cpu_seconds)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample}
     if dist is not None:
@@ -934,7 +951,7 @@ def finish_w8a8(torch, args, world, rank, dist, r):
     peak, src = measured_int8_peak()
     achieved = r["alg_ops_per_launch"] / (r["kern_ms"] / 1e3) / 1e12
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, threads, sample = cpu_baseline_w8a8(args.cpu_seconds)
         cpu = {"value": round(v, 4), "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample}
     if dist is not None:
@@ -974,7 +991,7 @@ def run_reference(args):
         raw = rng.integers(0, 256, size=(nb, Q4K_TS), dtype=np.uint8)
         raw[:, 0:4] = (rng.uniform(0, 0.01, (nb, 2)).astype(np.float16)).view(np.uint8)
         raws.append((raw, a * b))
-    threads = oracle.max_threads()
+    threads = use_all_host_threads(oracle)
 
     def step():
         for raw, n in raws:

@@ -54,6 +54,8 @@ def lib():
         L.wfo_quant_rows.restype = None
         L.wfo_max_threads.argtypes = []
         L.wfo_max_threads.restype = i32
+        L.wfo_set_threads.argtypes = [i32]
+        L.wfo_set_threads.restype = i32
         _lib = L
     return _lib
 
@@ -64,6 +66,11 @@ def _ptr(a):
 
 def max_threads():
     return lib().wfo_max_threads()
+
+
+def set_threads(n):
+    """OpenMP threads of the oracle's parallel loops on the calling thread; returns the count now in effect."""
+    return lib().wfo_set_threads(int(n))
 
 
 def dequant_gguf(raw, n_values, qtype, mid, out, diff=None, sa=0.0, threads=0):

@@ -217,6 +217,7 @@ WFO_API int wfo_lora_add(const float *diff, void *w, int64_t n, int out, float s
 }
 
 WFO_API int wfo_max_threads(void) { return set_threads(0); }
+WFO_API int wfo_set_threads(int threads) { return set_threads(threads); }
 
 /* ================================================================================================ fused block */
 static inline float bf(uint16_t b) { return u2f((uint32_t)b << 16); }
