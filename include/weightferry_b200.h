@@ -122,8 +122,8 @@ WF_API int wf_quant_rows(const void *x, const void *s1, const void *shift, const
 
 /* Measurement helper of the benchmark (no reference counterpart): one streaming pass that reads in_bytes and writes
  * out_bytes (both multiples of 16, 16-byte aligned, each below 32 GiB, in_bytes <= out_bytes) with coalesced 16-byte
- * accesses, each input
- * byte read from DRAM once: the HBM rate a plain kernel reaches for the dequantisation's read : write mix. */
+ * accesses, each input byte read from DRAM once: the HBM rate a plain kernel reaches for the dequantisation's
+ * read : write mix. */
 WF_API int wf_hbm_probe(const void *in, int64_t in_bytes, void *out, int64_t out_bytes, wf_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------- W8A8 linear */
