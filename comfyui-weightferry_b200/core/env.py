@@ -25,6 +25,7 @@ DEFAULTS = {
     "WEIGHTFERRY_DISK_DIR": None,          # folder of the SSD tier's cache files (None: ComfyUI's / the system temp)
     "WEIGHTFERRY_DISK_THREADS": None,      # SSD reader threads (None: the probe's fastest count)
     "WEIGHTFERRY_SSD_LAYOUT": "interleave",  # which streamed blocks go to the SSD: interleave / tail
+    "WEIGHTFERRY_TP_CHUNKS": "1",          # row chunks of the tensor-parallel stack's overlapped sub-layers (1: off)
     "WEIGHTFERRY_SETTINGS_FILE": None,
 }
 

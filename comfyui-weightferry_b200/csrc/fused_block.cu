@@ -81,6 +81,32 @@ __global__ void __launch_bounds__(256) modulate_kernel(const uint4 *__restrict__
     }
 }
 
+// ------------------------------------------------------------------------------------------------- gated residual
+// out = bf16_rn(x + f32(gate * o)) -- PyTorch's bf16 addcmul(x, gate, o) (one float32 product, one float32 sum, one
+// rounding), the block's residual update (fused_block.py:527-532 _add_residual). gate row (row / rows_per_group),
+// 8 values per thread, grid-stride; out may be x. d % 8 == 0.
+__global__ void __launch_bounds__(256) gated_residual_kernel(const uint4 *__restrict__ x,
+                                                             const __nv_bfloat16 *__restrict__ gate,
+                                                             const uint4 *__restrict__ o, uint4 *out, int64_t n_vec,
+                                                             int64_t d, int64_t rows_per_group) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_vec; i += stride) {
+        const int64_t e = i * 8;
+        const int64_t row = e / d, col = e - row * d;
+        const uint4 xv = x[i];  // plain load: out may alias x
+        const uint4 ov = __ldg(o + i);
+        const uint4 gv = __ldg(reinterpret_cast<const uint4 *>(gate + (row / rows_per_group) * d + col));
+        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, os[4] = {ov.x, ov.y, ov.z, ov.w},
+                       gs[4] = {gv.x, gv.y, gv.z, gv.w};
+        uint32_t r[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            r[k] = pack2(__fadd_rn(bf_lo(xs[k]), __fmul_rn(bf_lo(gs[k]), bf_lo(os[k]))),
+                         __fadd_rn(bf_hi(xs[k]), __fmul_rn(bf_hi(gs[k]), bf_hi(os[k]))));
+        out[i] = make_uint4(r[0], r[1], r[2], r[3]);
+    }
+}
+
 // ------------------------------------------------------------------------------------------------- Welford
 struct Welford {
     float m, s, c;
@@ -796,6 +822,20 @@ extern "C" WF_API int wf_modulate(const void *x, const void *s1, const void *shi
     modulate_kernel<<<grid_for(n_vec, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint4 *>(x), static_cast<const __nv_bfloat16 *>(s1),
         static_cast<const __nv_bfloat16 *>(shift), static_cast<uint4 *>(out), n_vec, d, rows_per_group);
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" WF_API int wf_gated_residual(const void *x, const void *gate, const void *o, void *out, int64_t rows,
+                                        int64_t d, int64_t rows_per_group, wf_stream_t stream) {
+    if (rows < 0 || d <= 0 || rows_per_group <= 0 || d % 8 != 0) return WF_ERR_ARG;
+    if (rows == 0) return WF_OK;
+    if (!x || !gate || !o || !out || !al(x, 16) || !al(gate, 16) || !al(o, 16) || !al(out, 16)) return WF_ERR_ARG;
+    int rc = check_device();
+    if (rc != WF_OK) return rc;
+    const int64_t n_vec = rows * d / 8;
+    gated_residual_kernel<<<grid_for(n_vec, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4 *>(x), static_cast<const __nv_bfloat16 *>(gate), static_cast<const uint4 *>(o),
+        static_cast<uint4 *>(out), n_vec, d, rows_per_group);
     return static_cast<int>(cudaGetLastError());
 }
 

@@ -17,6 +17,7 @@ ComfyUI is present; the block body itself (adaLN chunks, the three sub-layers, t
 
 import torch
 
+from .. import _ext
 from ..core import env as _env
 from ..utils.logging import log_info, log_warn
 from .fused_kernels import _get_kernels, _kernels  # noqa: F401 -- re-exported like the reference
@@ -68,6 +69,30 @@ def modulate(normed, scale, shift):
     out = torch.empty_like(normed)
     _get_kernels()["mod"][(B * T * H * W,)](normed, one_plus, shift.contiguous(), out, D, H * W)
     return out
+
+
+def gated_residual(x, gate_rows, o, rows_per_group, out=None):
+    """x + gate * o for (n, D) rows x and o, the gate row of row r being gate_rows[r // rows_per_group] -- ComfyUI's
+    bf16 addcmul (the block's _add_residual, reference :527-532) in one vectorised kernel with the same bits; out may
+    be x. Other dtypes / layouts take PyTorch's addcmul."""
+    n, D = x.shape
+    if (x.dtype == torch.bfloat16 and o.dtype == torch.bfloat16 and gate_rows.dtype == torch.bfloat16 and x.is_cuda
+            and x.is_contiguous() and o.is_contiguous() and gate_rows.is_contiguous() and D % 8 == 0
+            and tuple(o.shape) == (n, D) and gate_rows.shape[-1] == D and rows_per_group > 0
+            and gate_rows.shape[0] * rows_per_group >= n):
+        if out is None:
+            out = torch.empty_like(x)
+        with torch.cuda.device(x.device):
+            rc = _ext.lib().wf_gated_residual(x.data_ptr(), gate_rows.data_ptr(), o.data_ptr(), out.data_ptr(), n, D,
+                                              int(rows_per_group), _ext.stream_of(x.device))
+        _ext.check(rc, "wf_gated_residual")
+        return out
+    g = gate_rows.repeat_interleave(rows_per_group, dim=0)[:n]
+    res = torch.addcmul(x, g.to(x.dtype), o.to(x.dtype))
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res
 
 
 def rms_norm_128(x, weight, eps, rs=0):

@@ -24,6 +24,8 @@ weights, 4 % of the bytes, are replicated). Parameter names follow ComfyUI's mod
 import torch
 import torch.nn.functional as F
 
+from ..core import env as _env
+
 from ..enhancers import fused_block as _fb
 from ..enhancers import sage_fused as _sf
 from .state import ParamSpec
@@ -189,6 +191,78 @@ class TP:
         self.dist.all_gather_into_tensor(out, x_local, group=self.group)
         return out
 
+    # -------------------------------------------------------------------- overlapped row chunks (NCCL's own stream)
+    def chunks(self, n):
+        """Row chunks of the overlapped sub-layers: WEIGHTFERRY_TP_CHUNKS when it divides n, else 1. Off (1) by
+        default: at 2 GPUs the overlap made a block slower (3.61 against 3.47 ms), NCCL's ring kernels taking SMs from
+        the concurrent GEMMs, and the chunked GEMMs being smaller."""
+        c = int(_env.get("WEIGHTFERRY_TP_CHUNKS"))
+        return c if self.world > 1 and c > 1 and n % c == 0 else 1
+
+    def _gather_async(self, x_local):
+        """(buffer of every rank's rows in rank order, work or None); NCCL runs it on its own stream."""
+        x_local = x_local.contiguous()
+        if self.gloo:
+            return self.all_gather_rows(x_local), None
+        out = torch.empty((x_local.shape[0] * self.world,) + tuple(x_local.shape[1:]), dtype=x_local.dtype,
+                          device=x_local.device)
+        return out, self.dist.all_gather_into_tensor(out, x_local, group=self.group, async_op=True)
+
+    def _scatter_async(self, out_rows, x_full):
+        """out_rows <- this rank's rows of the sum over ranks of x_full; returns the work (None when done)."""
+        if self.gloo:
+            out_rows.copy_(self.reduce_scatter_rows(x_full))
+            return None
+        return self.dist.reduce_scatter_tensor(out_rows, x_full.contiguous(), group=self.group, async_op=True)
+
+    def mlp_rows(self, normed_rows, w1, w2):
+        """reduce_scatter_rows(layer2(gelu(layer1(all_gather_rows(normed_rows))))) in row chunks: chunk c takes rows
+        [c * m, (c + 1) * m) of every rank (rank-major, so the chunked all-gather / reduce-scatter compose as the
+        whole ones do); the all-gather of chunk c + 1 and the reduce-scatter of chunk c run on NCCL's stream while
+        the compute stream does chunk c's and c + 1's GEMMs."""
+        n = normed_rows.shape[0]
+        C = self.chunks(n)
+        if C == 1:
+            return self.reduce_scatter_rows(F.linear(F.gelu(F.linear(self.all_gather_rows(normed_rows), w1)), w2))
+        m = n // C
+        out = torch.empty((n, w2.shape[0]), dtype=normed_rows.dtype, device=normed_rows.device)
+        gathered = [self._gather_async(normed_rows[0:m])]
+        pending = []
+        for c in range(C):
+            if c + 1 < C:
+                gathered.append(self._gather_async(normed_rows[(c + 1) * m:(c + 2) * m]))
+            buf, work = gathered[c]
+            if work is not None:
+                work.wait()
+            y = F.linear(F.gelu(F.linear(buf, w1)), w2)
+            gathered[c] = None
+            pending.append((self._scatter_async(out[c * m:(c + 1) * m], y), y))
+        for work, _y in pending:
+            if work is not None:
+                work.wait()
+        return out
+
+    def row_parallel_rows(self, a_full, w):
+        """reduce_scatter_rows(linear(a_full, w)) for a_full in natural row order (world * n rows), in row chunks:
+        chunk c is rows [c * m, (c + 1) * m) of every rank's share; its reduce-scatter runs on NCCL's stream while
+        the next chunk's GEMM runs."""
+        n = a_full.shape[0] // self.world
+        C = self.chunks(n)
+        if C == 1:
+            return self.reduce_scatter_rows(F.linear(a_full, w))
+        m = n // C
+        K = a_full.shape[1]
+        parts = a_full.view(self.world, C, m, K)
+        out = torch.empty((n, w.shape[0]), dtype=a_full.dtype, device=a_full.device)
+        pending = []
+        for c in range(C):
+            y = F.linear(parts[:, c], w).reshape(self.world * m, w.shape[0])
+            pending.append((self._scatter_async(out[c * m:(c + 1) * m], y), y))
+        for work, _y in pending:
+            if work is not None:
+                work.wait()
+        return out
+
     def reduce_scatter_rows(self, x_full):
         """Sum over ranks of (world * R, ...) -> this rank's (R, ...) rows."""
         if self.world == 1:
@@ -220,14 +294,14 @@ def _ln_mod_rows(x_rows, scale_b, shift_b, row0, rows_per_batch, eps):
 
 
 def _residual(x_rows, gate_b, o, row0, rows_per_batch):
-    """x + gate * o on the shard's rows (ComfyUI's torch.addcmul), gate_b (B, D) broadcast over each batch's rows."""
+    """x + gate * o on the shard's rows (ComfyUI's addcmul, the bits of enhancers/fused_block.gated_residual), gate_b
+    (B, D) broadcast over each batch's rows."""
     n, D = x_rows.shape
     b0 = row0 // rows_per_batch
     if n >= rows_per_batch:
         nb = n // rows_per_batch
-        return torch.addcmul(x_rows.view(nb, rows_per_batch, D), gate_b[b0:b0 + nb].view(nb, 1, D),
-                             o.view(nb, rows_per_batch, D)).view(n, D)
-    return torch.addcmul(x_rows, gate_b[b0:b0 + 1], o)
+        return _fb.gated_residual(x_rows, gate_b[b0:b0 + nb].contiguous(), o.contiguous(), rows_per_batch)
+    return _fb.gated_residual(x_rows, gate_b[b0:b0 + 1].contiguous(), o.contiguous(), n)
 
 
 def _attention(q, k, v):
@@ -265,7 +339,7 @@ def block_forward(x_rows, emb, ctx, rope, W, cfg, tp, batch, tokens, lora_term=N
     q = _sf.rms_rope(q, rope, W["self_attn.q_norm.weight"], eps)
     k = _sf.rms_rope(k, rope, W["self_attn.k_norm.weight"], eps)
     a = _attention(q, k, v).view(batch * tokens, Hw * hd)
-    o = tp.reduce_scatter_rows(F.linear(a, W["self_attn.output_proj.weight"]))              # (n, D)
+    o = tp.row_parallel_rows(a, W["self_attn.output_proj.weight"])                          # (n, D)
     x_rows = _residual(x_rows, gate, o, row0, tokens)
 
     # --- cross-attention
@@ -278,14 +352,13 @@ def block_forward(x_rows, emb, ctx, rope, W, cfg, tp, batch, tokens, lora_term=N
     kc = _fb.rms_norm_128(kc.contiguous(), W["cross_attn.k_norm.weight"], eps)
     vc = F.linear(ctx, W["cross_attn.v_proj.weight"]).view(batch, S, Hw, hd)
     a = _attention(q, kc, vc).view(batch * tokens, Hw * hd)
-    o = tp.reduce_scatter_rows(F.linear(a, W["cross_attn.output_proj.weight"]))
+    o = tp.row_parallel_rows(a, W["cross_attn.output_proj.weight"])
     x_rows = _residual(x_rows, gate, o, row0, tokens)
 
     # --- MLP
     shift, scale, gate = adaln(W, "mlp", emb, lora_term)
-    normed = tp.all_gather_rows(_ln_mod_rows(x_rows, scale, shift, row0, tokens, eps))
-    h = F.gelu(F.linear(normed, W["mlp.layer1.weight"]))
-    o = tp.reduce_scatter_rows(F.linear(h, W["mlp.layer2.weight"]))
+    o = tp.mlp_rows(_ln_mod_rows(x_rows, scale, shift, row0, tokens, eps), W["mlp.layer1.weight"],
+                    W["mlp.layer2.weight"])
     return _residual(x_rows, gate, o, row0, tokens)
 
 

@@ -92,6 +92,13 @@ WF_API int wf_lora_add(const float *diff, void *w, int64_t n_values, int out, fl
 WF_API int wf_modulate(const void *x, const void *s1, const void *shift, void *out, int64_t rows, int64_t d,
                        int64_t rows_per_group, wf_stream_t stream);
 
+/* Gated residual update out[r, c] = bf16_rn(x[r, c] + f32(gate[r / rows_per_group, c] * o[r, c])) on bf16 [rows, d]
+ * (d % 8 == 0, all pointers 16-byte aligned; out may be x): PyTorch's bf16 addcmul(x, gate, o) with the same bits, in
+ * one vectorised pass. Replaces the block's residual addcmul (enhancers/fused_block.py:527-532, _add_residual) where
+ * the residual is not folded into an int8 GEMM's epilogue. */
+WF_API int wf_gated_residual(const void *x, const void *gate, const void *o, void *out, int64_t rows, int64_t d,
+                             int64_t rows_per_group, wf_stream_t stream);
+
 /* LayerNorm (no affine, PyTorch's vectorized Welford order) + modulate in one pass over rows of K (K % 512 == 0,
  * K <= 8192): x = R16((x - mean) * rsqrt(var + eps)); out = R16(R16(x * s1) + shift). Replaces ln_modulate()'s
  * launch (enhancers/fused_block.py:165-179, kernel _lnmod fused_kernels.py:219-232). */

@@ -294,3 +294,24 @@ def test_quant_rows_register_kernel_matches_shared_kernel(cuda, pre, k):
     assert torch.equal(outs[0][1].view(torch.int32), outs[1][1].view(torch.int32))
     if pre != 2:                                                      # (with modulate the row becomes the shift)
         assert float(outs[0][1][3]) == pytest.approx(1e-30)
+
+
+@pytest.mark.parametrize("n,D,rpg", [(4096, 5120, 4096), (300, 1024, 7), (8192, 2048, 4096), (8, 8, 1)])
+def test_gated_residual_equals_addcmul(cuda, n, D, rpg):
+    """wf_gated_residual (the block's residual update) gives PyTorch's bf16 addcmul bit for bit, also in place."""
+    import torch
+    fb = wf("enhancers.fused_block")
+    g = torch.Generator(device="cuda").manual_seed(n + D)
+    x = torch.randn((n, D), device="cuda", generator=g).to(torch.bfloat16)
+    o = (torch.randn((n, D), device="cuda", generator=g) * 3).to(torch.bfloat16)
+    groups = (n + rpg - 1) // rpg
+    gate = (torch.randn((groups, D), device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    want = torch.addcmul(x, gate.repeat_interleave(rpg, dim=0)[:n], o)
+    got = fb.gated_residual(x, gate, o, rpg)
+    inplace = x.clone()
+    fb.gated_residual(inplace, gate, o, rpg, out=inplace)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want) and torch.equal(inplace, want)
+    if n % rpg == 0:   # the block's broadcast form
+        b = n // rpg
+        assert torch.equal(torch.addcmul(x.view(b, rpg, D), gate.view(b, 1, D), o.view(b, rpg, D)).view(n, D), want)

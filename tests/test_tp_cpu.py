@@ -1,5 +1,6 @@
 """The multi-rank host logic on CPU with gloo (world size 2): the TP group's all-gather / reduce-scatter of token
-rows, a column / row split of a two-layer MLP combined through them equals the unsplit product, and the sweep's
+rows, a column / row split of a two-layer MLP combined through them equals the unsplit product (also in the
+overlapped row-chunk forms mlp_rows / row_parallel_rows at 1, 2 and 4 chunks), and the sweep's
 tensor bin-packing gives every rank a disjoint share whose union is the whole table."""
 
 import os
@@ -35,6 +36,27 @@ def _worker(rank, world, port, q):
         y_local = tp.reduce_scatter_rows(part)
         ref = (x @ w1.t() @ w2.t())[rank * rows:(rank + 1) * rows]
         ok = torch.allclose(y_local, ref, rtol=1e-12, atol=1e-9) and torch.equal(full_x, x)
+        # the overlapped row-chunk forms (NCCL async on GPUs; the same chunk algebra here) equal the whole ones
+        F = torch.nn.functional
+        xx = torch.randn(16, 16, generator=g, dtype=torch.float64)
+        aa = torch.randn(16, 32, generator=g, dtype=torch.float64)
+        wo = torch.randn(16, 32, generator=g, dtype=torch.float64)
+        r16 = 16 // world
+        xl = xx[rank * r16:(rank + 1) * r16]
+        w1s, w2s = w1[rank * 16:(rank + 1) * 16], w2[:, rank * 16:(rank + 1) * 16]
+        ks = slice(rank * 32 // world, (rank + 1) * 32 // world)
+        want_mlp = (F.gelu(xx @ w1.t()) @ w2.t())[rank * r16:(rank + 1) * r16]
+        want_row = (aa @ wo.t())[rank * r16:(rank + 1) * r16]
+        for chunks in ("1", "2", "4"):
+            os.environ["WEIGHTFERRY_TP_CHUNKS"] = chunks
+            assert tp.chunks(r16) == int(chunks)
+            got_mlp = tp.mlp_rows(xl, w1s, w2s)
+            got_row = tp.row_parallel_rows(aa[:, ks].contiguous(), wo[:, ks].contiguous())
+            ok = ok and torch.allclose(got_mlp, want_mlp, rtol=1e-12, atol=1e-9)
+            ok = ok and torch.allclose(got_row, want_row, rtol=1e-12, atol=1e-9)
+        os.environ["WEIGHTFERRY_TP_CHUNKS"] = "3"
+        ok = ok and tp.chunks(r16) == 1               # a count that does not divide the rows: unchunked
+        os.environ.pop("WEIGHTFERRY_TP_CHUNKS")
         bench = importlib.import_module("bench")
         table = [s for _ in range(36 * world) for s in bench.cosmos14b_block_shapes()]
         sizes = [a * b for a, b in table]

@@ -33,14 +33,19 @@ def main():
     rows = batch * tokens // world
     stack = stk.StreamedStack(cfg, 3, "cuda", tp, seed=77, num_slots=2)
     out = stack.forward(x[rank * rows:(rank + 1) * rows].contiguous(), emb, ctx, rope, batch, tokens, lora)
+    # the same forward with the overlapped row chunks (WEIGHTFERRY_TP_CHUNKS=4): only GEMM shapes differ
+    os.environ["WEIGHTFERRY_TP_CHUNKS"] = "4"
+    chunked = stack.forward(x[rank * rows:(rank + 1) * rows].contiguous(), emb, ctx, rope, batch, tokens, lora)
+    os.environ.pop("WEIGHTFERRY_TP_CHUNKS")
+    chunk_err = ((chunked.float() - out.float()).norm() / out.float().norm()).item()
     full = tp.all_gather_rows(out)
     ok = torch.ones(1, device="cuda")
     if rank == 0:
         single = stk.StreamedStack(cfg, 3, "cuda", cb.TP(single=True), seed=77, num_slots=2)
         ref = single.forward(x, emb, ctx, rope, batch, tokens, lora)
         err = ((full.float() - ref.float()).norm() / ref.float().norm()).item()
-        print(f"tp{world} vs single-GPU relative L2 error {err:.3e}", flush=True)
-        if not (err < 2e-2 and torch.isfinite(full.float()).all()):
+        print(f"tp{world} vs single-GPU relative L2 error {err:.3e}; row chunks vs none {chunk_err:.3e}", flush=True)
+        if not (err < 2e-2 and chunk_err < 1e-2 and torch.isfinite(full.float()).all()):
             ok.zero_()
         single.close()
     dist.broadcast(ok, 0)
