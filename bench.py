@@ -553,6 +553,8 @@ def run_stack(torch, args, world, rank, dist):
     tp = cb.TP()
     batch, T, H, W, S = 2, 1, 64, 64, 512
     tokens = T * H * W
+    # each rank's pinned weights on its GPU's NUMA node (first touch after binding): no cross-socket DMA
+    numa_cpus = _pkg("core.tiers.pinned").bind_to_gpu_numa(dev.index) if world > 1 else None
     probe = h2d_probe(torch, dev)
     t_build = time.perf_counter()
     stack = stk.StreamedStack(cfg, args.blocks, dev, tp, seed=20261201 + 4, num_slots=args.slots)
@@ -616,7 +618,7 @@ def run_stack(torch, args, world, rank, dist):
     stack.close()
     return {"ms": ms, "clk": clk.summary(), "e2e": e2e, "finite": finite, "probe": probe, "h2d_rate": h2d_rate,
             "h2d_rank": h2d_rank, "flops": flops, "summary": summ, "build_s": build_s,
-            "slots": stack.state.num_slots}
+            "slots": stack.state.num_slots, "numa_cpus": None if numa_cpus is None else len(numa_cpus)}
 
 
 def cpu_baseline_stack(seconds=10.0):
@@ -673,6 +675,7 @@ def finish_stack(torch, args, world, rank, dist, r):
                        "parallelism": f"tp{world} (column/row split, sequence-sharded residual)",
                        "h2d_bytes_per_block_per_rank": r["h2d_rank"] // args.blocks,
                        "h2d_probe_gbs_per_rank": round(r["probe"], 2), "finite_output": r["finite"],
+                       "numa_local_cpus_per_rank": r.get("numa_cpus"),
                        "build_s": round(r["build_s"], 1),
                        "timeline_one_forward": r["summary"]},
             "roofline": {"bound": "pcie_h2d", "achieved": round(r["h2d_rate"], 2), "peak": round(r["probe"], 2),

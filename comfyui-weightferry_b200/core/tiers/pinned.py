@@ -63,6 +63,45 @@ class PinnedHost:
             pass
 
 
+def gpu_local_cpus(device_index, nvml=None):
+    """The CPUs on the NUMA node of CUDA device ``device_index`` (NVML's CPU affinity of the GPU found by its PCI bus
+    id, so CUDA_VISIBLE_DEVICES renumbering does not matter), or None when NVML cannot tell."""
+    try:
+        if nvml is None:
+            import pynvml as nvml
+        props = torch.cuda.get_device_properties(device_index)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        nvml.nvmlInit()
+        try:
+            h = nvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = nvml.nvmlDeviceGetCpuAffinity(h, 16)   # 16 x 64 CPUs
+        finally:
+            nvml.nvmlShutdown()
+    except Exception:  # noqa: BLE001 -- no NVML, no such device: leave the affinity alone
+        return None
+    cpus = [64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1]
+    return cpus or None
+
+
+def bind_to_gpu_numa(device_index, nvml=None):
+    """Restrict this process to the CPUs local to the GPU, so that pinned host buffers allocated (first touched) from
+    now on live on the GPU's NUMA node and its host-to-device copies do not cross sockets. Returns the CPUs bound,
+    or None (left unchanged)."""
+    import os
+    cpus = gpu_local_cpus(device_index, nvml)
+    if not cpus:
+        return None
+    try:
+        allowed = os.sched_getaffinity(0)
+        mine = sorted(set(cpus) & allowed)
+        if not mine:
+            return None
+        os.sched_setaffinity(0, mine)
+        return mine
+    except (AttributeError, OSError):
+        return None
+
+
 def release_all(holders):
     for h in holders or ():
         if h is not None:

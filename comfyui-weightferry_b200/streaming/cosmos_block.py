@@ -45,7 +45,9 @@ COSMOS_2B = CosmosConfig(hidden=2048, heads=16, mlp=8192)
 
 def block_specs(cfg, world=1, rank=0, qtype=Q8_0):
     """ParamSpecs of this rank's share of one block: column-parallel projections split their output rows,
-    row-parallel ones their input columns; adaLN and norm weights replicated."""
+    row-parallel ones their input columns, the adaLN output layers (3 D outputs) their output rows too (each rank
+    computes its slice of shift / scale / gate and the (B, 3 D) result is gathered: a few KB instead of streaming the
+    whole layer to every rank); the adaLN input layers and the norm weights are replicated."""
     if cfg.heads % world or cfg.mlp % world or cfg.hidden % world:
         raise ValueError(f"{world} ranks do not divide heads {cfg.heads} / mlp {cfg.mlp}")
     D, Dw, Mw = cfg.hidden, cfg.hidden // world, cfg.mlp // world
@@ -61,7 +63,7 @@ def block_specs(cfg, world=1, rank=0, qtype=Q8_0):
     s.append(ParamSpec("mlp.layer2.weight", (D, Mw), qtype=qtype))
     for sub in ("self_attn", "cross_attn", "mlp"):
         s.append(ParamSpec(f"adaln_modulation_{sub}.1.weight", (cfg.lora, D), qtype=qtype))
-        s.append(ParamSpec(f"adaln_modulation_{sub}.2.weight", (3 * D, cfg.lora), qtype=qtype))
+        s.append(ParamSpec(f"adaln_modulation_{sub}.2.weight", (3 * D // world, cfg.lora), qtype=qtype))
     for sub in ("self_attn", "cross_attn"):
         s.append(ParamSpec(f"{sub}.q_norm.weight", (cfg.head_dim,), dtype=torch.bfloat16))
         s.append(ParamSpec(f"{sub}.k_norm.weight", (cfg.head_dim,), dtype=torch.bfloat16))
@@ -73,7 +75,7 @@ def shard_of(name, world, rank):
     of the full dimension as rank / world), or None (replicated)."""
     if world == 1:
         return None
-    if name.endswith(("q_proj.weight", "k_proj.weight", "v_proj.weight", "mlp.layer1.weight")):
+    if name.endswith(("q_proj.weight", "k_proj.weight", "v_proj.weight", "mlp.layer1.weight", ".2.weight")):
         return ("col", rank, world)
     if name.endswith(("output_proj.weight", "mlp.layer2.weight")):
         return ("row", rank, world)
@@ -311,11 +313,14 @@ def _attention(q, k, v):
     return o.transpose(1, 2).reshape(B, L, H * d)
 
 
-def adaln(W, sub, emb, lora_term):
-    """(shift, scale, gate), each (B, D), of one sub-layer: Linear(Linear(SiLU(emb))) + AdaLN-LoRA term."""
+def adaln(W, sub, emb, lora_term, tp=None):
+    """(shift, scale, gate), each (B, D), of one sub-layer: Linear(Linear(SiLU(emb))) + AdaLN-LoRA term. Under
+    tensor parallelism the output layer holds this rank's 3 D / world outputs: the (B, 3 D) result is gathered."""
     h = F.linear(F.silu(emb), W[f"adaln_modulation_{sub}.1.weight"])
-    m = F.linear(h, W[f"adaln_modulation_{sub}.2.weight"]) + lora_term
-    return m.chunk(3, dim=-1)
+    m = F.linear(h, W[f"adaln_modulation_{sub}.2.weight"])
+    if tp is not None and tp.world > 1:
+        m = tp.all_gather_rows(m.t().contiguous()).t()
+    return (m + lora_term).chunk(3, dim=-1)
 
 
 def block_forward(x_rows, emb, ctx, rope, W, cfg, tp, batch, tokens, lora_term=None):
@@ -331,7 +336,7 @@ def block_forward(x_rows, emb, ctx, rope, W, cfg, tp, batch, tokens, lora_term=N
     eps = cfg.eps
 
     # --- self-attention
-    shift, scale, gate = adaln(W, "self_attn", emb, lora_term)
+    shift, scale, gate = adaln(W, "self_attn", emb, lora_term, tp)
     normed = tp.all_gather_rows(_ln_mod_rows(x_rows, scale, shift, row0, tokens, eps))       # (B*L, D)
     q = F.linear(normed, W["self_attn.q_proj.weight"]).view(batch, tokens, Hw, hd)
     k = F.linear(normed, W["self_attn.k_proj.weight"]).view(batch, tokens, Hw, hd)
@@ -343,7 +348,7 @@ def block_forward(x_rows, emb, ctx, rope, W, cfg, tp, batch, tokens, lora_term=N
     x_rows = _residual(x_rows, gate, o, row0, tokens)
 
     # --- cross-attention
-    shift, scale, gate = adaln(W, "cross_attn", emb, lora_term)
+    shift, scale, gate = adaln(W, "cross_attn", emb, lora_term, tp)
     normed = tp.all_gather_rows(_ln_mod_rows(x_rows, scale, shift, row0, tokens, eps))
     q = F.linear(normed, W["cross_attn.q_proj.weight"]).view(batch, tokens, Hw, hd)
     q = _fb.rms_norm_128(q.contiguous(), W["cross_attn.q_norm.weight"], eps)
@@ -356,7 +361,7 @@ def block_forward(x_rows, emb, ctx, rope, W, cfg, tp, batch, tokens, lora_term=N
     x_rows = _residual(x_rows, gate, o, row0, tokens)
 
     # --- MLP
-    shift, scale, gate = adaln(W, "mlp", emb, lora_term)
+    shift, scale, gate = adaln(W, "mlp", emb, lora_term, tp)
     o = tp.mlp_rows(_ln_mod_rows(x_rows, scale, shift, row0, tokens, eps), W["mlp.layer1.weight"],
                     W["mlp.layer2.weight"])
     return _residual(x_rows, gate, o, row0, tokens)

@@ -68,3 +68,32 @@ def test_pinned_host_holder_exact_size():
     h.tensor.fill_(7)
     h.release()
     assert h.tensor is None
+
+
+def test_gpu_numa_binding_with_a_fake_nvml(monkeypatch):
+    """bind_to_gpu_numa takes the GPU's NVML CPU affinity (bitmask words) and restricts the process to the CPUs it
+    may use among them; without NVML it leaves the affinity alone."""
+    import os
+    import types
+    import torch
+    pinned = wf("core.tiers.pinned")
+    allowed = sorted(os.sched_getaffinity(0))
+    want = allowed[: max(1, len(allowed) // 2)]
+    words = [0] * 16
+    for c in want:
+        words[c // 64] |= 1 << (c % 64)
+    seen = {}
+    fake = types.SimpleNamespace(
+        nvmlInit=lambda: None, nvmlShutdown=lambda: None,
+        nvmlDeviceGetHandleByPciBusId=lambda bus: seen.setdefault("bus", bus),
+        nvmlDeviceGetCpuAffinity=lambda h, n: words)
+    props = types.SimpleNamespace(pci_domain_id=0, pci_bus_id=0x1B, pci_device_id=0)
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda i: props)
+    assert pinned.gpu_local_cpus(0, fake) == want and seen["bus"] == "00000000:1b:00.0"
+    try:
+        assert pinned.bind_to_gpu_numa(0, fake) == want
+        assert sorted(os.sched_getaffinity(0)) == want
+    finally:
+        os.sched_setaffinity(0, allowed)
+    broken = types.SimpleNamespace(nvmlInit=lambda: (_ for _ in ()).throw(RuntimeError("no driver")))
+    assert pinned.bind_to_gpu_numa(0, broken) is None and sorted(os.sched_getaffinity(0)) == allowed
