@@ -164,6 +164,8 @@ def setup_dist(torch):
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # NCCL's own messages (its version line included) go to stderr: stdout carries only the JSON result line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     return world, rank, local, dist

@@ -205,8 +205,7 @@ class _NodeState:
                 self.holders.append(holder)
                 flat = holder.tensor
                 flats.append(flat)
-            flat.zero_()
-            params = dict(blk.named_parameters())
+            params = dict(blk.named_parameters())  # (the alignment gaps between parameters are never read)
             block_params = []
             for sp, d, off in zip(specs, deq, layout.offsets):
                 p = params[sp.name]
