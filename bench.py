@@ -164,10 +164,20 @@ def setup_dist(torch):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        # NCCL's own messages (its version line included) go to stderr: stdout carries only the JSON result line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        # NCCL prints its version line (and, with NCCL_DEBUG, more) on the C-level stdout when the communicator is
+        # created: during that, file descriptor 1 points at stderr, so stdout carries only the JSON result line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     return world, rank, local, dist
 
 
