@@ -878,9 +878,24 @@ def run_single_weight(torch, args, world, rank, dist, which):
     ms = max_over_ranks(torch, dist, kern_ms)
     out_bytes = n * 2
     value = sum_over_ranks(torch, dist, out_bytes / (ms / 1e3) / 1e9)
+    # the same read / write byte counts through wf_hbm_probe after the same flush: what a no-arithmetic kernel of this
+    # shape reaches for a launch this short (the flush's dirty lines drain while it runs)
+    pin, pout = src.numel() // 16 * 16, out_bytes // 16 * 16
+    pev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps + 2):
+        flush.zero_()
+        if i >= 2:
+            pev[i - 2][0].record(stream)
+        ext.check(lib.wf_hbm_probe(src.data_ptr(), pin, dst.data_ptr(), pout, stream.cuda_stream), "wf_hbm_probe")
+        if i >= 2:
+            pev[i - 2][1].record(stream)
+    torch.cuda.synchronize()
+    probe_ms = statistics.mean(a.elapsed_time(b) for a, b in pev)
+    mix = (pin + pout) / (probe_ms / 1e3) / 1e9
     return {
         "value": value, "ms_per_step": ms, "kern_ms": kern_ms, "alg_bytes_per_launch": src.numel() + out_bytes,
         "clk": clk.summary(), "e2e": None, "gpu_launches": int(sum_over_ranks(torch, dist, args.steps)),
+        "mix_gbs": mix,
         "config": {"workload": f"GGUF {'Q8_0' if qt == 8 else 'Q4_K'} {shape[0]}x{shape[1]} -> bf16 (one weight)",
                    "mid_dtype": "f16", "l2": "flushed (512 MB write) before every timed launch",
                    "timing": "sum of per-launch CUDA-event durations"},
@@ -944,7 +959,9 @@ def main():
             # the copy-based peak assumes read = write; this traffic is write-heavy (in : out about 1 : 3.6), and a
             # plain streaming kernel with the same byte counts (wf_hbm_probe) is the ceiling it is measured against too
             line["roofline"]["mix_ceiling"] = {"gbs": round(r["mix_gbs"], 1), "frac": round(achieved / r["mix_gbs"], 4),
-                                               "probe": "wf_hbm_probe over the sweep's in / out byte counts"}
+                                               "probe": "wf_hbm_probe over the same in / out byte counts"
+                                                        + (" after the same L2 flush" if args.workload != "sweep"
+                                                           else "")}
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
