@@ -742,6 +742,95 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const __nv_bfloat16
     }
 }
 
+// The quantiser with the pending LayerNorm + modulate (pre 3) and no rotation, K = 512 * NV: ln_modulate_kernel's
+// structure (one row per 128-thread CTA in PyTorch's vectorised layout, the same Welford order, persistent with the
+// next row's loads in flight) with a quantising epilogue instead of the bf16 store: o = bf16(bf16(n * s1) + shift)
+// as there, then the row's absmax over the CTA, scale = max(amax / 127, 1e-30) (div.full) and
+// q = clamp(rint(bf16(o / bf16(scale)))), 4 int8 per thread-vector store.
+template <int NV>
+__global__ void __launch_bounds__(128) quant_lnmod_kernel(const __nv_bfloat16 *__restrict__ x,
+                                                          const __nv_bfloat16 *__restrict__ s1,
+                                                          const __nv_bfloat16 *__restrict__ sh,
+                                                          int8_t *__restrict__ q, float *__restrict__ scale_out,
+                                                          int64_t rows, int64_t K, int64_t rows_per_group, float eps) {
+    __shared__ float red[16];
+    __shared__ float amax_w[2][4];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    int64_t row = blockIdx.x;
+    if (row >= rows) return;
+    uint2 raw[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) raw[j] = __ldg(reinterpret_cast<const uint2 *>(x + row * K) + t + 128 * j);
+    uint2 sraw[NV], hraw[NV];
+    int64_t cached_group = -1;
+    int parity = 0;
+    for (; row < rows; row += gridDim.x, parity ^= 1) {
+        float v[NV * 4];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) unpack4(raw[j], v + 4 * j);
+        const int64_t nrow = row + gridDim.x;
+        if (nrow < rows) {
+#pragma unroll
+            for (int j = 0; j < NV; ++j) raw[j] = __ldg(reinterpret_cast<const uint2 *>(x + nrow * K) + t + 128 * j);
+        }
+        const int64_t group = static_cast<int64_t>(static_cast<uint32_t>(row) / static_cast<uint32_t>(rows_per_group));
+        if (group != cached_group) {
+            cached_group = group;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                sraw[j] = __ldg(reinterpret_cast<const uint2 *>(s1 + group * K) + t + 128 * j);
+                hraw[j] = __ldg(reinterpret_cast<const uint2 *>(sh + group * K) + t + 128 * j);
+            }
+        }
+        float mu, var;
+        ln_stats_n<NV * 4>(v, K, mu, var, red);
+        const float rstd = rsqrt_approx(__fadd_rn(var, eps));
+        uint32_t ob[NV * 2];  // the modulated row as bf16 pairs
+        float amax = 0.f;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            float sv[4], h[4];
+            unpack4(sraw[j], sv);
+            unpack4(hraw[j], h);
+#pragma unroll
+            for (int k = 0; k < 4; k += 2) {
+                const float2 n = r16x2(__fmul_rn(__fsub_rn(v[4 * j + k], mu), rstd),
+                                       __fmul_rn(__fsub_rn(v[4 * j + k + 1], mu), rstd));
+                const float2 tt = r16x2(__fmul_rn(n.x, sv[k]), __fmul_rn(n.y, sv[k + 1]));
+                const uint32_t pr = pack2(__fadd_rn(tt.x, h[k]), __fadd_rn(tt.y, h[k + 1]));
+                ob[2 * j + k / 2] = pr;
+                amax = fmaxf(amax, fmaxf(fabsf(bf_lo(pr)), fabsf(bf_hi(pr))));
+            }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+        if (lane == 0) amax_w[parity][warp] = amax;  // two buffers: a fast warp may reach the next row first
+        __syncthreads();
+        amax = fmaxf(fmaxf(amax_w[parity][0], amax_w[parity][1]), fmaxf(amax_w[parity][2], amax_w[parity][3]));
+        amax = fminf(amax, 3.38953139e38f);
+        const float scale = fmaxf(div_full(amax, 127.0f), 1.0e-30f);
+        if (t == 0) scale_out[row] = scale;
+        const float sb = r16(scale);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int64_t c = static_cast<int64_t>(t + 128 * j) * 4;
+            *reinterpret_cast<uint32_t *>(q + row * K + c) = quant_quad(ob[2 * j], ob[2 * j + 1], sb);
+        }
+        // (red[] of the next row's statistics is written only after this row's ln_stats barriers, and amax_w
+        // alternates between two buffers, so one barrier per row suffices)
+    }
+}
+
+template <int NV>
+int launch_quant_lnmod(const void *x, const void *s1, const void *sh, int8_t *q, float *sc, int64_t rows, int64_t K,
+                       int64_t rpg, float eps, cudaStream_t s) {
+    const int g = persistent_grid<quant_lnmod_kernel<NV>>(128, 0, rows);
+    quant_lnmod_kernel<NV><<<g, 128, 0, s>>>(static_cast<const __nv_bfloat16 *>(x),
+                                             static_cast<const __nv_bfloat16 *>(s1),
+                                             static_cast<const __nv_bfloat16 *>(sh), q, sc, rows, K, rpg, eps);
+    return static_cast<int>(cudaGetLastError());
+}
+
 template <int PRE, int NCH, int WPR>
 int launch_quant_reg(const void *x, const void *s1, const void *sh, const void *gelu, int8_t *q, float *sc,
                      int64_t rows, int64_t rpg, cudaStream_t s) {
@@ -918,6 +1007,15 @@ extern "C" WF_API int wf_quant_rows(const void *x, const void *s1, const void *s
     int rc = check_device();
     if (rc != WF_OK) return rc;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (!rotate && pre == 3 && rows <= INT32_MAX && al(q, 4)) {
+        switch (K / 512) {  // K % 512 == 0 and K <= 8192 were checked above
+#define WF_QL(NV) case NV: return launch_quant_lnmod<NV>(x, s1, shift, q, scale, rows, K, rows_per_group, eps, s);
+            WF_QL(1) WF_QL(2) WF_QL(3) WF_QL(4) WF_QL(5) WF_QL(6) WF_QL(7) WF_QL(8)
+            WF_QL(9) WF_QL(10) WF_QL(11) WF_QL(12) WF_QL(13) WF_QL(14) WF_QL(15) WF_QL(16)
+#undef WF_QL
+            default: break;
+        }
+    }
     if (!rotate && pre != 3 && al(x, 16) && al(q, 8) && (pre != 2 || (al(s1, 16) && al(shift, 16)))) {
         bool done = false;
         switch (pre) {

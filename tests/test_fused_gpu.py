@@ -315,3 +315,33 @@ def test_gated_residual_equals_addcmul(cuda, n, D, rpg):
     if n % rpg == 0:   # the block's broadcast form
         b = n // rpg
         assert torch.equal(torch.addcmul(x.view(b, rpg, D), gate.view(b, 1, D), o.view(b, rpg, D)).view(n, D), want)
+
+
+@pytest.mark.parametrize("k,rpg", [(2048, 4096), (512, 3), (5120, 100), (8192, 7)])
+def test_quant_rows_lnmod_equals_lnmod_then_quant(cuda, k, rpg):
+    """The quantiser with the pending LayerNorm + modulate (pre 3, the fused kernel) gives exactly kernel A's bf16
+    rows (wf_ln_modulate) quantised by the plain quantiser (pre 0): the same values, rounded the same way."""
+    import torch
+    ext = wf("_ext")
+    L = ext.lib()
+    g = torch.Generator(device="cuda").manual_seed(k + rpg)
+    rows = 300
+    groups = (rows + rpg - 1) // rpg
+    x = (torch.randn((rows, k), device="cuda", generator=g) * 2 + 0.5).to(torch.bfloat16)
+    x[5] = 1.0                                                      # a constant row: variance 0
+    s1 = (1 + 0.1 * torch.randn((groups, k), device="cuda", generator=g)).to(torch.bfloat16)
+    sh = (0.1 * torch.randn((groups, k), device="cuda", generator=g)).to(torch.bfloat16)
+    st = ext.stream_of(x.device)
+    q3 = torch.empty((rows, k), dtype=torch.int8, device="cuda")
+    s3 = torch.empty((rows,), dtype=torch.float32, device="cuda")
+    ext.check(L.wf_quant_rows(x.data_ptr(), s1.data_ptr(), sh.data_ptr(), None, q3.data_ptr(), s3.data_ptr(), rows, k,
+                              rpg, 1e-6, 3, 0, st), "quant pre 3")
+    y = torch.empty_like(x)
+    ext.check(L.wf_ln_modulate(x.data_ptr(), s1.data_ptr(), sh.data_ptr(), y.data_ptr(), rows, k, rpg, 1e-6, st), "ln")
+    q0 = torch.empty_like(q3)
+    s0 = torch.empty_like(s3)
+    ext.check(L.wf_quant_rows(y.data_ptr(), None, None, None, q0.data_ptr(), s0.data_ptr(), rows, k, 1, 0.0, 0, 0, st),
+              "quant pre 0")
+    torch.cuda.synchronize()
+    assert torch.equal(q3, q0)
+    assert torch.equal(s3.view(torch.int32), s0.view(torch.int32))
