@@ -144,6 +144,26 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------------------------------- helpers
+class L2Flush:
+    """Evicts L2 (126 MB) between timed launches: writes a 512 MB buffer, then reads another 512 MB one. The write
+    evicts the inputs; the read then replaces the lines the write left dirty with clean ones, so their write-back to
+    DRAM happens here and not inside the next timed launch (where it would add up to 126 MB of writes to a kernel of
+    a few tens of microseconds)."""
+
+    def __init__(self, torch, dev):
+        self.torch = torch
+        self.w = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        self.r = torch.zeros(128 * 1024 * 1024, dtype=torch.float32, device=dev)
+        self.sink = torch.empty((), dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.w.zero_()
+        self.torch.sum(self.r, dim=0, dtype=self.torch.float32, out=self.sink)
+
+
+L2_NOTE = "flushed before every timed launch: 512 MB written, then 512 MB read (the write-back leaves L2 first)"
+
+
 def measured_peaks():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -410,7 +430,7 @@ def run_w8a8(torch, args, world, rank, dist):
     xq = torch.empty((M, K), dtype=torch.int8, device=dev)
     xs = torch.empty((M, 1), dtype=torch.float32, device=dev)
     y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = L2Flush(torch, dev)
     lib = ext.lib()
     stream = torch.cuda.current_stream(dev)
     kq = fk._get_kernels()["quant_row"][(M,)]
@@ -425,7 +445,7 @@ def run_w8a8(torch, args, world, rank, dist):
             ext.check(rc, "wf_w8a8_gemm")
 
     for _ in range(args.warmup):
-        flush.zero_()
+        flush()
         quant()
         gemm()
     barrier(torch, dist)
@@ -434,7 +454,7 @@ def run_w8a8(torch, args, world, rank, dist):
     with ClockSampler(torch.cuda.current_device()) as clk:
         barrier(torch, dist)
         for s in range(args.steps):
-            flush.zero_()
+            flush()
             evq[s][0].record(stream)
             quant()
             evq[s][1].record(stream)
@@ -456,7 +476,7 @@ def run_w8a8(torch, args, world, rank, dist):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         tot = 0.0
         for _ in range(5):
-            flush.zero_()
+            flush()
             e0.record(stream)
             torch._int_mm(xq, wq.t())
             e1.record(stream)
@@ -477,7 +497,7 @@ def run_w8a8(torch, args, world, rank, dist):
                    "quantiser": "per-token absmax int8 (plain, no rotation)", "quant_ms": round(q_ms, 4),
                    "gemm_ms": round(g_ms, 4),
                    "cublaslt_int_mm_ms": None if lib_ms is None else round(lib_ms, 4),
-                   "l2": "flushed (512 MB write) before every step"},
+                   "l2": L2_NOTE},
     }
 
 
@@ -718,7 +738,7 @@ def run_prologue(torch, args, world, rank, dist):
     wq = (1 + torch.randn(128, device=dev, generator=g) * 0.02).to(torch.bfloat16)
     wk = (1 + torch.randn(128, device=dev, generator=g) * 0.02).to(torch.bfloat16)
     rope = cb.rope3d_table(1, 64, 64, device=dev)
-    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = L2Flush(torch, dev)
     stream = torch.cuda.current_stream(dev)
     s1 = (1 + sc).contiguous()
     ln = fb._get_kernels()["lnmod"][(8192,)]
@@ -731,7 +751,7 @@ def run_prologue(torch, args, world, rank, dist):
         return sf.rms_rope(q, rope, wq, 1e-6), sf.rms_rope(k, rope, wk, 1e-6)
 
     for _ in range(args.warmup):
-        flush.zero_()
+        flush()
         kernel_a()
         kernel_b()
     barrier(torch, dist)
@@ -740,7 +760,7 @@ def run_prologue(torch, args, world, rank, dist):
     with ClockSampler(torch.cuda.current_device()) as clk:
         barrier(torch, dist)
         for s_ in range(args.steps):
-            flush.zero_()
+            flush()
             ea[s_][0].record(stream)
             kernel_a()
             ea[s_][1].record(stream)
@@ -753,12 +773,12 @@ def run_prologue(torch, args, world, rank, dist):
     ca, cb_ = torch.empty_like(x), torch.empty_like(q)
     copy_a, copy_b = [], []
     for _ in range(5):
-        flush.zero_()
+        flush()
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record(stream)
         ca.copy_(x)
         e1.record(stream)
-        flush.zero_()
+        flush()
         e2.record(stream)
         cb_.copy_(q)
         e3 = torch.cuda.Event(enable_timing=True)
@@ -824,7 +844,7 @@ def finish_prologue(torch, args, world, rank, dist, r):
                        "kernel_a_bytes": r["bytes_a"], "kernel_b_us_q_and_k": round(r["b_ms"] * 1e3, 2),
                        "kernel_b_gbs": round(b_rate, 1), "kernel_b_bytes": r["bytes_b"],
                        "torch_copy_same_bytes_us": {"a": round(r["copy_a_us"], 2), "b_q_and_k": round(r["copy_b_us"], 2)},
-                       "l2": "flushed (512 MB write) before every step"},
+                       "l2": L2_NOTE},
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(ach / peak, 4), "traffic": NCU_TRAFFIC.get("prologue"),
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})",
@@ -852,7 +872,7 @@ def run_single_weight(torch, args, world, rank, dist, which):
         src = fill_q4k(torch, shape[0] * shape[1] // 256, dev, gen)
     n = shape[0] * shape[1]
     dst = torch.empty(shape, dtype=torch.bfloat16, device=dev)
-    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)  # 512 MB > 126 MB L2
+    flush = L2Flush(torch, dev)
     lib = ext.lib()
     stream = torch.cuda.current_stream(dev)
 
@@ -862,14 +882,14 @@ def run_single_weight(torch, args, world, rank, dist, which):
             ext.check(rc, "wf_dequant_gguf")
 
     for _ in range(args.warmup):
-        flush.zero_()
+        flush()
         step()
     barrier(torch, dist)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with ClockSampler(torch.cuda.current_device()) as clk:
         barrier(torch, dist)
         for s in range(args.steps):
-            flush.zero_()
+            flush()
             ev[s][0].record(stream)
             step()
             ev[s][1].record(stream)
@@ -879,11 +899,11 @@ def run_single_weight(torch, args, world, rank, dist, which):
     out_bytes = n * 2
     value = sum_over_ranks(torch, dist, out_bytes / (ms / 1e3) / 1e9)
     # the same read / write byte counts through wf_hbm_probe after the same flush: what a no-arithmetic kernel of this
-    # shape reaches for a launch this short (the flush's dirty lines drain while it runs)
+    # shape reaches for a launch this short
     pin, pout = src.numel() // 16 * 16, out_bytes // 16 * 16
     pev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     for i in range(args.steps + 2):
-        flush.zero_()
+        flush()
         if i >= 2:
             pev[i - 2][0].record(stream)
         ext.check(lib.wf_hbm_probe(src.data_ptr(), pin, dst.data_ptr(), pout, stream.cuda_stream), "wf_hbm_probe")
@@ -897,7 +917,7 @@ def run_single_weight(torch, args, world, rank, dist, which):
         "clk": clk.summary(), "e2e": None, "gpu_launches": int(sum_over_ranks(torch, dist, args.steps)),
         "mix_gbs": mix,
         "config": {"workload": f"GGUF {'Q8_0' if qt == 8 else 'Q4_K'} {shape[0]}x{shape[1]} -> bf16 (one weight)",
-                   "mid_dtype": "f16", "l2": "flushed (512 MB write) before every timed launch",
+                   "mid_dtype": "f16", "l2": L2_NOTE,
                    "timing": "sum of per-launch CUDA-event durations"},
     }
 
