@@ -55,6 +55,17 @@ __device__ __forceinline__ float load_w(const void *w, int wdt, int i) {
     return static_cast<const float *>(w)[i];
 }
 
+// bf16(bf16(n * s) + h) for bf16 pairs: the product of two bf16 values is exact in float32, so one bf16 rounding of it
+// (mul.rn.bf16x2) is the reference's float product rounded to bf16; float32 holds at least 2 * 8 + 2 bits, so the
+// float sum of two bf16 values rounded to bf16 is the correctly rounded bf16 sum (add.rn.bf16x2). The _rn forms keep
+// the compiler from contracting the two into one fma, which would round once instead of twice.
+__device__ __forceinline__ uint32_t mod_bf16x2(uint32_t n, uint32_t s, uint32_t h) {
+    const __nv_bfloat162 t = __hmul2_rn(*reinterpret_cast<const __nv_bfloat162 *>(&n),
+                                        *reinterpret_cast<const __nv_bfloat162 *>(&s));
+    const __nv_bfloat162 o = __hadd2_rn(t, *reinterpret_cast<const __nv_bfloat162 *>(&h));
+    return *reinterpret_cast<const uint32_t *>(&o);
+}
+
 // ------------------------------------------------------------------------------------------------- modulate
 // out = R16(R16(x * s1) + shift) (fused_kernels.py:51-62 _mod), 8 values per thread, grid-stride. d % 8 == 0.
 __global__ void __launch_bounds__(256) modulate_kernel(const uint4 *__restrict__ x, const __nv_bfloat16 *__restrict__ s1,
@@ -68,16 +79,8 @@ __global__ void __launch_bounds__(256) modulate_kernel(const uint4 *__restrict__
         const uint4 xv = __ldg(x + i);
         const uint4 sv = __ldg(reinterpret_cast<const uint4 *>(s1 + goff));
         const uint4 hv = __ldg(reinterpret_cast<const uint4 *>(sh + goff));
-        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w},
-                       hs[4] = {hv.x, hv.y, hv.z, hv.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float t0 = r16(__fmul_rn(bf_lo(xs[k]), bf_lo(ss[k])));
-            const float t1 = r16(__fmul_rn(bf_hi(xs[k]), bf_hi(ss[k])));
-            o[k] = pack2(__fadd_rn(t0, bf_lo(hs[k])), __fadd_rn(t1, bf_hi(hs[k])));
-        }
-        out[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        out[i] = make_uint4(mod_bf16x2(xv.x, sv.x, hv.x), mod_bf16x2(xv.y, sv.y, hv.y), mod_bf16x2(xv.z, sv.z, hv.z),
+                            mod_bf16x2(xv.w, sv.w, hv.w));
     }
 }
 
@@ -165,18 +168,19 @@ __device__ __forceinline__ float2 r16x2(float a, float b) {
 
 __device__ __forceinline__ void ln_merge(Welford w, int64_t K, float &mu, float &var, float *red);
 
+
 // wcombine of two states that each hold C values: the count C + C and its correctly rounded reciprocal are
 // compile-time constants (C is the same in every lane), so the division of the merge becomes a product
 template <int C>
 __device__ __forceinline__ Welford wcombine_n(Welford own, Welford oth) {
     constexpr float count = static_cast<float>(2 * C);
     constexpr float coef = 1.0f / count;  // evaluated at compile time in IEEE arithmetic: div.rn's value
+    constexpr float c_one = static_cast<float>(C);  // both states hold C values
+    constexpr float nab = c_one * coef;              // each side's weight, in IEEE arithmetic as at run time
     const float delta = __fsub_rn(own.m, oth.m);
-    const float n_a = __fmul_rn(oth.c, coef);
-    const float n_b = __fmul_rn(own.c, coef);
     Welford r;
-    r.m = __fmaf_rn(n_a, oth.m, __fmul_rn(n_b, own.m));
-    r.s = __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), oth.c), n_b, __fadd_rn(oth.s, own.s));
+    r.m = __fmaf_rn(nab, oth.m, __fmul_rn(nab, own.m));
+    r.s = __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), c_one), nab, __fadd_rn(oth.s, own.s));
     r.c = count;
     return r;
 }
@@ -188,7 +192,7 @@ __device__ __forceinline__ void ln_merge_n(Welford w, int64_t K, float &mu, floa
         Welford o;                                              \
         o.m = __shfl_down_sync(0xFFFFFFFFu, w.m, OFF);          \
         o.s = __shfl_down_sync(0xFFFFFFFFu, w.s, OFF);          \
-        o.c = __shfl_down_sync(0xFFFFFFFFu, w.c, OFF);          \
+        o.c = static_cast<float>(C);  /* the same in every lane */ \
         w = wcombine_n<C>(w, o);                                \
     }
     WF_SHFL_MERGE(16, N) WF_SHFL_MERGE(8, 2 * N) WF_SHFL_MERGE(4, 4 * N) WF_SHFL_MERGE(2, 8 * N)
@@ -319,19 +323,12 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
             const int64_t c = static_cast<int64_t>(t + 128 * j) * 4;
-            float sv[4], h[4];
-            unpack4(sraw[j], sv);
-            unpack4(hraw[j], h);
-            float o[4];
-#pragma unroll
-            for (int k = 0; k < 4; k += 2) {
-                const float2 n = r16x2(__fmul_rn(__fsub_rn(v[4 * j + k], mu), rstd),
-                                       __fmul_rn(__fsub_rn(v[4 * j + k + 1], mu), rstd));
-                const float2 tt = r16x2(__fmul_rn(n.x, sv[k]), __fmul_rn(n.y, sv[k + 1]));
-                o[k] = __fadd_rn(tt.x, h[k]);
-                o[k + 1] = __fadd_rn(tt.y, h[k + 1]);
-            }
-            *reinterpret_cast<uint2 *>(out + row * K + c) = make_uint2(pack2(o[0], o[1]), pack2(o[2], o[3]));
+            const uint32_t n01 = pack2(__fmul_rn(__fsub_rn(v[4 * j], mu), rstd),
+                                       __fmul_rn(__fsub_rn(v[4 * j + 1], mu), rstd));
+            const uint32_t n23 = pack2(__fmul_rn(__fsub_rn(v[4 * j + 2], mu), rstd),
+                                       __fmul_rn(__fsub_rn(v[4 * j + 3], mu), rstd));
+            *reinterpret_cast<uint2 *>(out + row * K + c) =
+                make_uint2(mod_bf16x2(n01, sraw[j].x, hraw[j].x), mod_bf16x2(n23, sraw[j].y, hraw[j].y));
         }
         __syncthreads();  // red[] is reused by the next row's statistics
     }
@@ -599,16 +596,8 @@ __device__ __forceinline__ void quant_pre(uint4 (&v)[NCH], const __nv_bfloat16 *
 #pragma unroll
         for (int j = 0; j < NCH; ++j) {
             const uint4 sv = __ldg(sr + 32 * j + lane), hv = __ldg(hr + 32 * j + lane);
-            const uint32_t xs[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-            const uint32_t ss[4] = {sv.x, sv.y, sv.z, sv.w}, hs[4] = {hv.x, hv.y, hv.z, hv.w};
-            uint32_t o[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float a = r16(__fadd_rn(r16(__fmul_rn(bf_lo(xs[k]), bf_lo(ss[k]))), bf_lo(hs[k])));
-                const float b = r16(__fadd_rn(r16(__fmul_rn(bf_hi(xs[k]), bf_hi(ss[k]))), bf_hi(hs[k])));
-                o[k] = (__float_as_uint(a) >> 16) | (__float_as_uint(b) & 0xFFFF0000u);
-            }
-            v[j] = make_uint4(o[0], o[1], o[2], o[3]);
+            v[j] = make_uint4(mod_bf16x2(v[j].x, sv.x, hv.x), mod_bf16x2(v[j].y, sv.y, hv.y),
+                              mod_bf16x2(v[j].z, sv.z, hv.z), mod_bf16x2(v[j].w, sv.w, hv.w));
         }
     } else if constexpr (PRE == 1) {
         const uint16_t *tab = reinterpret_cast<const uint16_t *>(gelu);
@@ -789,18 +778,14 @@ __global__ void __launch_bounds__(128) quant_lnmod_kernel(const __nv_bfloat16 *_
         float amax = 0.f;
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-            float sv[4], h[4];
-            unpack4(sraw[j], sv);
-            unpack4(hraw[j], h);
-#pragma unroll
-            for (int k = 0; k < 4; k += 2) {
-                const float2 n = r16x2(__fmul_rn(__fsub_rn(v[4 * j + k], mu), rstd),
-                                       __fmul_rn(__fsub_rn(v[4 * j + k + 1], mu), rstd));
-                const float2 tt = r16x2(__fmul_rn(n.x, sv[k]), __fmul_rn(n.y, sv[k + 1]));
-                const uint32_t pr = pack2(__fadd_rn(tt.x, h[k]), __fadd_rn(tt.y, h[k + 1]));
-                ob[2 * j + k / 2] = pr;
-                amax = fmaxf(amax, fmaxf(fabsf(bf_lo(pr)), fabsf(bf_hi(pr))));
-            }
+            const uint32_t n01 = pack2(__fmul_rn(__fsub_rn(v[4 * j], mu), rstd),
+                                       __fmul_rn(__fsub_rn(v[4 * j + 1], mu), rstd));
+            const uint32_t n23 = pack2(__fmul_rn(__fsub_rn(v[4 * j + 2], mu), rstd),
+                                       __fmul_rn(__fsub_rn(v[4 * j + 3], mu), rstd));
+            ob[2 * j] = mod_bf16x2(n01, sraw[j].x, hraw[j].x);
+            ob[2 * j + 1] = mod_bf16x2(n23, sraw[j].y, hraw[j].y);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(bf_lo(ob[2 * j])), fabsf(bf_hi(ob[2 * j]))),
+                                     fmaxf(fabsf(bf_lo(ob[2 * j + 1])), fabsf(bf_hi(ob[2 * j + 1])))));
         }
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
