@@ -658,7 +658,73 @@ __device__ __forceinline__ void quant_store(const uint4 (&v)[NCH], float sb, uin
 // arithmetic as quant_rows_kernel above: the pending operation rounded to bf16 as there, amax = min(max |v|,
 // 3.38953139e38), scale = max(amax / 127, 1e-30) (div.full), q = clamp(rint(bf16(v / bf16(scale)))) -- every v is
 // already a bf16 value here, so the reference's bf16 rounding of v before the division is the identity.
-template <int PRE, int NCH, int WPR>
+// ConvRot: the 256-wide Hadamard of the quantiser (quant_rows_kernel's four radix-4 stages) on a register chunk. Element
+// e = 8 * lane + i of a 256-group (i = 0..7 in the lane) has base-4 digits d0 = i & 3, d1 = 2 * (lane & 1) + (i >> 2),
+// d2 = (lane >> 1) & 3, d3 = (lane >> 3) & 3; stage s combines the four elements that differ only in digit s, taken
+// in digit order (a, b, c, d), into output k = their digit: ((+-a +- b) +- c) +- d with the signs of output k --
+// k = 0: (+, +, +, -), 1: (+, +, -, +), 2: (+, -, +, +), 3: (-, +, +, +) -- the reference's sums, left to right.
+__device__ __forceinline__ float neg_if(float x, bool n) { return n ? -x : x; }
+__device__ __forceinline__ float had4(float a, float b, float c, float d, int k) {
+    const float t = __fadd_rn(neg_if(a, k == 3), neg_if(b, k == 2));
+    return __fadd_rn(__fadd_rn(t, neg_if(c, k == 1)), neg_if(d, k == 0));
+}
+
+// the chunk's 8 values of this lane, rotated and scaled by 1/16 (exact); all 32 lanes take part
+__device__ __forceinline__ void hadamard256(float (&f)[8], int lane) {
+    float o[8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)  // digit 0: inside the lane
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[4 * h + k] = had4(f[4 * h], f[4 * h + 1], f[4 * h + 2], f[4 * h + 3], k);
+    const int p = lane & 1;  // digit 1: the lane pair (lane ^ 1); this lane holds digit values 2p and 2p + 1
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const float q0 = __shfl_xor_sync(0xFFFFFFFFu, o[m], 1), q1 = __shfl_xor_sync(0xFFFFFFFFu, o[4 + m], 1);
+        const float a = p ? q0 : o[m], b = p ? q1 : o[4 + m], c = p ? o[m] : q0, d = p ? o[4 + m] : q1;
+        f[m] = had4(a, b, c, d, 2 * p);
+        f[4 + m] = had4(a, b, c, d, 2 * p + 1);
+    }
+    const int d2 = (lane >> 1) & 3, base2 = lane & ~6;  // digit 2: lanes that differ in bits 1-2
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float v4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v4[k] = __shfl_sync(0xFFFFFFFFu, f[i], base2 | (k << 1));
+        f[i] = had4(v4[0], v4[1], v4[2], v4[3], d2);
+    }
+    const int d3 = (lane >> 3) & 3, base3 = lane & ~24;  // digit 3: lanes that differ in bits 3-4
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float v4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v4[k] = __shfl_sync(0xFFFFFFFFu, f[i], base3 | (k << 3));
+        f[i] = __fmul_rn(had4(v4[0], v4[1], v4[2], v4[3], d3), 0.0625f);
+    }
+}
+
+// ROT: every chunk rotated in place, the row's absmax taken on the rotated float values (as the shared-memory
+// kernel does), each value then held as bf16(value) -- what the quantiser divides
+template <int NCH>
+__device__ __forceinline__ float rotate_chunks(uint4 (&v)[NCH], int lane) {
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) {
+        const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+        float f[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            f[2 * k] = bf_lo(w[k]);
+            f[2 * k + 1] = bf_hi(w[k]);
+        }
+        hadamard256(f, lane);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(f[k]));
+        v[j] = make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+    }
+    return amax;
+}
+
+template <int PRE, int NCH, int WPR, bool ROT = false>
 __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const __nv_bfloat16 *__restrict__ x,
                                                              const __nv_bfloat16 *__restrict__ s1,
                                                              const __nv_bfloat16 *__restrict__ sh,
@@ -685,7 +751,7 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const __nv_bfloat16
                     nx[j] = __ldg(reinterpret_cast<const uint4 *>(x + nrow * K) + 32 * j + lane);
             }
             quant_pre<PRE, NCH>(v, s1, sh, gelu, (row / rows_per_group) * K, lane);
-            float amax = chunk_amax<NCH>(v);
+            float amax = ROT ? rotate_chunks<NCH>(v, lane) : chunk_amax<NCH>(v);
 #pragma unroll
             for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
             amax = fminf(amax, 3.38953139e38f);
@@ -709,7 +775,7 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const __nv_bfloat16
 #pragma unroll
                 for (int j = 0; j < NCH; ++j) v[j] = __ldg(xr + 32 * j + lane);
                 quant_pre<PRE, NCH>(v, s1, sh, gelu, (row / rows_per_group) * K + off, lane);
-                amax = chunk_amax<NCH>(v);
+                amax = ROT ? rotate_chunks<NCH>(v, lane) : chunk_amax<NCH>(v);
             }
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
@@ -816,10 +882,10 @@ int launch_quant_lnmod(const void *x, const void *s1, const void *sh, int8_t *q,
     return static_cast<int>(cudaGetLastError());
 }
 
-template <int PRE, int NCH, int WPR>
+template <int PRE, int NCH, int WPR, bool ROT = false>
 int launch_quant_reg(const void *x, const void *s1, const void *sh, const void *gelu, int8_t *q, float *sc,
                      int64_t rows, int64_t rpg, cudaStream_t s) {
-    auto kern = quant_rows_reg_kernel<PRE, NCH, WPR>;
+    auto kern = quant_rows_reg_kernel<PRE, NCH, WPR, ROT>;
     static int per_sm = 0;
     if (per_sm == 0) {
         int n = 0;
@@ -835,6 +901,21 @@ int launch_quant_reg(const void *x, const void *s1, const void *sh, const void *
                               static_cast<const __nv_bfloat16 *>(sh), static_cast<const __nv_bfloat16 *>(gelu), q,
                               sc, rows, rpg);
     return static_cast<int>(cudaGetLastError());
+}
+
+// The rotated (ConvRot) register kernel for K = 256 * n up to 6144 (one warp per row), or false.
+template <int PRE>
+bool quant_rot_dispatch(int64_t K, const void *x, const void *s1, const void *sh, const void *gelu, int8_t *q,
+                        float *sc, int64_t rows, int64_t rpg, cudaStream_t s, int *rc) {
+#define WF_QT(N) do { *rc = launch_quant_reg<PRE, N, 1, true>(x, s1, sh, gelu, q, sc, rows, rpg, s); return true; } while (0)
+    if (K % 256 != 0) return false;
+    switch (K / 256) {
+        case 1: WF_QT(1); case 2: WF_QT(2); case 3: WF_QT(3); case 4: WF_QT(4); case 5: WF_QT(5); case 6: WF_QT(6);
+        case 8: WF_QT(8); case 10: WF_QT(10); case 12: WF_QT(12); case 16: WF_QT(16); case 20: WF_QT(20);
+        case 24: WF_QT(24);
+        default: return false;
+    }
+#undef WF_QT
 }
 
 // The register kernel's (NCH, WPR) for K, or false: one warp per row up to K = 6144, eight from K = 8192 to 32768.
@@ -1000,6 +1081,15 @@ extern "C" WF_API int wf_quant_rows(const void *x, const void *s1, const void *s
 #undef WF_QL
             default: break;
         }
+    }
+    if (rotate && pre != 3 && al(x, 16) && al(q, 8) && (pre != 2 || (al(s1, 16) && al(shift, 16)))) {
+        bool done = false;
+        switch (pre) {
+            case 0: done = quant_rot_dispatch<0>(K, x, s1, shift, gelu_table, q, scale, rows, rows_per_group, s, &rc); break;
+            case 1: done = quant_rot_dispatch<1>(K, x, s1, shift, gelu_table, q, scale, rows, rows_per_group, s, &rc); break;
+            default: done = quant_rot_dispatch<2>(K, x, s1, shift, gelu_table, q, scale, rows, rows_per_group, s, &rc); break;
+        }
+        if (done) return rc;
     }
     if (!rotate && pre != 3 && al(x, 16) && al(q, 8) && (pre != 2 || (al(s1, 16) && al(shift, 16)))) {
         bool done = false;

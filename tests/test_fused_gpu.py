@@ -261,12 +261,16 @@ def test_fused_c_abi_rejections(cuda):
     assert L.wf_quant_rows(p, None, None, None, p, p, 4, 1024, 1, 0.0, 2, 0, st) == -1  # modulate needs s1 / shift
 
 
+@pytest.mark.parametrize("rotate", [0, 1])
 @pytest.mark.parametrize("pre", [0, 1, 2])
 @pytest.mark.parametrize("k", [256, 768, 1280, 2048, 5120, 6144, 8192, 20480, 1000])
-def test_quant_rows_register_kernel_matches_shared_kernel(cuda, pre, k):
-    """The register-resident quantiser (16-byte aligned operands, K = 256 * n for the sizes it takes) and the
-    shared-memory one (any K % 4 == 0; reached here through an x that is only 8-byte aligned) give the same bits."""
+def test_quant_rows_register_kernel_matches_shared_kernel(cuda, pre, k, rotate):
+    """The register-resident quantiser (16-byte aligned operands, K = 256 * n for the sizes it takes; with the
+    ConvRot Hadamard up to K = 6144) and the shared-memory one (any K % 4 == 0; reached here through an x that is only
+    8-byte aligned) give the same bits."""
     import torch
+    if rotate and k % 256:
+        pytest.skip("the rotation needs K % 256 == 0")
     ext = wf("_ext")
     L = ext.lib()
     g = torch.Generator(device="cuda").manual_seed(k + pre)
@@ -286,7 +290,7 @@ def test_quant_rows_register_kernel_matches_shared_kernel(cuda, pre, k):
         sc = torch.empty((rows,), dtype=torch.float32, device="cuda")
         rc = L.wf_quant_rows(x.data_ptr(), s1.data_ptr() if pre == 2 else None, sh.data_ptr() if pre == 2 else None,
                              gelu.data_ptr() if pre == 1 else None, q.data_ptr(), sc.data_ptr(), rows, k, rpg, 0.0,
-                             pre, 0, ext.stream_of(x.device))
+                             pre, rotate, ext.stream_of(x.device))
         ext.check(rc, "wf_quant_rows")
         outs.append((q, sc))
     torch.cuda.synchronize()
