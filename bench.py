@@ -922,13 +922,241 @@ def run_single_weight(torch, args, world, rank, dist, which):
     }
 
 
+# ------------------------------------------------------------------------------------ §8(f) rows: formats, LoRA, SSD
+GGUF_GEOMETRY = {2: ("Q4_0", 32, 18, (0,)), 3: ("Q4_1", 32, 20, (0, 2)), 6: ("Q5_0", 32, 22, (0,)),
+                 7: ("Q5_1", 32, 24, (0, 2)), 8: ("Q8_0", 32, 34, (0,)), 10: ("Q2_K", 256, 84, (80, 82)),
+                 11: ("Q3_K", 256, 110, (108,)), 12: ("Q4_K", 256, 144, (0, 2)), 13: ("Q5_K", 256, 176, (0, 2)),
+                 14: ("Q6_K", 256, 210, (208,))}
+
+
+def fill_gguf(torch, qt, n_values, device, gen):
+    """Random packed blocks of GGML type qt with every float16 field (d, dmin) finite: U(0, 0.01)."""
+    _name, vpb, ts, f16 = GGUF_GEOMETRY[qt]
+    nb = n_values // vpb
+    raw = torch.randint(0, 256, (nb, ts), dtype=torch.uint8, device=device, generator=gen)
+    for off in f16:
+        raw[:, off:off + 2] = (torch.rand((nb, 1), device=device, generator=gen) * 0.01).half().view(torch.uint8)
+    return raw.reshape(-1)
+
+
+def time_launches(torch, flush, stream, fn, steps):
+    """Mean CUDA-event time (ms) of fn over `steps` launches, L2 flushed before each."""
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush()
+        ev[i][0].record(stream)
+        fn()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    return statistics.mean(a.elapsed_time(b) for a, b in ev)
+
+
+def run_formats(torch, args, world, rank, dist):
+    """§8(f) 2: every GGML type of the kernel family on one 5120 x 13824 weight (bf16 out, mid f16), L2 flushed per
+    launch; each against the copy peak and against wf_hbm_probe over its own in / out bytes after the same flush."""
+    ext = _pkg("_ext")
+    lib = ext.lib()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev)
+    flush = L2Flush(torch, dev)
+    n = 5120 * 13824
+    dst = torch.empty(n, dtype=torch.bfloat16, device=dev)
+    peak, _kind = measured_peaks()
+    per, gbs_all = {}, []
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for qt, (name, _vpb, _ts, _f16) in GGUF_GEOMETRY.items():
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(20261201 + 100 + qt)
+            src = fill_gguf(torch, qt, n, dev, gen)
+
+            def launch():
+                ext.check(lib.wf_dequant_gguf(src.data_ptr(), src.numel(), dst.data_ptr(), n, qt, 0, 1,
+                                              stream.cuda_stream), "wf_dequant_gguf")
+
+            for _ in range(args.warmup):
+                launch()
+            ms = time_launches(torch, flush, stream, launch, args.steps)
+            pin, pout = src.numel() // 16 * 16, n * 2
+            pms = time_launches(torch, flush, stream, lambda: ext.check(lib.wf_hbm_probe(
+                src.data_ptr(), pin, dst.data_ptr(), pout, stream.cuda_stream), "probe"), args.steps)
+            alg = (src.numel() + 2 * n) / (ms / 1e3) / 1e9
+            mix = (pin + pout) / (pms / 1e3) / 1e9
+            per[name] = {"us": round(ms * 1e3, 2), "alg_gbs": round(alg, 1), "frac_of_copy_peak": round(alg / peak, 4),
+                         "mix_ceiling_gbs": round(mix, 1), "frac_of_mix_ceiling": round(alg / mix, 4),
+                         "in_bytes": src.numel(), "out_bytes": 2 * n}
+            gbs_all.append(2 * n / (ms / 1e3) / 1e9)
+            del src
+    geo = float(np.exp(np.mean(np.log(gbs_all))))
+    fr = [v["frac_of_mix_ceiling"] for v in per.values()]
+    return {"value": geo, "per": per, "clk": clk.summary(), "peak": peak, "min_frac_mix": min(fr),
+            "mean_frac_copy": float(np.mean([v["frac_of_copy_peak"] for v in per.values()]))}
+
+
+def finish_formats(torch, args, world, rank, dist, r):
+    if rank == 0:
+        print(json.dumps({
+            "metric": "GGUF dequant out GB/s, all 10 GGML types (geometric mean)", "value": round(r["value"], 2),
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8->bf16 (mid f16)",
+            "data": "synthetic (seeded random blocks, float16 fields U(0, 0.01))",
+            "config": {"workload": "one 5120 x 13824 weight per GGML type -> bf16", "l2": L2_NOTE,
+                       "per_format": r["per"]},
+            "roofline": {"bound": "hbm", "peak": r["peak"], "unit": "GB/s",
+                         "mean_frac_of_copy_peak": round(r["mean_frac_copy"], 4),
+                         "min_frac_of_mix_ceiling": round(r["min_frac_mix"], 4),
+                         "kernel": "dequant_kernel (single weight)"},
+            "clocks": r["clk"]}), flush=True)
+
+
+def run_lora(torch, args, world, rank, dist):
+    """§8(f) 1: LoRA-in-dequant (wf_dequant_gguf_lora: w = R_out(dequant + R_out(diff * sa))) on configs[1]'s Q4_K
+    weight with a float32 LoRA difference of the same shape, against the plain dequantisation of the same weight."""
+    ext = _pkg("_ext")
+    lib = ext.lib()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev)
+    flush = L2Flush(torch, dev)
+    n = 5120 * 13824
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(20261201 + 1)
+    src = fill_q4k(torch, n // 256, dev, gen)
+    diff = torch.randn(n, device=dev, generator=gen) * 0.01
+    dst = torch.empty(n, dtype=torch.bfloat16, device=dev)
+
+    def lora():
+        ext.check(lib.wf_dequant_gguf_lora(src.data_ptr(), src.numel(), diff.data_ptr(), dst.data_ptr(), n, 12, 0, 1,
+                                           0.75, stream.cuda_stream), "lora")
+
+    def plain():
+        ext.check(lib.wf_dequant_gguf(src.data_ptr(), src.numel(), dst.data_ptr(), n, 12, 0, 1, stream.cuda_stream),
+                  "plain")
+
+    for _ in range(args.warmup):
+        lora()
+        plain()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ms = time_launches(torch, flush, stream, lora, args.steps)
+        ms_plain = time_launches(torch, flush, stream, plain, args.steps)
+    alg = src.numel() + 4 * n + 2 * n
+    return {"ms": ms, "ms_plain": ms_plain, "alg": alg, "clk": clk.summary(), "n": n}
+
+
+def finish_lora(torch, args, world, rank, dist, r):
+    if rank == 0:
+        peak, kind = measured_peaks()
+        achieved = r["alg"] / (r["ms"] / 1e3) / 1e9
+        print(json.dumps({
+            "metric": "GGUF dequant + LoRA out GB/s", "value": round(2 * r["n"] / (r["ms"] / 1e3) / 1e9, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8 + f32 diff -> bf16",
+            "data": "synthetic (seeded)",
+            "config": {"workload": "Q4_K 5120 x 13824 + float32 LoRA difference (sa 0.75) -> bf16 (configs[1] weight)",
+                       "plain_dequant_ms": round(r["ms_plain"], 4), "l2": L2_NOTE,
+                       "alg_bytes": r["alg"], "bytes": "packed + 4 B of difference + 2 B of output per value"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})",
+                         "kernel": "dequant_kernel<LORA> (single weight)"},
+            "clocks": r["clk"]}), flush=True)
+
+
+def mount_of(path):
+    """(mount point, filesystem type, device) of the longest /proc/mounts entry holding path."""
+    best = ("", "?", "?")
+    try:
+        with open("/proc/mounts") as f:
+            for ln in f:
+                dev, mnt, fstype = ln.split()[:3]
+                if (path == mnt or path.startswith(mnt.rstrip("/") + "/")) and len(mnt) >= len(best[0]):
+                    best = (mnt, fstype, dev)
+    except OSError:
+        pass
+    return {"mount": best[0], "type": best[1], "device": best[2]}
+
+
+def run_ssd(torch, args, world, rank, dist):
+    """§8(f) 4: the SSD tier's read path -- blocks of configs[4]'s size (417,793,024 B) written once to a cache file
+    (O_DIRECT) in a fresh folder under the streaming tier's default cache folder (WEIGHTFERRY_DISK_DIR, else the
+    temp folder), then read back cyclically by a DiskRing (pinned 4 KiB aligned buffers, the probe's best
+    reader-thread count) and copied to a GPU slot on a side stream, as the uploader does; against the drive's own
+    probed read rate over the same folder. Reports the folder's filesystem; deletes its files."""
+    import shutil
+    tiers = "core.tiers."
+    dio, cf, src_mod = _pkg(tiers + "disk_io"), _pkg(tiers + "cache_files"), _pkg(tiers + "sources")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    folder = os.path.join(cf.default_cache_dir(), f"bench_{os.getpid()}")
+    os.makedirs(folder, exist_ok=True)
+    fs = mount_of(folder)
+    n_blocks, block = args.ssd_blocks, 417_793_024
+    try:
+        probe = dio.probe_disk(folder, size_mb=1024, chunk_mb=64, thread_counts=(1, 2, 4))
+        store = cf.DiskBlockStore(cf.new_cache_path(folder), block, n_blocks)
+        st = store.staging()
+        g = torch.Generator()
+        g.manual_seed(20261201 + 4)
+        t0 = time.perf_counter()
+        for i in range(n_blocks):
+            st.copy_(torch.randint(0, 256, (block,), dtype=torch.uint8, generator=g))
+            store.write_block(i, st)
+        store.finalize()
+        write_s = time.perf_counter() - t0
+        ring = src_mod.DiskRing(store, depth=4, pin=True, threads=probe["threads"])
+        slot = torch.empty(block, dtype=torch.uint8, device=dev)
+        cs = torch.cuda.Stream(device=dev)
+        try:
+            for i in range(n_blocks):  # one warm-up cycle
+                view, b = ring.acquire(i)
+                with torch.cuda.stream(cs):
+                    slot.copy_(view, non_blocking=True)
+                    ring.release(b, cs)
+            cs.synchronize()
+            t0 = time.perf_counter()
+            cycles = max(1, args.steps // n_blocks)
+            for _ in range(cycles):
+                for i in range(n_blocks):
+                    view, b = ring.acquire(i)
+                    with torch.cuda.stream(cs):
+                        slot.copy_(view, non_blocking=True)
+                        ring.release(b, cs)
+            cs.synchronize()
+            el = time.perf_counter() - t0
+        finally:
+            ring.close()
+            store.delete()
+    finally:
+        shutil.rmtree(folder, ignore_errors=True)
+    gbs = cycles * n_blocks * block / el / 1e9
+    return {"gbs": gbs, "probe": probe, "cycles": cycles, "fs": fs, "folder": folder, "threads": ring.threads, "n_blocks": n_blocks, "write_gbs": n_blocks * block / write_s
+            / 1e9, "el": el}
+
+
+def finish_ssd(torch, args, world, rank, dist, r):
+    if rank == 0:
+        peak = r["probe"]["gbps"]
+        print(json.dumps({
+            "metric": "SSD tier block read to GPU GB/s", "value": round(r["gbs"], 3), "unit": "GB/s", "n_gpus": world,
+            "steps": r["cycles"] * r["n_blocks"], "warmup": r["n_blocks"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bytes", "data": "synthetic (seeded random bytes)",
+            "config": {"workload": f"{r['n_blocks']} Cosmos-14B Q8_0 blocks of 417,793,024 B in a cache file on the "
+                                   "box's drive, DiskRing depth 4 -> one GPU slot",
+                       "drive_probe": r["probe"], "cache_write_gbs": round(r["write_gbs"], 3),
+                       "folder": r["folder"], "filesystem": r["fs"], "ring_threads": r["threads"],
+                       "timed_s": round(r["el"], 3), "timing": "host wall clock around whole cycles (the copies "
+                                                            "are synchronised at the end)"},
+            "roofline": {"bound": "disk", "achieved": round(r["gbs"], 3), "peak": peak, "unit": "GB/s",
+                         "frac": round(r["gbs"] / peak, 4), "peak_source": "probe_disk of the same folder (O_DIRECT "
+                                                                          "reads, best thread count)"}}),
+              flush=True)
+
+
 # ----------------------------------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="sweep", choices=["sweep", "q8", "q4k", "w8a8", "stack", "prologue"])
+    ap.add_argument("--workload", default="sweep",
+                    choices=["sweep", "q8", "q4k", "w8a8", "stack", "prologue", "formats", "lora", "ssd"])
+    ap.add_argument("--ssd-blocks", type=int, default=8, help="ssd: blocks in the cache file")
     ap.add_argument("--slots", type=int, default=3, help="stack: GPU slots of the streaming ring")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -945,6 +1173,12 @@ def main():
     world, rank, local, dist = setup_dist(torch)
     if args.workload == "sweep":
         r = run_sweep(torch, args, world, rank, dist)
+    elif args.workload == "formats":
+        return finish_formats(torch, args, world, rank, dist, run_formats(torch, args, world, rank, dist))
+    elif args.workload == "lora":
+        return finish_lora(torch, args, world, rank, dist, run_lora(torch, args, world, rank, dist))
+    elif args.workload == "ssd":
+        return finish_ssd(torch, args, world, rank, dist, run_ssd(torch, args, world, rank, dist))
     elif args.workload == "prologue":
         return finish_prologue(torch, args, world, rank, dist, run_prologue(torch, args, world, rank, dist))
     elif args.workload == "stack":
