@@ -371,13 +371,63 @@ __device__ __forceinline__ void stage_chunk(uint8_t *sdst, const uint8_t *gsrc, 
     }
 }
 
+// The chunk's float32 LoRA difference into shared memory by cp.async (16-byte aligned; a chunk holds a whole number
+// of 32-value blocks, so its difference is whole 16-byte units).
+__device__ __forceinline__ void stage_diff(float *sdst, const float *gsrc, int nvalues) {
+    const int units = nvalues >> 2;
+    for (int u = threadIdx.x; u < units; u += kThreads) cp_async16(sdst + 4 * u, gsrc + 4 * u);
+}
+
+// Eight float16 results plus the LoRA difference, written as dtype OUT (float16 or bfloat16):
+// w = R_out(R_out(x) + R_out(diff * sa)) in packed pairs. R_out(x) is the same conversion store8_h makes; the product
+// is rounded to float32 (__fmul_rn) and then to OUT by cvt.rn, as the reference's integer round does for non-NaN
+// values; the sum of two OUT values is exact in float32 whenever their exponents are close (11 + 13 bits for
+// float16, 8 + 16 for bfloat16), and otherwise the smaller one is far below half an ulp of the larger, so one
+// correctly rounded add.rn.{f16x2, bf16x2} equals the reference's float32 add followed by its rounding.
+// dl: the 8 differences, in shared memory when ALIGNED, else in global memory.
+template <int OUT, bool ALIGNED>
+__device__ __forceinline__ void store8_h_lora(void *dst, const __half2 h[4], const float *dl, float sa) {
+    float d[8];
+    if constexpr (ALIGNED) {
+        const float4 a = *reinterpret_cast<const float4 *>(dl);
+        const float4 b = *(reinterpret_cast<const float4 *>(dl) + 1);
+        d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w; d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) d[k] = __ldg(dl + k);
+    }
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float p0 = __fmul_rn(d[2 * i], sa), p1 = __fmul_rn(d[2 * i + 1], sa);
+        if constexpr (OUT == WF_BF16) {
+            const float2 f = __half22float2(h[i]);
+            const __nv_bfloat162 r = __hadd2_rn(__floats2bfloat162_rn(f.x, f.y), __floats2bfloat162_rn(p0, p1));
+            w[i] = *reinterpret_cast<const uint32_t *>(&r);
+        } else {
+            const __half2 r = __hadd2_rn(h[i], __floats2half2_rn(p0, p1));
+            w[i] = *reinterpret_cast<const uint32_t *>(&r);
+        }
+    }
+    if constexpr (ALIGNED) {
+        *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+        uint16_t *ds = static_cast<uint16_t *>(dst);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ds[k] = static_cast<uint16_t>(w[k >> 1] >> (16 * (k & 1)));
+    }
+}
+
 // LORA: the first LoRA difference added on the way out, w = R_out(w + R_out(diff * sa)) (the DEQ branch of the
-// reference's _deq_add, enhancers/gguf_dequant.py:99-133); diff_chunk is the chunk's float32 difference.
+// reference's _deq_add, enhancers/gguf_dequant.py:99-133); diff_chunk is the chunk's float32 difference (in shared
+// memory when ALIGNED, else in global memory).
 template <int QT, int MID, int OUT, bool ALIGNED, bool LORA>
 __device__ __forceinline__ void decode_chunk(const uint8_t *sbuf, void *dst_chunk, int valid_values,
                                              const float *diff_chunk, float sa) {
     constexpr int VPB = Fmt<QT>::VPB, TS = Fmt<QT>::TS;
-    if constexpr (MID == WF_F16 && !LORA && (QT == 12 || QT == 13)) {
+    // the float16 chain stays packed up to the store, with or without LoRA (float32 output: the float path below)
+    constexpr bool kHalf = MID == WF_F16 && (!LORA || OUT != WF_F32);
+    if constexpr (kHalf && (QT == 12 || QT == 13)) {
         // Q4_K / Q5_K: each thread decodes one 32-value sub-block's (ds, dm) into shared memory once per chunk
         // (kChunkValues / 32 == kThreads), so the groups below read it with one load instead of unpacking the
         // 6-bit scales again for every 8 values
@@ -398,7 +448,9 @@ __device__ __forceinline__ void decode_chunk(const uint8_t *sbuf, void *dst_chun
             __half2 h[4];
             decode8_kq<QT>(sbuf + (v / VPB) * TS, v % VPB, *reinterpret_cast<const __half2 *>(&sd.x),
                            *reinterpret_cast<const __half2 *>(&sd.y), h);
-            store8_h<OUT, ALIGNED>(static_cast<uint8_t *>(dst_chunk) + static_cast<size_t>(v) * dtype_size(OUT), h);
+            uint8_t *out = static_cast<uint8_t *>(dst_chunk) + static_cast<size_t>(v) * dtype_size(OUT);
+            if constexpr (LORA) store8_h_lora<OUT, ALIGNED>(out, h, diff_chunk + v, sa);
+            else store8_h<OUT, ALIGNED>(out, h);
         }
         return;
     }
@@ -407,10 +459,12 @@ __device__ __forceinline__ void decode_chunk(const uint8_t *sbuf, void *dst_chun
         const int g = threadIdx.x + i * kThreads;
         const int v = 8 * g;
         if (v >= valid_values) break;
-        if constexpr (MID == WF_F16 && !LORA) {
+        if constexpr (kHalf) {
             __half2 h[4];
             decode8_h<QT>(sbuf + (v / VPB) * TS, v % VPB, h);
-            store8_h<OUT, ALIGNED>(static_cast<uint8_t *>(dst_chunk) + static_cast<size_t>(v) * dtype_size(OUT), h);
+            uint8_t *out = static_cast<uint8_t *>(dst_chunk) + static_cast<size_t>(v) * dtype_size(OUT);
+            if constexpr (LORA) store8_h_lora<OUT, ALIGNED>(out, h, diff_chunk + v, sa);
+            else store8_h<OUT, ALIGNED>(out, h);
             continue;
         }
         float x[8];
@@ -423,9 +477,9 @@ __device__ __forceinline__ void decode_chunk(const uint8_t *sbuf, void *dst_chun
         }
         if constexpr (LORA) {
             float dl[8];
-            if constexpr (ALIGNED) {
-                const float4 a = __ldg(reinterpret_cast<const float4 *>(diff_chunk + v));
-                const float4 b = __ldg(reinterpret_cast<const float4 *>(diff_chunk + v) + 1);
+            if constexpr (ALIGNED) {  // diff_chunk: the chunk's difference, staged in shared memory
+                const float4 a = *reinterpret_cast<const float4 *>(diff_chunk + v);
+                const float4 b = *(reinterpret_cast<const float4 *>(diff_chunk + v) + 1);
                 dl[0] = a.x; dl[1] = a.y; dl[2] = a.z; dl[3] = a.w; dl[4] = b.x; dl[5] = b.y; dl[6] = b.z; dl[7] = b.w;
             } else {
 #pragma unroll
@@ -505,8 +559,12 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
     const int64_t n_chunks = total_chunks(p);
     int64_t c = blockIdx.x;
     if (c >= n_chunks) return;
+    // LORA && ALIGNED: the chunks' differences ride in the same double buffer, after the packed bytes
+    constexpr bool kStageDiff = LORA && ALIGNED;
+    float *sdiff = reinterpret_cast<float *>(smem + 2 * kStride);
     ChunkRef cur = chunk_of<QT, OUT>(p, c);
     stage_chunk<ALIGNED>(smem, cur.src, cur.nbytes);
+    if constexpr (kStageDiff) stage_diff(sdiff, lora_diff(p, c), cur.nvalues);
     cp_async_commit();
     for (int it = 0; c < n_chunks; ++it, c += gridDim.x) {
         const int64_t cn = c + gridDim.x;
@@ -514,12 +572,16 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
         if (cn < n_chunks) {
             nxt = chunk_of<QT, OUT>(p, cn);
             stage_chunk<ALIGNED>(smem + ((it + 1) & 1) * kStride, nxt.src, nxt.nbytes);
+            if constexpr (kStageDiff) stage_diff(sdiff + ((it + 1) & 1) * kChunkValues, lora_diff(p, cn), nxt.nvalues);
         }
         cp_async_commit();
         cp_async_wait<1>();  // this thread's copies of the current chunk have landed
         __syncthreads();     // ... and every other thread's
-        decode_chunk<QT, MID, OUT, ALIGNED, LORA>(smem + (it & 1) * kStride, cur.dst, cur.nvalues,
-                                                  LORA ? lora_diff(p, c) : nullptr, lora_scale(p));
+        const float *dchunk = nullptr;
+        if constexpr (kStageDiff) dchunk = sdiff + (it & 1) * kChunkValues;
+        else if constexpr (LORA) dchunk = lora_diff(p, c);
+        decode_chunk<QT, MID, OUT, ALIGNED, LORA>(smem + (it & 1) * kStride, cur.dst, cur.nvalues, dchunk,
+                                                  lora_scale(p));
         __syncthreads();     // the buffer is free for the chunk after next
         cur = nxt;
     }
@@ -529,7 +591,7 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
 template <int QT, int MID, int OUT, bool ALIGNED, bool LORA = false, typename P>
 int launch(const P &p, int64_t n_chunks, cudaStream_t stream) {
     if (n_chunks <= 0) return WF_OK;
-    constexpr int smem = 2 * buf_stride<QT>();
+    constexpr int smem = 2 * buf_stride<QT>() + (LORA && ALIGNED ? 2 * kChunkValues * 4 : 0);
     auto kern = dequant_kernel<QT, MID, OUT, ALIGNED, LORA, P>;
     // per instantiation and device: resident CTAs per SM (the persistent grid's width)
     static int occ[64] = {0};
@@ -538,7 +600,12 @@ int launch(const P &p, int64_t n_chunks, cudaStream_t stream) {
     if (dev < 0 || dev >= 64) return WF_ERR_DEVICE;
     if (occ[dev] == 0) {
         int o = 0;
-        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, kThreads, smem);
+        cudaError_t e = cudaSuccess;
+        if constexpr (smem > 48 * 1024) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return static_cast<int>(e);
+        }
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, kThreads, smem);
         if (e != cudaSuccess) return static_cast<int>(e);
         occ[dev] = std::max(o, 1);
     }

@@ -169,6 +169,36 @@ def test_lora_golden(cuda, qt, mid, out):
     assert _same(_np_out(w), G[f"lora_q{qt}_m{mid}_o{out}"])
 
 
+@pytest.mark.parametrize("qt", sorted(FMT))
+@pytest.mark.parametrize("diff_offset,out", [(0, 1), (1, 1), (0, 0), (1, 0)])
+def test_lora_many_chunks_vs_oracle(cuda, qt, diff_offset, out):
+    """wf_dequant_gguf_lora over ~4.2 M values (more chunks than the persistent grid holds, so every CTA cycles both
+    staging buffers; the last chunk ragged) against the oracle, bf16 and f16 out; diff_offset 1 moves the float32
+    difference off its 16-byte alignment (the unstaged path). A few differences are huge (their products overflow
+    f16 to infinity, or round to the largest finite value), infinite, or tiny (far below half an ulp of the
+    weight)."""
+    import torch
+    ext = wf("_ext")
+    vpb, ts = FMT[qt]
+    n_blocks = (131_075 if vpb == 32 else 16_401)
+    raw = _blocks(qt, n_blocks, seed=500 + qt)
+    n = n_blocks * vpb
+    rng = np.random.default_rng(600 + qt)
+    diff = (rng.standard_normal(n) * 0.01).astype(np.float32)
+    extreme = np.array([3.4e38, -3.4e38, np.inf, -np.inf, 1.0e5, -1.0e5, 65504 / 0.625, 1e-30, -1e-30, 3e-8],
+                       dtype=np.float32)
+    diff[rng.choice(n, 4096, replace=False)] = rng.choice(extreme, 4096)
+    sa = 0.625
+    src = torch.from_numpy(raw).cuda()
+    dbuf = torch.empty(n + diff_offset, dtype=torch.float32, device="cuda")
+    dbuf[diff_offset:].copy_(torch.from_numpy(diff))
+    w = torch.empty(n, dtype={0: torch.float16, 1: torch.bfloat16}[out], device="cuda")
+    ext.check(ext.lib().wf_dequant_gguf_lora(src.data_ptr(), raw.size, dbuf.data_ptr() + 4 * diff_offset, w.data_ptr(),
+                                             n, qt, 0, out, ctypes.c_float(sa), ext.stream_of(src.device)), "lora")
+    torch.cuda.synchronize()
+    assert _same(_np_out(w), oracle().dequant_gguf(raw, n, qt, 0, out, diff=diff, sa=sa))
+
+
 def test_dequantize_lora_entry_point(cuda):
     """gguf_dequant.dequantize_lora with two plain LoRAs (the torch.mm differences computed once here and handed to
     the oracle, so the comparison is exact)."""
