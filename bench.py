@@ -748,7 +748,7 @@ def run_prologue(torch, args, world, rank, dist):
         ln(x, s1, sh.contiguous(), out_a, 4096, 1e-6, K=2048)
 
     def kernel_b():
-        return sf.rms_rope(q, rope, wq, 1e-6), sf.rms_rope(k, rope, wk, 1e-6)
+        return sf.rms_rope_pair(q, k, rope, wq, wk, 1e-6)
 
     for _ in range(args.warmup):
         flush()
@@ -788,11 +788,11 @@ def run_prologue(torch, args, world, rank, dist):
         copy_b.append(e2.elapsed_time(e3))
     del ca, cb_
     bytes_a = 2 * x.numel() * 2                          # read x + write out (+16 KB parameters)
-    bytes_b = 2 * (q.numel() + k.numel()) * 2 + 2 * rope.numel() * 4  # q, k in + out; the table read per launch
+    bytes_b = 2 * (q.numel() + k.numel()) * 2 + rope.numel() * 4  # q, k in + out; the table (one launch for both)
     step_ms = max_over_ranks(torch, dist, a_ms + b_ms)
     value = sum_over_ranks(torch, dist, (bytes_a + bytes_b) / (step_ms / 1e3) / 1e9)
     return {"value": value, "ms": step_ms, "a_ms": a_ms, "b_ms": b_ms, "bytes_a": bytes_a, "bytes_b": bytes_b,
-            "clk": clk.summary(), "launches": int(sum_over_ranks(torch, dist, 3 * args.steps)),
+            "clk": clk.summary(), "launches": int(sum_over_ranks(torch, dist, 2 * args.steps)),
             "copy_a_us": statistics.median(copy_a) * 1e3, "copy_b_us": 2 * statistics.median(copy_b) * 1e3}
 
 

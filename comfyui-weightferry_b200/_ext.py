@@ -53,6 +53,9 @@ SIGNATURES = {
     "wf_rms_rope128": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int64] * 4
                        + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p] + [ctypes.c_int64] * 3
                        + [ctypes.c_float, ctypes.c_void_p]),
+    "wf_rms_rope128_pair": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4
+                            + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+                            + [ctypes.c_int64] * 3 + [ctypes.c_float, ctypes.c_void_p]),
     "wf_quant_rows": (ctypes.c_int, [ctypes.c_void_p] * 6 + [ctypes.c_int64] * 3
                       + [ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "wf_w8a8_gemm": (ctypes.c_int, [ctypes.c_void_p] * 6 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]),

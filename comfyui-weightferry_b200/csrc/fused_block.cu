@@ -398,69 +398,147 @@ __device__ __forceinline__ void load_rot(const float *fd, int64_t s_i, int64_t s
 }
 
 constexpr int kRopeHeads = 16;  // head rows staged per warp at a time (4 KB)
+constexpr int kRopeWarps = 4;   // warps per CTA (two 4 KB buffers each: 32 KB of shared memory)
+
+// Staging layout of a row block: 16-byte chunk c of row R at chunk (c ^ 2 (R & 1)) of the row, so that the two
+// half-warps (rows of opposite parity, 256 bytes apart: the same banks) read and write disjoint banks.
+__device__ __forceinline__ int rope_swz(int q) { return q ^ (((q >> 4) & 1) << 1); }
+
+// The tensors of one launch: q alone, or q and k (same shape, rotations and weight dtype).
+struct RopeTensors {
+    const __nv_bfloat16 *x[2];
+    const void *w[2];
+    __nv_bfloat16 *out[2];
+};
 
 template <bool F4>
-__global__ void __launch_bounds__(256) rms_rope_kernel(const __nv_bfloat16 *__restrict__ x,
-                                                       const float *__restrict__ f, const void *__restrict__ w,
-                                                       int wdt, __nv_bfloat16 *__restrict__ out, int64_t n_tok,
-                                                       int64_t heads, int64_t tokens, float eps, int64_t s_tok,
-                                                       int64_t s_d, int64_t s_i, int64_t s_j) {
-    // One (batch, token) per warp at a time: up to 16 of its head rows (4 KB) are copied into shared memory with
-    // 16-byte cp.async, the reduction reads the lane layout its order needs (t, t+32, t+64, t+96) from there, the
-    // results go back in place and leave with 16-byte stores; the token's rotations are read once for all its heads.
-    __shared__ __align__(16) __nv_bfloat16 stage[8][kRopeHeads * 128];
+__global__ void __launch_bounds__(kRopeWarps * 32) rms_rope_kernel(const __grid_constant__ RopeTensors t, int n_tensors,
+                                                                   const float *__restrict__ f, int wdt,
+                                                                   int64_t n_tok, int64_t heads, int64_t tokens,
+                                                                   float eps, int64_t s_tok, int64_t s_d, int64_t s_i,
+                                                                   int64_t s_j) {
+    // Work item = (tensor, batch, token, group of up to 16 heads). A warp walks its items with two shared-memory
+    // buffers: the next item's rows (4 KB) are copied in by 16-byte cp.async while the current one is computed. Each
+    // half-warp reduces rows (layout below) reading the values its sums need from shared memory, two rows at a time
+    // so their shuffle chains overlap; the results go back in place and leave with 16-byte stores; the token's
+    // rotations are read once for all heads of the item. q and k in one launch give each warp twice the items (one
+    // ramp and one tail instead of two).
+    __shared__ __align__(16) __nv_bfloat16 stage[kRopeWarps][2][kRopeHeads * 128];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    __nv_bfloat16 *buf = stage[wid];
-    float wv[4];
+    const int64_t n_hc = (heads + kRopeHeads - 1) / kRopeHeads;
+    const int64_t per_tensor = n_tok * n_hc;
+    const int64_t items = per_tensor * n_tensors;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * kRopeWarps;
+    int64_t it = static_cast<int64_t>(blockIdx.x) * kRopeWarps + wid;
+    if (it >= items) return;  // whole warps only; nothing below synchronises the CTA
+    // Half-warp layout: half hf (= lane / 16) of the warp takes rows hh + hf, hh + 2 + hf of each group of four;
+    // its lane L holds values L + 16 k (k = 0..7) of the row, i.e. the partial sums of lanes L (k even) and L + 16
+    // (k odd) of the reference's 32-lane layout. The first level of the reference's shuffle-down tree (t + 16) is
+    // then a local add and the other four levels an xor butterfly inside the half: every lane ends with the bits of
+    // the reference's lane 0, each node being the same two operands (IEEE addition is commutative).
+    const int hf = lane >> 4, L = lane & 15;
+    float wv[2][8];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) wv[k] = load_w(w, wdt, lane + 32 * k);
-    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-    for (int64_t bt = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + wid; bt < n_tok; bt += warps) {
+    for (int k = 0; k < 8; ++k) {
+        wv[0][k] = load_w(t.w[0], wdt, L + 16 * k);
+        wv[1][k] = n_tensors > 1 ? load_w(t.w[1], wdt, L + 16 * k) : 0.f;
+    }
+    // item -> (tensor ti, row block bt, first head h0); returns the item's head count
+    auto rows_of = [&](int64_t item, int &ti, int64_t &bt, int64_t &h0) -> int {
+        ti = item >= per_tensor ? 1 : 0;
+        const int64_t local = item - ti * per_tensor;
+        bt = local / n_hc;
+        h0 = (local - bt * n_hc) * kRopeHeads;
+        return static_cast<int>(heads - h0 < kRopeHeads ? heads - h0 : kRopeHeads);
+    };
+    auto issue = [&](int64_t item, __nv_bfloat16 *dst) {
+        int ti;
+        int64_t bt, h0;
+        const int chunks = rows_of(item, ti, bt, h0) * 16;  // 16-byte chunks of the item's rows
+        const uint4 *src = reinterpret_cast<const uint4 *>(t.x[ti] + (bt * heads + h0) * 128);
+#pragma unroll
+        for (int i = 0; i < kRopeHeads / 2; ++i) {
+            const int q = lane + 32 * i;
+            if (q < chunks) cp_async16(reinterpret_cast<uint4 *>(dst) + rope_swz(q), src + q);
+        }
+        cp_async_commit();
+    };
+    issue(it, stage[wid][0]);
+    for (int p = 0; it < items; it += warps, p ^= 1) {
+        if (it + warps < items) issue(it + warps, stage[wid][p ^ 1]);
+        else cp_async_commit();  // an empty group: wait_group<1> below then still means "this item's copies"
+        int ti;
+        int64_t bt, h0;
+        const int nh = rows_of(it, ti, bt, h0);
         const int64_t tok = bt % tokens;
-        float rot[2][4];
-        load_rot<F4>(f + tok * s_tok + lane * s_d, s_i, s_j, rot[0]);
-        load_rot<F4>(f + tok * s_tok + (lane + 32) * s_d, s_i, s_j, rot[1]);
-        for (int64_t h0 = 0; h0 < heads; h0 += kRopeHeads) {
-            const int nh = static_cast<int>(heads - h0 < kRopeHeads ? heads - h0 : kRopeHeads);
-            const int chunks = nh * 16;  // 16-byte chunks of the nh rows
-            const uint4 *src = reinterpret_cast<const uint4 *>(x + (bt * heads + h0) * 128);
+        float rot[4][4];  // frequencies d = L + 16 k, k = 0..3 (pairs (d, d + 64))
 #pragma unroll
-            for (int i = 0; i < kRopeHeads / 2; ++i)
-                if (lane + 32 * i < chunks) cp_async16(reinterpret_cast<uint4 *>(buf) + lane + 32 * i, src + lane + 32 * i);
-            cp_async_commit();
-            cp_async_wait<0>();
-            __syncwarp();
-            for (int hh = 0; hh < nh; ++hh) {
-                __nv_bfloat16 *rowb = buf + hh * 128;
-                float v[4];
+        for (int k = 0; k < 4; ++k) load_rot<F4>(f + tok * s_tok + (L + 16 * k) * s_d, s_i, s_j, rot[k]);
+        float w[8];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) v[k] = __bfloat162float(rowb[lane + 32 * k]);
-                float a = __fmul_rn(v[0], v[0]);
-                a = __fmaf_rn(v[1], v[1], a);
-                a = __fmaf_rn(v[2], v[2], a);
-                a = __fmaf_rn(v[3], v[3], a);
+        for (int k = 0; k < 8; ++k) w[k] = ti ? wv[1][k] : wv[0][k];
+        cp_async_wait<1>();
+        __syncwarp();
+        __nv_bfloat16 *buf = stage[wid][p];
+        for (int hh = 0; hh < nh; hh += 4) {  // rows hh + hf and hh + 2 + hf (those >= nh computed, not written)
+            float v[2][8], sum[2];
 #pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xFFFFFFFFu, a, off));
-                a = __shfl_sync(0xFFFFFFFFu, a, 0);
-                const float rr = rsqrt_approx(__fadd_rn(__fmul_rn(a, 0.0078125f), eps));
-                const float2 n01 = r16x2(__fmul_rn(__fmul_rn(v[0], rr), wv[0]), __fmul_rn(__fmul_rn(v[1], rr), wv[1]));
-                const float2 n23 = r16x2(__fmul_rn(__fmul_rn(v[2], rr), wv[2]), __fmul_rn(__fmul_rn(v[3], rr), wv[3]));
-                const float n[4] = {n01.x, n01.y, n23.x, n23.y};
+            for (int r = 0; r < 2; ++r) {
+                // value L + 16 k of row R sits at element 16 (k ^ (R & 1)) + L of the row (R & 1 == hf)
+                const __nv_bfloat16 *ev = buf + (hh + 2 * r + hf) * 128 + L + 16 * hf;  // k even
+                const __nv_bfloat16 *od = ev - 32 * hf;                                  // k odd
 #pragma unroll
-                for (int p = 0; p < 2; ++p) {  // d = lane (+ 32): pairs (n[p], n[p + 2]); this lane's own slots
-                    const float lo = n[p], hi = n[p + 2];
-                    rowb[lane + 32 * p] = __float2bfloat16_rn(__fmaf_rn(rot[p][0], lo, __fmul_rn(rot[p][1], hi)));
-                    rowb[lane + 32 * p + 64] = __float2bfloat16_rn(__fmaf_rn(rot[p][2], lo, __fmul_rn(rot[p][3], hi)));
+                for (int k = 0; k < 8; ++k) v[r][k] = __bfloat162float((k & 1) ? od[16 * k] : ev[16 * k]);
+                float a0 = __fmul_rn(v[r][0], v[r][0]), a1 = __fmul_rn(v[r][1], v[r][1]);
+                a0 = __fmaf_rn(v[r][2], v[r][2], a0);
+                a1 = __fmaf_rn(v[r][3], v[r][3], a1);
+                a0 = __fmaf_rn(v[r][4], v[r][4], a0);
+                a1 = __fmaf_rn(v[r][5], v[r][5], a1);
+                a0 = __fmaf_rn(v[r][6], v[r][6], a0);
+                a1 = __fmaf_rn(v[r][7], v[r][7], a1);
+                sum[r] = __fadd_rn(a0, a1);
+            }
+#pragma unroll
+            for (int off = 8; off >= 1; off >>= 1) {
+#pragma unroll
+                for (int r = 0; r < 2; ++r) sum[r] = __fadd_rn(sum[r], __shfl_xor_sync(0xFFFFFFFFu, sum[r], off));
+            }
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int row = hh + 2 * r + hf;
+                const float rr = rsqrt_approx(__fadd_rn(__fmul_rn(sum[r], 0.0078125f), eps));
+                float n[8];
+#pragma unroll
+                for (int k = 0; k < 8; k += 2) {
+                    const float2 nn = r16x2(__fmul_rn(__fmul_rn(v[r][k], rr), w[k]),
+                                            __fmul_rn(__fmul_rn(v[r][k + 1], rr), w[k + 1]));
+                    n[k] = nn.x;
+                    n[k + 1] = nn.y;
+                }
+                if (row < nh) {  // the other half's row may be valid: no warp-wide operation below
+                    __nv_bfloat16 *ev = buf + row * 128 + L + 16 * hf;
+                    __nv_bfloat16 *od = ev - 32 * hf;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {  // pair (d, d + 64), d = L + 16 k (k and k + 4 of one parity)
+                        const float lo = n[k], hi = n[k + 4];
+                        __nv_bfloat16 *e = (k & 1) ? od : ev;
+                        e[16 * k] = __float2bfloat16_rn(__fmaf_rn(rot[k][0], lo, __fmul_rn(rot[k][1], hi)));
+                        e[16 * k + 64] = __float2bfloat16_rn(__fmaf_rn(rot[k][2], lo, __fmul_rn(rot[k][3], hi)));
+                    }
                 }
             }
-            __syncwarp();
-            uint4 *dst = reinterpret_cast<uint4 *>(out + (bt * heads + h0) * 128);
-#pragma unroll
-            for (int i = 0; i < kRopeHeads / 2; ++i)
-                if (lane + 32 * i < chunks) dst[lane + 32 * i] = reinterpret_cast<const uint4 *>(buf)[lane + 32 * i];
-            __syncwarp();
         }
+        __syncwarp();
+        const int chunks = nh * 16;
+        uint4 *dst = reinterpret_cast<uint4 *>(t.out[ti] + (bt * heads + h0) * 128);
+#pragma unroll
+        for (int i = 0; i < kRopeHeads / 2; ++i) {
+            const int q = lane + 32 * i;
+            if (q < chunks) dst[q] = reinterpret_cast<const uint4 *>(buf)[rope_swz(q)];
+        }
+        __syncwarp();  // every lane has read this buffer before it is refilled (the next iteration's issue)
     }
+    cp_async_wait<0>();
 }
 
 // ------------------------------------------------------------------------------------------------- quantiser
@@ -1033,30 +1111,64 @@ extern "C" WF_API int wf_rms_norm_128(const void *x, const void *w, int w_dtype,
     return static_cast<int>(cudaGetLastError());
 }
 
-extern "C" WF_API int wf_rms_rope128(const void *x, const float *freqs, int64_t f_stride_token, int64_t f_stride_d,
-                                    int64_t f_stride_i, int64_t f_stride_j, const void *w, int w_dtype, void *out,
-                                    int64_t batch, int64_t tokens, int64_t heads, float eps, wf_stream_t stream) {
+namespace wf {
+namespace {
+
+int rope_launch(const RopeTensors &t, int n_tensors, const float *freqs, int64_t f_stride_token, int64_t f_stride_d,
+                int64_t f_stride_i, int64_t f_stride_j, int w_dtype, int64_t batch, int64_t tokens, int64_t heads,
+                float eps, wf_stream_t stream) {
     if (batch < 0 || tokens < 0 || heads < 0 || w_dtype < WF_F16 || w_dtype > WF_F32) return WF_ERR_ARG;
-    const int64_t n_rows = batch * tokens * heads;
-    if (n_rows == 0) return WF_OK;
-    if (!x || !freqs || !w || !out || !al(x, 16) || !al(out, 16) || !al(freqs, 4) || !al(w, dtype_size(w_dtype)))
-        return WF_ERR_ARG;
+    if (batch * tokens * heads == 0) return WF_OK;
+    if (!freqs || !al(freqs, 4)) return WF_ERR_ARG;
+    for (int i = 0; i < n_tensors; ++i)
+        if (!t.x[i] || !t.w[i] || !t.out[i] || !al(t.x[i], 16) || !al(t.out[i], 16) || !al(t.w[i], dtype_size(w_dtype)))
+            return WF_ERR_ARG;
     int rc = check_device();
     if (rc != WF_OK) return rc;
     const int64_t n_tok = batch * tokens;
+    const int64_t blocks =
+        (n_tensors * n_tok * ((heads + kRopeHeads - 1) / kRopeHeads) + kRopeWarps - 1) / kRopeWarps;
     const bool f4 = f_stride_j == 1 && f_stride_i == 2 && f_stride_d % 4 == 0 && f_stride_token % 4 == 0 &&
                     al(freqs, 16);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    constexpr int kT = kRopeWarps * 32;
     if (f4) {
-        rms_rope_kernel<true><<<persistent_grid<rms_rope_kernel<true>>(256, 0, (n_tok + 7) / 8), 256, 0, s>>>(
-            static_cast<const __nv_bfloat16 *>(x), freqs, w, w_dtype, static_cast<__nv_bfloat16 *>(out), n_tok, heads,
-            tokens, eps, f_stride_token, f_stride_d, f_stride_i, f_stride_j);
+        rms_rope_kernel<true><<<persistent_grid<rms_rope_kernel<true>>(kT, 0, blocks), kT, 0, s>>>(
+            t, n_tensors, freqs, w_dtype, n_tok, heads, tokens, eps, f_stride_token, f_stride_d, f_stride_i, f_stride_j);
     } else {
-        rms_rope_kernel<false><<<persistent_grid<rms_rope_kernel<false>>(256, 0, (n_tok + 7) / 8), 256, 0, s>>>(
-            static_cast<const __nv_bfloat16 *>(x), freqs, w, w_dtype, static_cast<__nv_bfloat16 *>(out), n_tok, heads,
-            tokens, eps, f_stride_token, f_stride_d, f_stride_i, f_stride_j);
+        rms_rope_kernel<false><<<persistent_grid<rms_rope_kernel<false>>(kT, 0, blocks), kT, 0, s>>>(
+            t, n_tensors, freqs, w_dtype, n_tok, heads, tokens, eps, f_stride_token, f_stride_d, f_stride_i, f_stride_j);
     }
     return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+}  // namespace wf
+
+extern "C" WF_API int wf_rms_rope128(const void *x, const float *freqs, int64_t f_stride_token, int64_t f_stride_d,
+                                    int64_t f_stride_i, int64_t f_stride_j, const void *w, int w_dtype, void *out,
+                                    int64_t batch, int64_t tokens, int64_t heads, float eps, wf_stream_t stream) {
+    wf::RopeTensors t{};
+    t.x[0] = static_cast<const __nv_bfloat16 *>(x);
+    t.w[0] = w;
+    t.out[0] = static_cast<__nv_bfloat16 *>(out);
+    return wf::rope_launch(t, 1, freqs, f_stride_token, f_stride_d, f_stride_i, f_stride_j, w_dtype, batch, tokens,
+                           heads, eps, stream);
+}
+
+extern "C" WF_API int wf_rms_rope128_pair(const void *q, const void *k, const float *freqs, int64_t f_stride_token,
+                                         int64_t f_stride_d, int64_t f_stride_i, int64_t f_stride_j, const void *wq,
+                                         const void *wk, int w_dtype, void *q_out, void *k_out, int64_t batch,
+                                         int64_t tokens, int64_t heads, float eps, wf_stream_t stream) {
+    wf::RopeTensors t{};
+    t.x[0] = static_cast<const __nv_bfloat16 *>(q);
+    t.x[1] = static_cast<const __nv_bfloat16 *>(k);
+    t.w[0] = wq;
+    t.w[1] = wk;
+    t.out[0] = static_cast<__nv_bfloat16 *>(q_out);
+    t.out[1] = static_cast<__nv_bfloat16 *>(k_out);
+    return wf::rope_launch(t, 2, freqs, f_stride_token, f_stride_d, f_stride_i, f_stride_j, w_dtype, batch, tokens,
+                           heads, eps, stream);
 }
 
 extern "C" WF_API int wf_quant_rows(const void *x, const void *s1, const void *shift, const void *gelu_table,

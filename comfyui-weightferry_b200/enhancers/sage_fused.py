@@ -1,5 +1,5 @@
 """RMSNorm-128 + split-half RoPE of the self-attention's q / k (the ``_rope_rows`` / ``rms_rope`` / ``rope_ok`` part
-of enhancers/sage_fused.py of the reference, :159-176, :246-334) on the sm_100a kernel wf_rms_rope128.
+of enhancers/sage_fused.py of the reference, :159-176, :246-334) on the sm_100a kernel wf_rms_rope128 (wf_rms_rope128_pair for q and k in one launch).
 
 The reference reproduces comfy_kitchen's rms_rope_split_half (lane t of 32 owns values t, t+32, t+64, t+96; the
 squares summed by fma; rsqrt.approx; n = bf16((x * rr) * w); pairs (d, d + 64) rotated by a 2x2 float32 matrix per
@@ -40,5 +40,16 @@ def rms_rope(x, f, w, eps):
 
 
 def rms_rope_pair(q, k, f, q_scale, k_scale, eps):
-    """(rms_rope(q), rms_rope(k)): the self-attention's q and k after their norms and the 3D RoPE."""
-    return rms_rope(q, f, q_scale, eps), rms_rope(k, f, k_scale, eps)
+    """(rms_rope(q), rms_rope(k)): the self-attention's q and k after their norms and the 3D RoPE -- one launch for
+    both when they have one shape and their scales one dtype (rope_ok's case), else one launch each."""
+    if q.shape != k.shape or q_scale.dtype != k_scale.dtype or q.device != k.device:
+        return rms_rope(q, f, q_scale, eps), rms_rope(k, f, k_scale, eps)
+    b, L, h, d = q.shape
+    qo, ko = torch.empty_like(q), torch.empty_like(k)
+    with torch.cuda.device(q.device):
+        rc = _ext.lib().wf_rms_rope128_pair(q.data_ptr(), k.data_ptr(), f.data_ptr(), f.stride(1), f.stride(3),
+                                            f.stride(4), f.stride(5), q_scale.data_ptr(), k_scale.data_ptr(),
+                                            _ext.dtype_code(q_scale.dtype), qo.data_ptr(), ko.data_ptr(), b, L, h,
+                                            float(eps), _ext.stream_of(q.device))
+    _ext.check(rc, "wf_rms_rope128_pair")
+    return qo, ko

@@ -341,8 +341,7 @@ def block_forward(x_rows, emb, ctx, rope, W, cfg, tp, batch, tokens, lora_term=N
     q = F.linear(normed, W["self_attn.q_proj.weight"]).view(batch, tokens, Hw, hd)
     k = F.linear(normed, W["self_attn.k_proj.weight"]).view(batch, tokens, Hw, hd)
     v = F.linear(normed, W["self_attn.v_proj.weight"]).view(batch, tokens, Hw, hd)
-    q = _sf.rms_rope(q, rope, W["self_attn.q_norm.weight"], eps)
-    k = _sf.rms_rope(k, rope, W["self_attn.k_norm.weight"], eps)
+    q, k = _sf.rms_rope_pair(q, k, rope, W["self_attn.q_norm.weight"], W["self_attn.k_norm.weight"], eps)
     a = _attention(q, k, v).view(batch * tokens, Hw * hd)
     o = tp.row_parallel_rows(a, W["self_attn.output_proj.weight"])                          # (n, D)
     x_rows = _residual(x_rows, gate, o, row0, tokens)

@@ -118,6 +118,14 @@ WF_API int wf_rms_rope128(const void *x, const float *freqs, int64_t f_stride_to
                           int64_t f_stride_i, int64_t f_stride_j, const void *w, int w_dtype, void *out,
                           int64_t batch, int64_t tokens, int64_t heads, float eps, wf_stream_t stream);
 
+/* wf_rms_rope128 of q and k (same shape, same rotations, weights wq / wk of one dtype) in one launch: the
+ * self-attention's two rms_rope() calls (enhancers/sage_fused.py:325-334, called for q and k by the patched block,
+ * enhancers/fused_block.py:652-703). Bit for bit the two single launches. */
+WF_API int wf_rms_rope128_pair(const void *q, const void *k, const float *freqs, int64_t f_stride_token,
+                               int64_t f_stride_d, int64_t f_stride_i, int64_t f_stride_j, const void *wq,
+                               const void *wk, int w_dtype, void *q_out, void *k_out, int64_t batch, int64_t tokens,
+                               int64_t heads, float eps, wf_stream_t stream);
+
 /* Per-token int8 quantisation of rows of K: q [rows, K] int8, scale [rows] float32 (scale = max(amax / 127,
  * 1e-30)). pre: 0 none, 1 GELU by a 65536-entry bf16 table (gelu_table), 2 modulate (s1, shift), 3 LayerNorm +
  * modulate (K % 512 == 0, K <= 8192); rotate: the 256-wide ConvRot Hadamard (K % 256 == 0) -- the reference always

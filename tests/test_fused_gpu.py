@@ -199,6 +199,50 @@ def test_rms_rope_baseline_vs_oracle(cuda):
         assert ok.all()
 
 
+@pytest.mark.parametrize("heads", [3, 20, 40])
+@pytest.mark.parametrize("strided", [False, True])
+def test_rms_rope_heads_vs_oracle(cuda, heads, strided):
+    """Head counts that are not 16: fewer than one 4-row group (3), more than one 16-head group per token (20, 40 as
+    Cosmos-Predict2-14B), over enough tokens that every warp cycles both staging buffers; strided: a rotation table
+    whose last axis is a slice (the scalar-load path)."""
+    import torch
+    sf = wf("enhancers.sage_fused")
+    g = torch.Generator(device="cuda").manual_seed(77 + heads)
+    B, L = 2, 1031
+    x = torch.randn((B, L, heads, 128), device="cuda", generator=g).to(torch.bfloat16)
+    w = (1 + torch.randn(128, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    fb = torch.randn((1, L, 1, 64, 2, 3 if strided else 2), device="cuda", generator=g)
+    f = fb[..., :2]
+    out = sf.rms_rope(x, f, w, 1e-6)
+    fn = np.ascontiguousarray(f.cpu().numpy())
+    wf32 = w.float().cpu().numpy()
+    ok = oracle().rows_match_some_rstd(_bits(out), lambda kk: oracle().rms_rope128(_bits(x), fn, wf32, heads, L, 1e-6,
+                                                                                  rstd_ulps=kk), 128)
+    assert ok.all()
+
+
+@pytest.mark.parametrize("heads,strided,wdt", [(16, False, "bf16"), (40, True, "f32"), (5, False, "f16")])
+def test_rms_rope_pair_matches_single_launches(cuda, heads, strided, wdt):
+    """wf_rms_rope128_pair (q and k in one launch) gives the bits of two wf_rms_rope128 launches; q / k scales of
+    different dtypes fall back to two launches."""
+    import torch
+    sf = wf("enhancers.sage_fused")
+    dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[wdt]
+    g = torch.Generator(device="cuda").manual_seed(91 + heads)
+    B, L = 2, 515
+    q = torch.randn((B, L, heads, 128), device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn((B, L, heads, 128), device="cuda", generator=g).to(torch.bfloat16) * 3
+    wq = (1 + torch.randn(128, device="cuda", generator=g) * 0.02).to(dt)
+    wk = (1 + torch.randn(128, device="cuda", generator=g) * 0.02).to(dt)
+    fb = torch.randn((1, L, 1, 64, 2, 3 if strided else 2), device="cuda", generator=g)
+    f = fb[..., :2]
+    qo, ko = sf.rms_rope_pair(q, k, f, wq, wk, 1e-6)
+    assert torch.equal(qo.view(torch.int16), sf.rms_rope(q, f, wq, 1e-6).view(torch.int16))
+    assert torch.equal(ko.view(torch.int16), sf.rms_rope(k, f, wk, 1e-6).view(torch.int16))
+    q2, k2 = sf.rms_rope_pair(q, k, f, wq, wk.float() if dt != torch.float32 else wk.half(), 1e-6)
+    assert torch.equal(q2.view(torch.int16), qo.view(torch.int16))
+
+
 @pytest.mark.parametrize("pre", [0, 1, 2, 3])
 def test_quant_rows_golden(cuda, pre):
     import torch
