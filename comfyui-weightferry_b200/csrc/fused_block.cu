@@ -437,12 +437,6 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rms_rope_kernel(const __grid_
     // then a local add and the other four levels an xor butterfly inside the half: every lane ends with the bits of
     // the reference's lane 0, each node being the same two operands (IEEE addition is commutative).
     const int hf = lane >> 4, L = lane & 15;
-    float wv[2][8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        wv[0][k] = load_w(t.w[0], wdt, L + 16 * k);
-        wv[1][k] = n_tensors > 1 ? load_w(t.w[1], wdt, L + 16 * k) : 0.f;
-    }
     // item -> (tensor ti, row block bt, first head h0); returns the item's head count
     auto rows_of = [&](int64_t item, int &ti, int64_t &bt, int64_t &h0) -> int {
         ti = item >= per_tensor ? 1 : 0;
@@ -474,9 +468,9 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rms_rope_kernel(const __grid_
         float rot[4][4];  // frequencies d = L + 16 k, k = 0..3 (pairs (d, d + 64))
 #pragma unroll
         for (int k = 0; k < 4; ++k) load_rot<F4>(f + tok * s_tok + (L + 16 * k) * s_d, s_i, s_j, rot[k]);
-        float w[8];
+        float w[8];  // the tensor's weights at this lane's values (L1 hits after the first item)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) w[k] = ti ? wv[1][k] : wv[0][k];
+        for (int k = 0; k < 8; ++k) w[k] = load_w(t.w[ti], wdt, L + 16 * k);
         cp_async_wait<1>();
         __syncwarp();
         __nv_bfloat16 *buf = stage[wid][p];
