@@ -360,10 +360,14 @@ def hbm_mix_probe(torch, lib, ext, dev, in_bytes, out_bytes, stream):
     return gbs
 
 
+E2E_STREAMS = int(os.environ.get("WEIGHTFERRY_BENCH_E2E_STREAMS", "4"))
+
+
 def e2e_block(torch, gd, dev, args):
     """gguf_dequant.dequantize on one block's 16 Q4_K tensors with pinned host buffers: per step H2D of the packed
-    bytes, the dequantisation, D2H of the bf16 weights (two streams, so one tensor's copies overlap another's
-    dequantisation)."""
+    bytes, the dequantisation, D2H of the bf16 weights (tensors spread over E2E_STREAMS streams, so the device-to-host
+    copies -- 3.6 x the bytes of the host-to-device ones -- always have one queued while other tensors arrive and are
+    dequantised)."""
     shapes = cosmos14b_block_shapes()
     gen = torch.Generator()
     gen.manual_seed(20261201 + 11)
@@ -374,13 +378,13 @@ def e2e_block(torch, gd, dev, args):
         hosts.append(raw.reshape(-1).pin_memory())
         houts.append(torch.empty((a, b), dtype=torch.bfloat16).pin_memory())
         dsrc.append(torch.empty(raw.numel(), dtype=torch.uint8, device=dev))
-    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    streams = [torch.cuda.Stream(dev) for _ in range(E2E_STREAMS)]
     h2d = sum(h.numel() for h in hosts)
     d2h = sum(h.numel() * 2 for h in houts)
 
     def step():
         for i, ((a, b), h) in enumerate(zip(shapes, hosts)):
-            s = streams[i % 2]
+            s = streams[i % len(streams)]
             with torch.cuda.stream(s):
                 dsrc[i].copy_(h, non_blocking=True)
                 w = gd.dequantize(dsrc[i], 12, (a, b), None, torch.bfloat16)
