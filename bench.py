@@ -361,6 +361,7 @@ def hbm_mix_probe(torch, lib, ext, dev, in_bytes, out_bytes, stream):
 
 
 E2E_STREAMS = int(os.environ.get("WEIGHTFERRY_BENCH_E2E_STREAMS", "4"))
+E2E_W8A8_CHUNKS = int(os.environ.get("WEIGHTFERRY_BENCH_E2E_CHUNKS", "8"))
 
 
 def e2e_block(torch, gd, dev, args):
@@ -507,15 +508,28 @@ def run_w8a8(torch, args, world, rank, dist):
 
 def e2e_w8a8(torch, fi, x, wq, ws, dev, args):
     """fused_int8.int8_linear (the package's entry point) with pinned host buffers: per step H2D of X, the linear,
-    D2H of Y."""
+    D2H of Y -- in E2E_W8A8_CHUNKS row chunks on their own streams (per-token quantisation is row by row, so the
+    chunks' results are the rows of the whole linear), so one chunk's device-to-host copy overlaps the next chunk's
+    host-to-device copy and linear."""
     hx = x.cpu().pin_memory()
     hy = torch.empty((x.shape[0], wq.shape[0]), dtype=torch.bfloat16).pin_memory()
     dx = torch.empty_like(x)
+    n_ch = E2E_W8A8_CHUNKS
+    bounds = [x.shape[0] * i // n_ch for i in range(n_ch + 1)]
+    streams = [torch.cuda.Stream(dev) for _ in range(n_ch)]
+    main = torch.cuda.current_stream(dev)
 
     def step():
-        dx.copy_(hx, non_blocking=True)
-        y = fi.int8_linear(dx, wq, ws)
-        hy.copy_(y, non_blocking=True)
+        for i, s in enumerate(streams):
+            s.wait_stream(main)
+            with torch.cuda.stream(s):
+                r0, r1 = bounds[i], bounds[i + 1]
+                dx[r0:r1].copy_(hx[r0:r1], non_blocking=True)
+                y = fi.int8_linear(dx[r0:r1], wq, ws)
+                hy[r0:r1].copy_(y, non_blocking=True)
+                y.record_stream(s)
+        for s in streams:
+            main.wait_stream(s)
 
     for _ in range(max(1, args.warmup)):
         step()
