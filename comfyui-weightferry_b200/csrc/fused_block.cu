@@ -19,6 +19,11 @@ namespace wf {
 namespace {
 
 // ------------------------------------------------------------------------------------------------- helpers
+// The quantisers feed the int8 GEMM, which is launched as a programmatic dependent: signalling at the start of every
+// CTA lets the GEMM's CTAs be launched (and do their set-up) as soon as all quantiser CTAs are running; the GEMM waits
+// for this grid's completion and memory before it reads anything (griddepcontrol.wait). No effect on other launches.
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float rsqrt_approx(float v) {
     float r;
     asm("rsqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(v));
@@ -553,6 +558,7 @@ __global__ void __launch_bounds__(128) quant_rows_kernel(const __nv_bfloat16 *__
                                                          int64_t K, int64_t rows_per_group, float eps) {
     extern __shared__ __align__(16) float srow[];
     __shared__ float red[16];
+    allow_dependents();
     const int64_t row = blockIdx.x;
     const int t = threadIdx.x;
     const __nv_bfloat16 *xr = x + row * K;
@@ -805,6 +811,7 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const __nv_bfloat16
                                                              int64_t rows, int64_t rows_per_group) {
     constexpr int K = 256 * NCH * WPR;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    allow_dependents();
     if constexpr (WPR == 1 && NCH <= 8) {
         const int64_t nw = static_cast<int64_t>(gridDim.x) * 8;
         int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp;
@@ -883,6 +890,7 @@ __global__ void __launch_bounds__(128) quant_lnmod_kernel(const __nv_bfloat16 *_
     __shared__ float red[16];
     __shared__ float amax_w[2][4];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    allow_dependents();
     int64_t row = blockIdx.x;
     if (row >= rows) return;
     uint2 raw[NV];

@@ -31,6 +31,7 @@
 
 #include <cstdlib>
 #include <mutex>
+#include <utility>
 
 namespace wf {
 namespace {
@@ -134,6 +135,12 @@ __device__ __forceinline__ void mma_commit(uint32_t mbar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
                  : "memory");
 }
+
+// Programmatic dependent launch: the kernel is launched while the previous kernel of the stream (the quantiser that
+// writes xq / xs) may still run, so its set-up (barriers, tensor memory, cluster sync) overlaps that kernel's tail;
+// every thread waits here for the previous grid's completion and memory before it touches global memory. Without a
+// programmatic launch this returns at once.
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -376,6 +383,7 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     __syncthreads();
     fence_after();
     const uint32_t tmem_base = s_tmem_base;
+    wait_prior_grid();
     volatile int *abort_flag = &s_abort;
 
     if (warp == 8) {
@@ -579,6 +587,7 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
     cluster_sync();  // barriers initialised and tensor memory allocated in both CTAs
     fence_after();
     const uint32_t tmem_base = s_tmem_base;
+    wait_prior_grid();
     volatile int *abort_flag = &s_abort;
 
     if (warp == 8) {
@@ -700,6 +709,31 @@ EncodeTiled encoder() {
 }
 
 // WEIGHTFERRY_W8A8_1SM=1 keeps every problem on the one-CTA kernel (the pair kernel is used for m > 128 otherwise)
+bool use_pdl() {
+    static const bool pdl = [] {
+        const char *v = getenv("WEIGHTFERRY_PDL");
+        return !(v != nullptr && v[0] == '0');
+    }();
+    return pdl;
+}
+
+// a kernel launch as a programmatic dependent of the previous one in the stream (WEIGHTFERRY_PDL=0: a plain launch)
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kern)(KArgs...), int grid, int threads, size_t smem, cudaStream_t stream,
+                             Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = use_pdl() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 bool use_pair_kernel() {
     static const bool pair = [] {
         const char *v = getenv("WEIGHTFERRY_W8A8_1SM");
@@ -768,9 +802,10 @@ int launch(const CUtensorMap &ma, const void *wq, const CUtensorMap &my, const f
         }
         const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
         const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, clusters[dev]));
-        w8a8_gemm_2sm_kernel<RES><<<grid, THREADS, SMEM2_BYTES, stream>>>(
-            ma, mb2, my, xs, ws, acc_out, res, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
-        return static_cast<int>(cudaGetLastError());
+        const cudaError_t e = launch_dependent(w8a8_gemm_2sm_kernel<RES>, grid, THREADS, SMEM2_BYTES, stream, ma, mb2,
+                                               my, xs, ws, acc_out, res, static_cast<int>(M), static_cast<int>(N),
+                                               static_cast<int>(K));
+        return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
     }
     CUtensorMap mb;
     if ((rc = make_map(&mb, wq, static_cast<int>(N), static_cast<int>(K), BN)) != WF_OK) return rc;
@@ -783,9 +818,9 @@ int launch(const CUtensorMap &ma, const void *wq, const CUtensorMap &my, const f
     }
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, device_sm_count()));
-    w8a8_gemm_kernel<RES><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, my, xs, ws, acc_out, res, static_cast<int>(M),
-                                                                 static_cast<int>(N), static_cast<int>(K));
-    return static_cast<int>(cudaGetLastError());
+    const cudaError_t e = launch_dependent(w8a8_gemm_kernel<RES>, grid, THREADS, SMEM_BYTES, stream, ma, mb, my, xs, ws,
+                                           acc_out, res, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+    return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
