@@ -802,33 +802,40 @@ __device__ __forceinline__ float rotate_chunks(uint4 (&v)[NCH], int lane) {
     return amax;
 }
 
-template <int PRE, int NCH, int WPR, bool ROT = false>
-__global__ void __launch_bounds__(256) quant_rows_reg_kernel(const __nv_bfloat16 *__restrict__ x,
-                                                             const __nv_bfloat16 *__restrict__ s1,
-                                                             const __nv_bfloat16 *__restrict__ sh,
-                                                             const __nv_bfloat16 *__restrict__ gelu,
-                                                             int8_t *__restrict__ q, float *__restrict__ scale_out,
-                                                             int64_t rows, int64_t rows_per_group) {
+template <int PRE, int NCH, int WPR, bool ROT>
+__device__ __forceinline__ void quant_rows_reg_body(const __nv_bfloat16 *__restrict__ x,
+                                                    const __nv_bfloat16 *__restrict__ s1,
+                                                    const __nv_bfloat16 *__restrict__ sh,
+                                                    const __nv_bfloat16 *__restrict__ gelu, int8_t *__restrict__ q,
+                                                    float *__restrict__ scale_out, int64_t rows,
+                                                    int64_t rows_per_group) {
     constexpr int K = 256 * NCH * WPR;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     allow_dependents();
     if constexpr (WPR == 1 && NCH <= 8) {
+        // the next row waits in shared memory (cp.async), not in registers: each lane reads back and refills only
+        // its own 16-byte slots, so the refill needs no synchronisation, and the kernel fits three CTAs per SM
+        __shared__ __align__(16) uint4 nxt[8][NCH][32];
         const int64_t nw = static_cast<int64_t>(gridDim.x) * 8;
         int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp;
-        uint4 v[NCH], nx[NCH];
+        uint4 v[NCH];
         if (row < rows) {
 #pragma unroll
-            for (int j = 0; j < NCH; ++j) nx[j] = __ldg(reinterpret_cast<const uint4 *>(x + row * K) + 32 * j + lane);
+            for (int j = 0; j < NCH; ++j)
+                cp_async16(&nxt[warp][j][lane], reinterpret_cast<const uint4 *>(x + row * K) + 32 * j + lane);
         }
+        cp_async_commit();
         for (; row < rows; row += nw) {
+            cp_async_wait<0>();
 #pragma unroll
-            for (int j = 0; j < NCH; ++j) v[j] = nx[j];
+            for (int j = 0; j < NCH; ++j) v[j] = nxt[warp][j][lane];
             const int64_t nrow = row + nw;
             if (nrow < rows) {
 #pragma unroll
                 for (int j = 0; j < NCH; ++j)
-                    nx[j] = __ldg(reinterpret_cast<const uint4 *>(x + nrow * K) + 32 * j + lane);
+                    cp_async16(&nxt[warp][j][lane], reinterpret_cast<const uint4 *>(x + nrow * K) + 32 * j + lane);
             }
+            cp_async_commit();
             quant_pre<PRE, NCH>(v, s1, sh, gelu, (row / rows_per_group) * K, lane);
             float amax = ROT ? rotate_chunks<NCH>(v, lane) : chunk_amax<NCH>(v);
 #pragma unroll
@@ -874,6 +881,28 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const __nv_bfloat16
             }
         }
     }
+}
+
+template <int PRE, int NCH, int WPR, bool ROT = false>
+__global__ void __launch_bounds__(256) quant_rows_reg_kernel(const __nv_bfloat16 *__restrict__ x,
+                                                             const __nv_bfloat16 *__restrict__ s1,
+                                                             const __nv_bfloat16 *__restrict__ sh,
+                                                             const __nv_bfloat16 *__restrict__ gelu,
+                                                             int8_t *__restrict__ q, float *__restrict__ scale_out,
+                                                             int64_t rows, int64_t rows_per_group) {
+    quant_rows_reg_body<PRE, NCH, WPR, ROT>(x, s1, sh, gelu, q, scale_out, rows, rows_per_group);
+}
+
+// The plain pipelined case (no rotation, one warp per row, K <= 2048) with three CTAs per SM: the next row waits in
+// shared memory, which leaves the registers for 24 warps per SM.
+template <int PRE, int NCH>
+__global__ void __launch_bounds__(256, 3) quant_rows_plain_kernel(const __nv_bfloat16 *__restrict__ x,
+                                                                  const __nv_bfloat16 *__restrict__ s1,
+                                                                  const __nv_bfloat16 *__restrict__ sh,
+                                                                  const __nv_bfloat16 *__restrict__ gelu,
+                                                                  int8_t *__restrict__ q, float *__restrict__ scale_out,
+                                                                  int64_t rows, int64_t rows_per_group) {
+    quant_rows_reg_body<PRE, NCH, 1, false>(x, s1, sh, gelu, q, scale_out, rows, rows_per_group);
 }
 
 // The quantiser with the pending LayerNorm + modulate (pre 3) and no rotation, K = 512 * NV: ln_modulate_kernel's
@@ -965,7 +994,10 @@ int launch_quant_lnmod(const void *x, const void *s1, const void *sh, int8_t *q,
 template <int PRE, int NCH, int WPR, bool ROT = false>
 int launch_quant_reg(const void *x, const void *s1, const void *sh, const void *gelu, int8_t *q, float *sc,
                      int64_t rows, int64_t rpg, cudaStream_t s) {
-    auto kern = quant_rows_reg_kernel<PRE, NCH, WPR, ROT>;
+    auto kern = [] {
+        if constexpr (!ROT && WPR == 1 && NCH <= 8) return quant_rows_plain_kernel<PRE, NCH>;
+        else return quant_rows_reg_kernel<PRE, NCH, WPR, ROT>;
+    }();
     static int per_sm = 0;
     if (per_sm == 0) {
         int n = 0;
