@@ -6,7 +6,6 @@ tensor bin-packing gives every rank a disjoint share whose union is the whole ta
 import os
 import sys
 
-import pytest
 import torch.multiprocessing as mp
 
 from conftest import REPO

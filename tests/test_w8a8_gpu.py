@@ -3,7 +3,6 @@ product of the same int8 operands, its bf16 outputs within 1 bf16 ulp of the flo
 bf16(acc * x_s[m] * w_s[n]), for one tile, ragged edges, many tiles and the BASELINE shape; the kernel's status word
 must read 0 (no pipeline wait ran out of time)."""
 
-import numpy as np
 import pytest
 
 from conftest import wf
