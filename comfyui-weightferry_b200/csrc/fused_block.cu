@@ -135,17 +135,13 @@ __device__ __forceinline__ Welford wcombine(Welford own, Welford oth) {
 }
 
 // PyTorch's vectorized layer-norm statistics of one row, as _ln_stats reproduces them (fused_kernels.py:106-135):
-// this thread's Welford state over its values v (already in its vector order), then shuffle-down merges 16 .. 1,
-// then warps 2, 3 into 0, 1 and 1 into 0. Returns (mean, sigma2 / K) to every thread. 128 threads.
-__device__ __forceinline__ void welford_step(Welford &w, float v) {
-    const float delta = __fsub_rn(v, w.m);
-    w.c = __fadd_rn(w.c, 1.0f);
-    w.m = __fmaf_rn(delta, __fdiv_rn(1.0f, w.c), w.m);
-    w.s = __fmaf_rn(delta, __fsub_rn(v, w.m), w.s);
-}
-
-// The same update when this is the thread's i-th value (i = 0, 1, ...): the count is i + 1 for every thread, so the
-// correctly rounded 1 / count comes from a table (the host's IEEE division of 1 by i + 1: the same bits as div.rn).
+// each thread's Welford state over its values (in its vector order), then shuffle-down merges 16 .. 1, then warps
+// 2, 3 into 0, 1 and 1 into 0 (ln_merge_n below); (mean, sigma2 / K) to every thread of the 128.
+//
+// One Welford update (fused_kernels.py:118-121: delta = v - m, c += 1, m = fma(delta, 1 / c, m),
+// s = fma(delta, v - m, s)) when this is the thread's i-th value (i = 0, 1, ...): the count is i + 1 for every
+// thread, so the correctly rounded 1 / count comes from a table (the host's IEEE division of 1 by i + 1: the same
+// bits as div.rn).
 struct RcpTable {
     float v[64];
 };
