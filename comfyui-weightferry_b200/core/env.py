@@ -19,6 +19,7 @@ DEFAULTS = {
     "WEIGHTFERRY_PROFILE": None,           # 1: CUDA-event timeline of the streaming pipeline
     "WEIGHTFERRY_AUTO": None,              # 1: the streaming node chooses resident blocks as with auto_config
     "WEIGHTFERRY_AUTO_HEADROOM_MB": "1536",  # VRAM auto_config leaves for activations
+    "WEIGHTFERRY_VRAM_BUDGET_GB": None,    # most VRAM this process may use (the node's vram_budget_gb wins when > 0)
     "WEIGHTFERRY_TIERING": None,           # auto / ram: overrides the streaming node's tiering option
     "WEIGHTFERRY_RAM_BUDGET_GB": None,     # pinned-RAM budget of the streamed blocks (None: the node's option)
     "WEIGHTFERRY_RAM_MARGIN_GB": "6",      # RAM kept free when the budget is the available RAM

@@ -31,8 +31,9 @@ DiskRing of pinned buffers and the uploader thread (streaming/ssd_uploader.py), 
 parameters rest on a mapping of the cache file.
 
 Options of the reference that select parts outside the quantized-weight path -- chunk streaming, self-managed
-resident blocks, SageAttention, the fp8 storage host format, the VRAM budget -- are accepted and logged as not used
-here. "Single Buffer (Synchronous)" issues each block's transfer when the block starts (no look-ahead)."""
+resident blocks, SageAttention, the fp8 storage host format -- are accepted and logged as not used
+here. "Single Buffer (Synchronous)" issues each block's transfer when the block starts (no look-ahead). A VRAM budget
+(vram_budget_gb or WEIGHTFERRY_VRAM_BUDGET_GB) bounds what the automatic resident-block choice counts as usable."""
 
 import torch
 
@@ -142,6 +143,28 @@ def auto_resident(num_blocks, block_bytes, slot_bytes, nonblock_bytes, usable, h
     slots = (max(2, int(prefetch_slots)) if is_double else 2) * slot_bytes
     resident = int((usable - headroom - nonblock_bytes - slots) // max(1, block_bytes))
     return max(1, min(num_blocks - 1, resident))
+
+
+def vram_budget_bytes(node_gb):
+    """The VRAM budget in bytes (core/vram_budget.py:35-43 of the reference): the node's vram_budget_gb when > 0,
+    else WEIGHTFERRY_VRAM_BUDGET_GB, else None (no budget: every free byte is used)."""
+    gb = float(node_gb or 0.0)
+    if gb <= 0:
+        try:
+            gb = float(_env.get("WEIGHTFERRY_VRAM_BUDGET_GB") or 0)
+        except ValueError:
+            gb = 0.0
+    return int(gb * 1024 ** 3) if gb > 0 else None
+
+
+def budget_usable(free_plus_cached, process_in_use, budget):
+    """The VRAM the resident-block plan may count on: free + PyTorch's cached bytes, and with a budget at most what the
+    budget leaves beside what this process already uses (the reference keeps that much free by raising ComfyUI's
+    reserve, streaming/auto_config.py:52-54; here the plan itself stays inside it). The budget only moves which
+    blocks stream, never the output."""
+    if budget is None:
+        return int(free_plus_cached)
+    return max(0, min(int(free_plus_cached), int(budget) - int(process_in_use)))
 
 
 class _PageableHost:
@@ -402,8 +425,7 @@ class WeightFerryDiT:
             return (model,)
         unused = [n for n, on in (("sage_attention", sage_attention), ("sage_pv_fp16", sage_pv_fp16),
                                   ("host_format=storage", host_format == HOST_FORMAT_STORAGE),
-                                  ("resident_mode=self", resident_mode == RESIDENT_MODE_SELF),
-                                  ("vram_budget_gb", vram_budget_gb > 0)) if on]
+                                  ("resident_mode=self", resident_mode == RESIDENT_MODE_SELF)) if on]
         if unused:
             log_info(f"DiT Layer Streaming: not used by this build: {', '.join(unused)}.")
 
@@ -433,7 +455,8 @@ class WeightFerryDiT:
         compute_dtype = getattr(getattr(patcher, "model", None), "manual_cast_dtype", None) or torch.bfloat16
 
         if auto_config or _env.get("WEIGHTFERRY_AUTO") == "1":
-            auto = self._auto(dit, blocks, device, prefetch_slots, is_double, compute_dtype)
+            auto = self._auto(dit, blocks, device, prefetch_slots, is_double, compute_dtype,
+                              vram_budget_bytes(vram_budget_gb))
             if auto is None:
                 log_info("DiT Layer Streaming [auto]: the whole model fits in VRAM; streaming not used.")
                 return (patcher,)
@@ -462,7 +485,7 @@ class WeightFerryDiT:
         return (patcher,)
 
     @staticmethod
-    def _auto(dit, blocks, device, prefetch_slots, is_double, compute_dtype):
+    def _auto(dit, blocks, device, prefetch_slots, is_double, compute_dtype, budget=None):
         block_ids = {id(p) for blk in blocks for p in blk.parameters()}
         block_bytes = max(sum(_nbytes(_raw(p)) for p in blk.parameters()) for blk in blocks)
         nonblock = sum(_nbytes(_raw(p)) for p in dit.parameters() if id(p) not in block_ids)
@@ -471,8 +494,13 @@ class WeightFerryDiT:
         free, _total = torch.cuda.mem_get_info(device)
         stats = torch.cuda.memory_stats(device)
         cached = stats.get("reserved_bytes.all.current", 0) - stats.get("active_bytes.all.current", 0)
+        in_use = stats.get("active_bytes.all.current", 0)
         headroom = int(_env.get("WEIGHTFERRY_AUTO_HEADROOM_MB")) * 1024 ** 2
-        return auto_resident(len(blocks), block_bytes, lay.flat_bytes + lay.weight_bytes, nonblock, free + cached,
+        usable = budget_usable(free + cached, in_use, budget)
+        if budget is not None:
+            log_info(f"DiT Layer Streaming [auto]: VRAM budget {budget / 1024 ** 3:.2f} GB -> "
+                     f"{usable / 1024 ** 2:.0f} MB usable (free + cached {(free + cached) / 1024 ** 2:.0f} MB).")
+        return auto_resident(len(blocks), block_bytes, lay.flat_bytes + lay.weight_bytes, nonblock, usable,
                              headroom, prefetch_slots, is_double)
 
 

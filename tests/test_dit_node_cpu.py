@@ -88,6 +88,30 @@ def test_auto_resident():
     assert dn.auto_resident(10, 1 * mb, 1, 0, 10 * mb, 1, 2, True) == 9
 
 
+def test_vram_budget(monkeypatch):
+    """vram_budget_gb (or WEIGHTFERRY_VRAM_BUDGET_GB; the node's value wins when > 0) bounds the usable VRAM of the
+    resident-block plan to the budget minus what the process already uses; no budget leaves it at free + cached."""
+    dn = _node()
+    gb, mb = 1024 ** 3, 1024 ** 2
+    monkeypatch.delenv("WEIGHTFERRY_VRAM_BUDGET_GB", raising=False)
+    assert dn.vram_budget_bytes(0.0) is None
+    assert dn.vram_budget_bytes(2.5) == int(2.5 * gb)
+    monkeypatch.setenv("WEIGHTFERRY_VRAM_BUDGET_GB", "4")
+    assert dn.vram_budget_bytes(0.0) == 4 * gb
+    assert dn.vram_budget_bytes(1.0) == 1 * gb
+    monkeypatch.setenv("WEIGHTFERRY_VRAM_BUDGET_GB", "x")
+    assert dn.vram_budget_bytes(0.0) is None
+    assert dn.budget_usable(3000 * mb, 500 * mb, None) == 3000 * mb
+    assert dn.budget_usable(3000 * mb, 500 * mb, 2000 * mb) == 1500 * mb   # the budget binds
+    assert dn.budget_usable(1000 * mb, 500 * mb, 4000 * mb) == 1000 * mb   # more budget than the device gives
+    assert dn.budget_usable(1000 * mb, 5000 * mb, 4000 * mb) == 0          # already past the budget
+    # the plan follows: 1500 usable -> 5 resident blocks (as test_auto_resident), 3000 -> all fit
+    assert dn.auto_resident(10, 100 * mb, 150 * mb, 50 * mb, dn.budget_usable(3000 * mb, 500 * mb, 2000 * mb),
+                            500 * mb, 3, True) == 5
+    assert dn.auto_resident(10, 100 * mb, 150 * mb, 50 * mb, dn.budget_usable(3000 * mb, 500 * mb, None),
+                            500 * mb, 3, True) is None
+
+
 def test_apply_streaming_passthrough():
     dn = _node()
     node = dn.WeightFerryDiT()
