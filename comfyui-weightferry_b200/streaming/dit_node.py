@@ -30,9 +30,9 @@ blocks, interleaved among the others, are written to a cache file (O_DIRECT) and
 DiskRing of pinned buffers and the uploader thread (streaming/ssd_uploader.py), which also dequantises them; their
 parameters rest on a mapping of the cache file.
 
-Options of the reference that select parts outside the quantized-weight path -- chunk streaming, self-managed
-resident blocks, SageAttention, the fp8 storage host format -- are accepted and logged as not used
-here. "Single Buffer (Synchronous)" issues each block's transfer when the block starts (no look-ahead). A VRAM budget
+Options of the reference that select parts outside the quantized-weight path -- chunk streaming, SageAttention,
+the fp8 storage host format -- are accepted and logged as not used here. resident_mode "Self-managed" dequantises the
+resident blocks' GGUF weights once and binds them for each whole forward. "Single Buffer (Synchronous)" issues each block's transfer when the block starts (no look-ahead). A VRAM budget
 (vram_budget_gb or WEIGHTFERRY_VRAM_BUDGET_GB) bounds what the automatic resident-block choice counts as usable."""
 
 import torch
@@ -59,6 +59,7 @@ HOST_FORMAT_STORAGE = "Storage dtype (fp8), LoRA on GPU (half transfer)"
 _BLOCK_LIST_ATTRS = ("blocks", "transformer_blocks", "layers", "block")
 _STATE_ATTR = "_weightferry_stream_state"
 _MID_CODE = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
+_MID_DTYPE = {v: k for k, v in _MID_CODE.items()}
 
 
 def _blocks(dit):
@@ -182,8 +183,11 @@ class _NodeState:
     """One streaming configuration of a diffusion model: the captured blocks, their rest binding and the slot ring."""
 
     def __init__(self, owner, dit, stream_idx, device, pin_memory, num_slots, lookahead, compute_dtype,
-                 tiering_auto=False, ram_budget_bytes=None):
+                 tiering_auto=False, ram_budget_bytes=None, self_resident=False):
         self.owner = owner
+        self.self_resident = self_resident
+        self.res_entries = []  # self-managed resident GGUF weights: (param, packed data, dequantised weight, tensor_type)
+        self.res_bound = False
         self.tiering_auto = tiering_auto
         self.ram_budget_bytes = ram_budget_bytes
         self.tier_plan = None
@@ -276,6 +280,51 @@ class _NodeState:
                     return False
         return bool(self.entries)
 
+    # ------------------------------------------------------------------------------------------------ resident blocks
+    def build_resident(self):
+        """Self-managed resident blocks (the reference's RESIDENT_MODE_SELF, streaming/state.py:80-95): the GGUF
+        weights of the blocks that do not stream are dequantised once, in one batched launch per (type, intermediate
+        precision), into GPU tensors of the compute dtype -- the bits their layers' per-use dequantisation gives --
+        and bound for each whole forward instead of being dequantised at every use. Weights the streamed path would
+        keep packed (LoRA patches, other intermediate precisions) stay packed here too. Their VRAM stays occupied
+        for the whole generation."""
+        self.unbind_resident()
+        self.res_entries = []
+        if not self.self_resident:
+            return
+        from ..enhancers import gguf_dequant as _gd
+        stream = set(self.stream_idx)
+        groups = {}
+        for i, blk in enumerate(_blocks(self.dit)):
+            if i in stream:
+                continue
+            for name, p in blk.named_parameters():
+                sp, d = param_spec(name, p, _param_owner(blk, name), self.compute_dtype)
+                if d:
+                    groups.setdefault((sp.qtype, sp.mid), []).append((p, sp))
+        for (qt, mid), items in groups.items():
+            packed = [(_raw(p).reshape(-1).to(self.device), sp.shape) for p, sp in items]
+            outs = _gd.dequantize_many(packed, qt, _MID_DTYPE[mid], self.compute_dtype)
+            for (p, _sp), w in zip(items, outs):
+                self.res_entries.append((p, p.data, w, getattr(p, "tensor_type", None)))
+
+    def resident_intact(self):
+        return all(p.data_ptr() == packed.data_ptr() for p, packed, _w, _tt in self.res_entries)
+
+    def bind_resident(self):
+        for p, _packed, w, _tt in self.res_entries:
+            p.data = w
+            p.tensor_type = None  # a plain tensor for the whole forward: used as it is
+        self.res_bound = bool(self.res_entries)
+
+    def unbind_resident(self):
+        if not self.res_bound:
+            return
+        for p, packed, _w, tt in self.res_entries:
+            p.data = packed
+            p.tensor_type = tt
+        self.res_bound = False
+
     def _plan_tiers(self, num_stream, block_bytes):
         """With tiering "Auto": how many streamed blocks go to the SSD (core/tiers/plan.plan_tiers), their positions
         (interleaved) and the cache file that holds them."""
@@ -351,14 +400,20 @@ class _NodeState:
             for k in list(self.bound):
                 self._restore(k)
             torch.cuda.synchronize(self.device)
+        self.unbind_resident()  # (still bound when the last forward raised)
         if self.ring is None or not self.bindings_intact():
             log_info("DiT Layer Streaming: the streamed weights were rebound; capturing them again.")
             self.capture()
+            self.build_resident()
+        elif not self.resident_intact():
+            self.build_resident()
+        self.bind_resident()
         self.ring.begin_forward()
         if self.lookahead:
             self.ring.prefetch_first_slots()
 
     def _dit_post(self, module, args, output):
+        self.unbind_resident()
         if self.ring is not None:
             self.ring.end_forward()
 
@@ -368,6 +423,8 @@ class _NodeState:
         for h in self.handles:
             h.remove()
         self.handles = []
+        self.unbind_resident()
+        self.res_entries = []
         for entries in self.entries:
             for p, _name, d, rest, tt in entries:
                 p.data = rest.to(self.device)
@@ -424,8 +481,7 @@ class WeightFerryDiT:
             log_info("DiT Layer Streaming: Disabled, passing original model.")
             return (model,)
         unused = [n for n, on in (("sage_attention", sage_attention), ("sage_pv_fp16", sage_pv_fp16),
-                                  ("host_format=storage", host_format == HOST_FORMAT_STORAGE),
-                                  ("resident_mode=self", resident_mode == RESIDENT_MODE_SELF)) if on]
+                                  ("host_format=storage", host_format == HOST_FORMAT_STORAGE)) if on]
         if unused:
             log_info(f"DiT Layer Streaming: not used by this build: {', '.join(unused)}.")
 
@@ -474,14 +530,18 @@ class WeightFerryDiT:
         env_budget = _env.get("WEIGHTFERRY_RAM_BUDGET_GB")
         ram_budget_bytes = int(float(env_budget if env_budget else ram_budget_gb) * 1024 ** 3) or None
         st = _NodeState(object(), dit, stream_idx, device, pin_memory, num_slots, is_double, compute_dtype,
-                        tiering_auto=tiering_auto, ram_budget_bytes=ram_budget_bytes)
+                        tiering_auto=tiering_auto, ram_budget_bytes=ram_budget_bytes,
+                        self_resident=resident_mode == RESIDENT_MODE_SELF)
         st.capture()
+        st.build_resident()
         st.install_hooks()
         setattr(dit, _STATE_ATTR, st)
         n_deq = sum(1 for _p, _n, d, _r, _t in st.entries[0] if d)
         log_info(f"DiT Layer Streaming: {resident_k}/{num_blocks} resident, {len(stream_idx)} streaming blocks, "
                  f"pin_memory={pin_memory}, double_buffer={is_double}, slots={st.ring.num_slots}; per block "
-                 f"{st.layout.flat_bytes / 1024 ** 2:.1f} MB host, {n_deq} GGUF weights dequantised on arrival.")
+                 f"{st.layout.flat_bytes / 1024 ** 2:.1f} MB host, {n_deq} GGUF weights dequantised on arrival"
+                 + (f"; self-managed resident blocks: {len(st.res_entries)} GGUF weights dequantised once."
+                    if st.self_resident else "."))
         return (patcher,)
 
     @staticmethod

@@ -133,6 +133,51 @@ def test_streamed_gguf_dit_is_bit_exact(gguf_patch, opts):
         assert torch.equal(dit(x), ref)
 
 
+@pytest.mark.parametrize("n_res", [1, 2])
+def test_self_managed_resident_blocks(gguf_patch, n_res):
+    """resident_mode "Self-managed": the resident blocks' GGUF weights are dequantised once and bound for each whole
+    forward -- the same bits as the layers' per-use dequantisation, no per-use dequantisation left, the packed
+    weights back between forwards (also after a forward that raised), and teardown leaves a working model."""
+    import torch
+    dn = wf("streaming.dit_node")
+    dit = _dit(torch)
+    x = _x(torch)
+    with torch.inference_mode():
+        ref = dit(x)
+    packed = {id(p): (p.data_ptr(), p.tensor_type) for i in range(n_res) for p in dit.blocks[i].parameters()
+              if getattr(p, "tensor_type", None) is not None}
+    (patcher,) = dn.WeightFerryDiT().apply_streaming(_Patcher(dit, torch), resident_blocks=n_res,
+                                                      resident_mode=dn.RESIDENT_MODE_SELF)
+    st = dit._weightferry_stream_state
+    assert st.self_resident and len(st.res_entries) == 2 * n_res  # up (Q8_0, f16 mid) and down (Q4_K, "target")
+    seen = []
+    h = dit.blocks[0].register_forward_pre_hook(
+        lambda m, a: seen.append(all(getattr(p, "tensor_type", None) is None and p.dtype == torch.bfloat16
+                                     for n, p in m.named_parameters() if n.endswith("weight") and "norm" not in n)))
+    gguf_patch.stats(reset=True)
+    with torch.inference_mode():
+        out1 = dit(x)
+        out2 = dit(x)
+    torch.cuda.synchronize()
+    h.remove()
+    assert torch.equal(out1, ref) and torch.equal(out2, ref)
+    assert seen == [True, True]                       # bound during the forward
+    assert gguf_patch.stats()["used"] == 0            # nothing dequantised per use
+    assert all((p.data_ptr(), p.tensor_type) == packed[id(p)] for i in range(n_res)
+               for p in dit.blocks[i].parameters() if id(p) in packed)  # packed again between forwards
+    dit.blocks[n_res - 1].fail = True                  # a forward that raises inside a resident block
+    with pytest.raises(RuntimeError):
+        with torch.inference_mode():
+            dit(x)
+    with torch.inference_mode():
+        assert torch.equal(dit(x), ref)
+    dn.teardown(dit)
+    assert all((p.data_ptr(), p.tensor_type) == packed[id(p)] for i in range(n_res)
+               for p in dit.blocks[i].parameters() if id(p) in packed)
+    with torch.inference_mode():
+        assert torch.equal(dit(x), ref)
+
+
 def test_streamed_slot_weights_are_the_layers_dequantisation(gguf_patch):
     """Inside a streamed block the bound weights are exactly what the layer's own dequantisation gives."""
     import torch
