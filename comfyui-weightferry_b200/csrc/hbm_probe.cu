@@ -6,10 +6,12 @@
 // out[j] = in[floor(j * r)] ^ j for every 16-byte unit j of the output, r = n_in / n_out rounded down to a 32.32
 // fixed-point number (so the input index never reaches n_in). The structure of the dequantisation without its
 // arithmetic: a CTA takes 2048 output units at a time, stages the input units they need (each read from DRAM once,
-// coalesced) in shared memory, and writes the 2048 units with coalesced 16-byte stores; persistent grid of CTAs of 256
-// threads, as many per SM as fit.
+// coalesced) in shared memory, and writes the 2048 units with coalesced 16-byte stores; CTAs of 256 threads, about
+// four tiles each.
 
 #include "wf_common.cuh"
+
+#include <algorithm>
 
 namespace wf {
 namespace {
@@ -56,7 +58,11 @@ extern "C" WF_API int wf_hbm_probe(const void *in, int64_t in_bytes, void *out, 
         if (e != cudaSuccess) return static_cast<int>(e);
         per_sm = n > 0 ? n : 1;
     }
-    const int grid = wf::device_sm_count() * per_sm;
+    // about four tiles per CTA, never fewer CTAs than fit at once (the dequantisation kernels' grid rule: the HBM
+    // sustains more of a write-heavy mix with many short-lived CTAs than with one persistent wave)
+    const int64_t n_tiles = (n_out + wf::kTileOut - 1) / wf::kTileOut;
+    const int64_t resident = static_cast<int64_t>(wf::device_sm_count()) * per_sm;
+    const int grid = static_cast<int>(std::min<int64_t>(n_tiles, std::max<int64_t>(resident, (n_tiles + 3) / 4)));
     wf::hbm_probe_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint4 *>(in), n_in, ratio_fp, static_cast<uint4 *>(out), n_out);
     return static_cast<int>(cudaGetLastError());
