@@ -1,0 +1,61 @@
+"""bench.py's host-side pieces without a GPU: its command line accepts every workload, its GGML geometry table agrees
+with the library's own table and the oracle's, its synthetic GGUF blocks carry finite float16 scales, and the SSD
+workload can name the filesystem it measures."""
+
+import ctypes
+import importlib
+import os
+import subprocess
+import sys
+
+import numpy as np
+import torch
+
+from conftest import REPO, wf
+
+
+def _bench():
+    sys.path.insert(0, REPO)
+    try:
+        return importlib.import_module("bench")
+    finally:
+        sys.path.remove(REPO)
+
+
+def test_command_line_lists_every_workload():
+    out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--help"], capture_output=True, text=True,
+                         timeout=120, cwd=REPO)
+    assert out.returncode == 0, out.stderr
+    for w in ("sweep", "q8", "q4k", "w8a8", "stack", "prologue", "formats", "lora", "ssd"):
+        assert w in out.stdout
+    assert "--impl" in out.stdout and "--ssd-blocks" in out.stdout
+
+
+def test_gguf_geometry_matches_the_library_and_the_oracle():
+    bench = _bench()
+    lib = wf("_ext").lib()
+    from oracle import oracle
+    for qt, (_name, vpb, ts, f16) in bench.GGUF_GEOMETRY.items():
+        a, b = ctypes.c_int(0), ctypes.c_int(0)
+        assert lib.wf_gguf_block_info(qt, ctypes.byref(a), ctypes.byref(b)) == 0
+        assert (a.value, b.value) == (vpb, ts)
+        assert all(0 <= off <= ts - 2 for off in f16)
+        raw = np.zeros(2 * ts, dtype=np.uint8)  # two all-zero blocks: a valid input of this type
+        assert oracle.dequant_gguf(raw, 2 * vpb, qt, 0, 1).size == 2 * vpb
+
+
+def test_fill_gguf_scales_are_finite():
+    bench = _bench()
+    gen = torch.Generator().manual_seed(5)
+    for qt, (_name, vpb, ts, f16) in bench.GGUF_GEOMETRY.items():
+        raw = bench.fill_gguf(torch, qt, 4 * vpb, torch.device("cpu"), gen).numpy().reshape(4, ts)
+        for off in f16:
+            d = raw[:, off:off + 2].copy().view(np.float16).astype(np.float32)
+            assert np.all(np.isfinite(d)) and np.all(d >= 0) and np.all(d <= 0.01)
+
+
+def test_mount_of_names_a_filesystem():
+    bench = _bench()
+    m = bench.mount_of(REPO)
+    assert set(m) == {"mount", "type", "device"}
+    assert REPO.startswith(m["mount"].rstrip("/") or "/")
