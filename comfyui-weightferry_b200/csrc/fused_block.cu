@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
                                                           const __nv_bfloat16 *__restrict__ sh,
                                                           __nv_bfloat16 *__restrict__ out, int64_t rows, int64_t K,
                                                           int64_t rows_per_group, float eps) {
-    __shared__ float red[16];
+    __shared__ float red[2][16];  // two buffers: row i + 1's statistics never overwrite what row i still reads
     const int t = threadIdx.x;
     int64_t row = blockIdx.x;
     if (row >= rows) return;
@@ -299,7 +299,8 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
     for (int j = 0; j < NV; ++j) raw[j] = __ldg(reinterpret_cast<const uint2 *>(x + row * K) + t + 128 * j);
     uint2 sraw[NV], hraw[NV];
     int64_t cached_group = -1;
-    for (; row < rows; row += gridDim.x) {
+    int parity = 0;
+    for (; row < rows; row += gridDim.x, parity ^= 1) {
         float v[NV * 4];
 #pragma unroll
         for (int j = 0; j < NV; ++j) unpack4(raw[j], v + 4 * j);
@@ -319,7 +320,7 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
             }
         }
         float mu, var;
-        ln_stats_n<NV * 4>(v, K, mu, var, red);
+        ln_stats_n<NV * 4>(v, K, mu, var, red[parity]);  // its two barriers are the row's only ones
         const float rstd = rsqrt_approx(__fadd_rn(var, eps));
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
@@ -331,7 +332,6 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
             *reinterpret_cast<uint2 *>(out + row * K + c) =
                 make_uint2(mod_bf16x2(n01, sraw[j].x, hraw[j].x), mod_bf16x2(n23, sraw[j].y, hraw[j].y));
         }
-        __syncthreads();  // red[] is reused by the next row's statistics
     }
 }
 
