@@ -8,7 +8,7 @@
 // Data movement (HBM-bound; one read of the packed bytes, one write of the values):
 //   * a "chunk" is 8192 values: 256 legacy blocks or 32 super-blocks; its packed bytes are a multiple of 16 and
 //     start 16-byte aligned whenever the tensor does;
-//   * the grid walks the chunks, about four per CTA (at least one full wave of resident CTAs); each CTA
+//   * the grid walks the chunks, about eight per CTA (at least one full wave of resident CTAs); each CTA
 //     double-buffers them in shared memory with 16-byte cp.async (the next chunk's bytes are in flight while the
 //     current one is decoded);
 //   * a thread decodes 8 consecutive values of one block from shared memory and writes them with one 16-byte store
@@ -25,7 +25,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kChunkValues = 8192;
 constexpr int kGroupsPerThread = kChunkValues / 8 / kThreads;  // 4
-constexpr int64_t kChunksPerCta = 4;                            // target chunks per CTA of a launch
+constexpr int64_t kChunksPerCta = 8;                            // target chunks per CTA of a launch
 constexpr int kMaxBatch = 640;  // tensors per batched launch (a 36-block checkpoint shard fits one; ~20 KB of parameters)
 
 // ------------------------------------------------------------------------------------------------- formats
@@ -613,8 +613,9 @@ int launch(const P &p, int64_t n_chunks, cudaStream_t stream) {
     }
     // about kChunksPerCta chunks per CTA, never fewer CTAs than fit at once: many short-lived CTAs instead of one
     // persistent wave. Measured on the 36-block Q4_K sweep (1.73 M chunks): one persistent wave 6.50 ms, ~27 chunks
-    // per CTA 5.55 ms, ~6 per CTA 5.44 ms, one per CTA 5.88 ms -- the HBM sustains more of this write-heavy mix when
-    // the CTAs in flight start and finish at different times than when one wave walks the tensor in step.
+    // per CTA 5.55 ms, ~6 per CTA 5.44 ms, one per CTA 5.88 ms; targets of 4 / 8 / 16 chunks 5.53 / 5.49 / 5.53 ms
+    // (three runs each) -- the HBM sustains more of this write-heavy mix when the CTAs in flight start and finish at
+    // different times than when one wave walks the tensor in step.
     const int64_t resident = static_cast<int64_t>(occ[dev]) * device_sm_count();
     const int64_t grid =
         std::min<int64_t>(n_chunks, std::max<int64_t>(resident, (n_chunks + kChunksPerCta - 1) / kChunksPerCta));
