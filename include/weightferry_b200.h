@@ -39,10 +39,11 @@ enum {
 
 enum { WF_F16 = 0, WF_BF16 = 1, WF_F32 = 2 };
 
-/* Library version (major * 10000 + minor * 100 + patch). */
+/* Library version (major * 10000 + minor * 100 + patch). No reference counterpart (a library utility). */
 WF_API int wf_version(void);
 
-/* A static, human-readable string for a status returned by any entry point. */
+/* A static, human-readable string for a status returned by any entry point. No reference counterpart: the reference's
+ * Python entry points raise exceptions (or answer None), which the Python layer over this library reproduces. */
 WF_API const char *wf_status_string(int status);
 
 /* Block geometry of a GGML quantisation type: values per block (32 or 256) and bytes per block.
