@@ -1,10 +1,12 @@
 """bench.py's host-side pieces without a GPU: its command line accepts every workload, its GGML geometry table agrees
-with the library's own table and the oracle's, its synthetic GGUF blocks carry finite float16 scales, and the SSD
-workload can name the filesystem it measures."""
+with the library's own table and the oracle's, its synthetic GGUF blocks carry finite float16 scales, the SSD
+workload can name the filesystem it measures, and the reference arm keeps the launch contract under torchrun."""
 
 import ctypes
 import importlib
+import json
 import os
+import socket
 import subprocess
 import sys
 
@@ -59,3 +61,24 @@ def test_mount_of_names_a_filesystem():
     m = bench.mount_of(REPO)
     assert set(m) == {"mount", "type", "device"}
     assert REPO.startswith(m["mount"].rstrip("/") or "/")
+
+
+def _free_port():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+def test_reference_arm_prints_one_line_from_rank_0_under_torchrun():
+    """`bench.py --impl reference` launched as the driver launches it for N > 1 (torchrun, one process per rank): rank
+    0 alone times the reference's algorithm on the host and prints one JSON line; every rank exits 0."""
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr",
+           "127.0.0.1", "--master-port", str(_free_port()), os.path.join(REPO, "bench.py"), "--impl", "reference",
+           "--gpus", "2", "--steps", "1", "--warmup", "3"]
+    out = subprocess.run(cmd, capture_output=True, text=True, timeout=600, cwd=REPO)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1, out.stdout
+    rec = json.loads(lines[0])
+    assert rec["impl"] == "reference" and rec["n_gpus"] == 2 and rec["value"] > 0
+    assert rec["e2e"]["h2d_bytes_per_step"] == 0 and rec["cpu_baseline"]["kind"] in ("port", "reference")
