@@ -59,7 +59,7 @@ extern "C" WF_API int wf_w8a8_linear_noalloc(const void *x, const int8_t *wq, co
                                             int64_t n, int64_t k, wf_stream_t stream) {
     if (m < 0 || n < 0 || k <= 0) return WF_ERR_ARG;
     if (m == 0 || n == 0) return WF_OK;
-    if (m > kScratchRows || m * k > kScratchActs) return WF_ERR_TOO_LARGE;
+    if (m > kScratchRows || k > kScratchActs / m) return WF_ERR_TOO_LARGE;  // m * k <= kScratchActs, no overflow
     if (k % 16 != 0 || n % 8 != 0) return WF_ERR_ARG;  // the GEMM's operand rules, checked before any launch
     int rc = wf::check_device();
     if (rc != WF_OK) return rc;
