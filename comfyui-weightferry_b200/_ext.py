@@ -62,6 +62,7 @@ SIGNATURES = {
     "wf_w8a8_gemm_residual": (ctypes.c_int, [ctypes.c_void_p] * 6 + [ctypes.c_int64, ctypes.c_void_p]
                               + [ctypes.c_int64] * 3 + [ctypes.c_void_p]),
     "wf_w8a8_gemm_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "wf_w8a8_gemm_set_wait_limit": (ctypes.c_int, [ctypes.c_uint64]),
     "wf_gated_residual": (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]),
     "wf_hbm_probe": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
     "wf_w8a8_linear_noalloc": (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]),

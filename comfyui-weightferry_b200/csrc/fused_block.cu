@@ -13,6 +13,8 @@
 
 #include "wf_common.cuh"
 
+#include <atomic>
+
 #include <algorithm>
 
 namespace wf {
@@ -339,13 +341,13 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
 template <auto KERN>
 int persistent_grid(int threads, size_t smem, int64_t items) {
     auto kern = KERN;
-    static int occ[64] = {0};  // one cache per kernel: KERN is a template parameter
+    static std::atomic<int> occ[64];  // one cache per kernel (KERN is a template parameter); any host thread
     int dev = 0;
     cudaGetDevice(&dev);
-    int o = (dev >= 0 && dev < 64) ? occ[dev] : 0;
+    int o = (dev >= 0 && dev < 64) ? occ[dev].load(std::memory_order_relaxed) : 0;
     if (o == 0) {
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, threads, smem) != cudaSuccess || o < 1) o = 1;
-        if (dev >= 0 && dev < 64) occ[dev] = o;
+        if (dev >= 0 && dev < 64) occ[dev].store(o, std::memory_order_relaxed);
     }
     const int64_t g = std::min<int64_t>(items, static_cast<int64_t>(o) * device_sm_count());
     return static_cast<int>(std::max<int64_t>(g, 1));

@@ -17,6 +17,8 @@
 
 #include "wf_common.cuh"
 
+#include <atomic>
+
 #include <algorithm>
 
 namespace wf {
@@ -596,11 +598,12 @@ int launch(const P &p, int64_t n_chunks, cudaStream_t stream) {
     constexpr int smem = 2 * buf_stride<QT>() + (LORA && ALIGNED ? 2 * kChunkValues * 4 : 0);
     auto kern = dequant_kernel<QT, MID, OUT, ALIGNED, LORA, P>;
     // per instantiation and device: resident CTAs per SM
-    static int occ[64] = {0};
+    // written by whichever host thread launches first (the compute thread and the SSD uploader's both do): atomic
+    static std::atomic<int> occ[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return WF_ERR_DEVICE;
-    if (occ[dev] == 0) {
+    if (occ[dev].load(std::memory_order_acquire) == 0) {
         int o = 0;
         cudaError_t e = cudaSuccess;
         if constexpr (smem > 48 * 1024) {
@@ -609,14 +612,14 @@ int launch(const P &p, int64_t n_chunks, cudaStream_t stream) {
         }
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, kThreads, smem);
         if (e != cudaSuccess) return static_cast<int>(e);
-        occ[dev] = std::max(o, 1);
+        occ[dev].store(std::max(o, 1), std::memory_order_release);
     }
     // about kChunksPerCta chunks per CTA, never fewer CTAs than fit at once: many short-lived CTAs instead of one
     // persistent wave. Measured on the 36-block Q4_K sweep (1.73 M chunks): one persistent wave 6.50 ms, ~27 chunks
     // per CTA 5.55 ms, ~6 per CTA 5.44 ms, one per CTA 5.88 ms; targets of 4 / 8 / 16 chunks 5.53 / 5.49 / 5.53 ms
     // (three runs each) -- the HBM sustains more of this write-heavy mix when the CTAs in flight start and finish at
     // different times than when one wave walks the tensor in step.
-    const int64_t resident = static_cast<int64_t>(occ[dev]) * device_sm_count();
+    const int64_t resident = static_cast<int64_t>(occ[dev].load(std::memory_order_acquire)) * device_sm_count();
     const int64_t grid =
         std::min<int64_t>(n_chunks, std::max<int64_t>(resident, (n_chunks + kChunksPerCta - 1) / kChunksPerCta));
     kern<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);

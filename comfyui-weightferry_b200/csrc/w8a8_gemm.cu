@@ -29,6 +29,7 @@
 
 #include <cuda.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 #include <utility>
@@ -52,6 +53,10 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) | ((BM >> 4) << 24);
 
 __device__ int g_gemm_status;  // 0 ok; 1 producer wait expired; 2 MMA wait expired; 3 epilogue wait expired
+// limit of the pipeline waits (the producer's, the MMA issuer's and the epilogue's); a test shortens it so that a wait
+// runs out and the abort path is exercised (wf_w8a8_gemm_set_wait_limit). The drain waits of the abort path keep
+// kWaitLimitNs.
+__device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -69,6 +74,11 @@ __device__ __forceinline__ void mbar_init(uint32_t a, uint32_t count) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void mbar_complete_tx(uint32_t a, uint32_t bytes) {  // bytes that will never arrive
+    asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
+}
+// bounded wait (kWaitLimitNs) for the phase of the given parity, for the drains of the abort path
+__device__ __forceinline__ void mbar_drain_wait(uint32_t a, uint32_t parity);
 __device__ __forceinline__ void mbar_arrive(uint32_t a) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
 }
@@ -87,7 +97,13 @@ __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for the phase of the given parity, at most kWaitLimitNs; gives up early when another role aborted.
+__device__ __forceinline__ void mbar_drain_wait(uint32_t a, uint32_t parity) {
+    const uint64_t t0 = global_ns();
+    while (!mbar_try(a, parity) && global_ns() - t0 < kWaitLimitNs) {
+    }
+}
+
+// Wait for the phase of the given parity, at most g_wait_limit_ns; gives up early when another role aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile int *abort_flag, int code) {
     if (mbar_try(a, parity)) return true;
     const uint64_t t0 = global_ns();
@@ -96,7 +112,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile 
         for (int i = 0; i < 32; ++i)
             if (mbar_try(a, parity)) return true;
         if (*abort_flag) return false;
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > g_wait_limit_ns) {
             *abort_flag = 1;
             atomicCAS(&g_gemm_status, 0, code);
             return false;
@@ -553,6 +569,7 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
     // bars: full[0..5] (used in the even CTA), empty[0..5], tmem_full[0..1], tmem_empty[0..1] (even CTA), drain
     __shared__ uint32_t s_tmem_base;
     __shared__ int s_abort;
+    __shared__ int s_issued[2];  // stage loads issued by this CTA's producer; [1] in the even CTA: the odd CTA's
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S2), tfull0 = smem_u32(bars + 2 * S2),
                    tempty0 = smem_u32(bars + 2 * S2 + 2), drain = smem_u32(bars + 2 * S2 + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -566,6 +583,7 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
 
     if (threadIdx.x == 0) {
         s_abort = 0;
+        s_issued[0] = s_issued[1] = 0;
         for (int s = 0; s < S2; ++s) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, 1);
@@ -597,6 +615,7 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_b)) : "memory");
             int stage = 0;
             uint32_t phase = 0;
+            int issued = 0;
             bool ok = true;
             for (int tile = cluster_id; tile < n_tiles && ok; tile += n_clusters) {
                 const int m0 = (tile % tiles_m) * 256 + static_cast<int>(rank) * 128;
@@ -608,13 +627,17 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
                     const uint32_t a_dst = smem_u32(ring + stage * STAGE2);
                     tma_load_2d_pair(a_dst, &tma_a, kb * BK, m0, leader_full);
                     tma_load_2d_pair(a_dst + A2_STAGE, &tma_b, kb * BK, n0, leader_full);
+                    ++issued;
                     if (++stage == S2) { stage = 0; phase ^= 1u; }
                 }
             }
-            if (!ok) {  // let issued copies land before this CTA can leave
-                const uint64_t t0 = global_ns();
-                while (global_ns() - t0 < 200000ull) {
-                }
+            // the count goes to the even CTA, whose full barriers count both CTAs' bytes: it drains after the pair
+            // has stopped (below)
+            if (rank == 0) {
+                s_issued[0] = issued;
+            } else {
+                const uint32_t dst = map_to_rank(smem_u32(&s_issued[1]), 0);
+                asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(dst), "r"(issued) : "memory");
             }
         }
     } else if (warp == 9) {
@@ -682,7 +705,27 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
     }
     fence_before();
     __syncthreads();
-    cluster_sync();  // no CTA leaves (or frees tensor memory) while the pair's MMAs may still use it
+    cluster_sync();  // both CTAs stopped issuing; the odd CTA's load count is in the even CTA's s_issued[1]
+    if (rank == 0 && warp == 8 && lane == 0) {
+        // Drain: every stage load either CTA issued lands before either CTA leaves. Stage s's full barrier counts
+        // both CTAs' bytes of a use; only its last issued use can be outstanding (a producer reuses a stage only
+        // after the MMA consumed the previous use, which needed that use complete). A use that one CTA issued and
+        // the other did not (it stopped first) gets the missing half: the arrive with the odd CTA's bytes expected,
+        // or the even CTA's expectation of the odd CTA's bytes cancelled. Without an abort every use was consumed and
+        // each wait returns at once.
+        const int n_even = s_issued[0], n_odd = s_issued[1];
+        const int last = max(n_even, n_odd);
+        for (int s = 0; s < S2 && s < last; ++s) {
+            const int u = s + ((last - 1 - s) / S2) * S2;
+            const uint32_t bar = full0 + 8 * s;
+            if (u >= n_even)
+                mbar_expect_tx(bar, STAGE2);
+            else if (u >= n_odd)
+                mbar_complete_tx(bar, STAGE2);
+            mbar_drain_wait(bar, static_cast<uint32_t>(u / S2) & 1u);
+        }
+    }
+    cluster_sync();  // no CTA leaves (or frees tensor memory) while loads into it or the pair's MMAs may still run
     fence_after();
     if (warp == 9) {
         asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
@@ -779,8 +822,8 @@ int launch(const CUtensorMap &ma, const void *wq, const CUtensorMap &my, const f
         // pairs of CTAs, 256 x 256 tiles: each CTA loads 128 rows of xq and 128 rows of wq per stage
         CUtensorMap mb2;
         if ((rc = make_map(&mb2, wq, static_cast<int>(N), static_cast<int>(K), 128)) != WF_OK) return rc;
-        static int clusters[64] = {0};
-        if (clusters[dev] == 0) {
+        static std::atomic<int> clusters[64];  // any host thread may launch first
+        if (clusters[dev].load(std::memory_order_acquire) == 0) {
             cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_2sm_kernel<RES>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
             if (e != cudaSuccess) return static_cast<int>(e);
@@ -798,10 +841,11 @@ int launch(const CUtensorMap &ma, const void *wq, const CUtensorMap &my, const f
             int n = 0;
             e = cudaOccupancyMaxActiveClusters(&n, w8a8_gemm_2sm_kernel<RES>, &cfg);
             if (e != cudaSuccess) return static_cast<int>(e);
-            clusters[dev] = std::max(n, 1);
+            clusters[dev].store(std::max(n, 1), std::memory_order_release);
         }
         const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
-        const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, clusters[dev]));
+        const int grid =
+            2 * static_cast<int>(std::min<int64_t>(tiles, clusters[dev].load(std::memory_order_acquire)));
         const cudaError_t e = launch_dependent(w8a8_gemm_2sm_kernel<RES>, grid, THREADS, SMEM2_BYTES, stream, ma, mb2,
                                                my, xs, ws, acc_out, res, static_cast<int>(M), static_cast<int>(N),
                                                static_cast<int>(K));
@@ -809,12 +853,12 @@ int launch(const CUtensorMap &ma, const void *wq, const CUtensorMap &my, const f
     }
     CUtensorMap mb;
     if ((rc = make_map(&mb, wq, static_cast<int>(N), static_cast<int>(K), BN)) != WF_OK) return rc;
-    static bool attr_set[64] = {false};
-    if (!attr_set[dev]) {
+    static std::atomic<bool> attr_set[64];
+    if (!attr_set[dev].load(std::memory_order_acquire)) {
         cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel<RES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              SMEM_BYTES);
         if (e != cudaSuccess) return static_cast<int>(e);
-        attr_set[dev] = true;
+        attr_set[dev].store(true, std::memory_order_release);
     }
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, device_sm_count()));
@@ -878,6 +922,12 @@ extern "C" WF_API int wf_w8a8_gemm_residual(const int8_t *xq, const int8_t *wq, 
     return wf::w8a8_gemm_launch(xq, wq, xs, ws, static_cast<__nv_bfloat16 *>(out), nullptr,
                                 static_cast<const __nv_bfloat16 *>(resid), static_cast<const __nv_bfloat16 *>(gate),
                                 rows_per_group, m, n, k, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" WF_API int wf_w8a8_gemm_set_wait_limit(uint64_t limit_ns) {
+    if (limit_ns == 0 || limit_ns > wf::kWaitLimitNs) limit_ns = wf::kWaitLimitNs;
+    const unsigned long long v = limit_ns;
+    return static_cast<int>(cudaMemcpyToSymbol(wf::g_wait_limit_ns, &v, sizeof(v)));
 }
 
 extern "C" WF_API int wf_w8a8_gemm_status(int *status) {

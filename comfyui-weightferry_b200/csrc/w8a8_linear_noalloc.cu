@@ -12,6 +12,8 @@
 // first call before any stream capture). All calls share the one buffer and it keeps the last call's contents;
 // nothing in it has to start at zero, because the quantiser writes every byte the GEMM then reads. Calls whose
 // work overlaps on the GPU (different streams, or different host threads without ordering) race on the buffer.
+// The address is kept per device index for the life of the process, so a device reset (cudaDeviceReset) while the
+// library is loaded is not supported.
 
 #include "wf_common.cuh"
 
@@ -22,6 +24,7 @@ namespace {
 
 constexpr int64_t kScratchActs = int64_t(1) << 24;  // int8 activations: m * k <= 16,777,216 (8192 x 2048 fits)
 constexpr int64_t kScratchRows = int64_t(1) << 16;  // float32 scales: m <= 65,536 tokens
+constexpr int64_t kMaxRowWidth = 51200;             // the quantiser's widest row (k), as wf_quant_rows checks
 
 // [0, kScratchActs): x_q; [kScratchActs, + 4 * kScratchRows): x_s. 256-byte aligned (TMA needs 16).
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kScratchActs + 4 * kScratchRows];
@@ -60,6 +63,7 @@ extern "C" WF_API int wf_w8a8_linear_noalloc(const void *x, const int8_t *wq, co
     if (m < 0 || n < 0 || k <= 0) return WF_ERR_ARG;
     if (m == 0 || n == 0) return WF_OK;
     if (m > kScratchRows || k > kScratchActs / m) return WF_ERR_TOO_LARGE;  // m * k <= kScratchActs, no overflow
+    if (k > kMaxRowWidth) return WF_ERR_UNSUPPORTED;  // refused before any launch, as the quantiser would
     if (k % 16 != 0 || n % 8 != 0) return WF_ERR_ARG;  // the GEMM's operand rules, checked before any launch
     int rc = wf::check_device();
     if (rc != WF_OK) return rc;

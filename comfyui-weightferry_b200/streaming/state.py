@@ -258,7 +258,9 @@ class _StreamState:
             self.profiler.add_cpu(time.perf_counter() - t0)
 
     def close(self):
-        """Stop the SSD tier's threads (uploader, ring readers) and release its buffers."""
+        """Stop the SSD tier's threads (uploader, ring readers), release its buffers, and wait for the transfer and
+        dequant streams: their H2D copies read the pinned host flats, which the owner unregisters right after close
+        (a copy still running from unregistered memory would read freed pages)."""
         if self.uploader is not None:
             self.uploader.drain()
             self.uploader.close()
@@ -266,6 +268,8 @@ class _StreamState:
         if self.ring is not None:
             self.ring.close()
             self.ring = None
+        self.copy_stream.synchronize()
+        self.dequant_stream.synchronize()
 
     def profile_summary(self):
         return None if self.profiler is None else self.profiler.summary()

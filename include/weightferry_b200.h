@@ -170,15 +170,22 @@ WF_API int wf_w8a8_gemm_residual(const int8_t *xq, const int8_t *wq, const float
  * (the reference's GEMM is a closed library call); it is this library's failure report. */
 WF_API int wf_w8a8_gemm_status(int *status);
 
+/* Test hook: the time limit, in nanoseconds, of the GEMM kernels' pipeline waits (default and maximum 2 s; 0 restores
+ * the default). A short limit makes a wait run out on purpose, so that a test can check the abort path -- the status
+ * code above, the kernel's bounded drain of its own copies and MMAs, and a correct GEMM afterwards -- without any
+ * fault or hang. The drain waits themselves keep the 2 s limit. No reference counterpart. */
+WF_API int wf_w8a8_gemm_set_wait_limit(uint64_t limit_ns);
+
 /* W8A8 linear that allocates nothing: y = bf16((float(xq @ wq^T) * xs) * ws) where xq / xs are the per-token absmax
  * int8 quantisation of the bf16 activations x [m, k] (what wf_quant_rows with pre 0, rotate 0 produces), kept in a
  * fixed buffer inside the library instead of caller memory. For callers that cannot allocate device memory when
  * they run (an application whose allocator owns the GPU's memory, or a path where a cudaMalloc and its possible
  * device synchronisation are not allowed). Limits: m * k <= 16,777,216 and m <= 65,536, else WF_ERR_TOO_LARGE;
- * the operand rules of wf_quant_rows and wf_w8a8_gemm apply. The buffer (about 16.3 MB per GPU that loads the
- * library) is shared by every call: calls that overlap on the GPU race. The first call on a device looks the
- * buffer up for that device; make it before any stream capture. This entry point has no counterpart in the
- * reference. */
+ * k <= 51,200 (the quantiser's row width), else WF_ERR_UNSUPPORTED; the operand rules of wf_quant_rows and
+ * wf_w8a8_gemm apply. The buffer (about 16.3 MB per GPU that loads the library) is shared by every call: calls that
+ * overlap on the GPU race. The first call on a device looks the buffer up for that device and keeps its address;
+ * make it before any stream capture. A device reset (cudaDeviceReset) while the library is loaded is not supported:
+ * the kept address would be stale. This entry point has no counterpart in the reference. */
 WF_API int wf_w8a8_linear_noalloc(const void *x, const int8_t *wq, const float *ws, void *y, int64_t m, int64_t n,
                                   int64_t k, wf_stream_t stream);
 

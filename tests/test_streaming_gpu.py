@@ -117,3 +117,27 @@ def test_block_hooks_bind_slot_weights(cuda):
     for h in handles:
         h.remove()
     ph.release_all(holders)
+
+
+def test_close_right_after_forward_waits_for_transfers(cuda):
+    """close() straight after a forward with no synchronisation: the transfer and dequant streams are idle when it
+    returns (their copies read pinned host buffers that are unregistered next), and a new stack built on the freed
+    memory gives the same bits."""
+    import torch
+    cb = wf("streaming.cosmos_block")
+    stk = wf("streaming.stack")
+    cfg = cb.CosmosConfig(**SMALL)
+    batch, T, H, W = 2, 1, 8, 8
+    tokens = T * H * W
+    rope = cb.rope3d_table(T, H, W, device="cuda")
+    x, emb, lora, ctx = _inputs(torch, cfg, batch, tokens, 16, 9)
+    outs = []
+    for _ in range(2):
+        s = stk.StreamedStack(cfg, 6, "cuda", num_slots=2)
+        y = s.forward(x, emb, ctx, rope, batch, tokens, lora)
+        st = s.state
+        s.close()
+        assert st.copy_stream.query() and st.dequant_stream.query()
+        outs.append(y)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])

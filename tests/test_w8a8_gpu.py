@@ -233,3 +233,29 @@ def test_int8_linear_residual_entry_point(cuda, five_d):
     want = torch.addcmul(xr, gate, plain.view(xr.shape))
     torch.cuda.synchronize()
     assert torch.equal(out, want)
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 512, 4096), (512, 512, 4096)])  # the one-CTA kernel, the CTA-pair kernel
+def test_gemm_wait_expiry_reports_and_recovers(cuda, m, n, k):
+    """A pipeline wait made to run out on purpose: with the wait limit shortened to 1 ns (the library's test hook), the
+    kernel stops issuing, drains the copies and MMAs it started, frees its tensor memory and reports the wait's code
+    (1 producer, 2 MMA issuer, 3 epilogue); a GEMM launched after it with the normal limit is exact again."""
+    import ctypes
+    import torch
+    ext = wf("_ext")
+    lib = ext.lib()
+    xq, wq, xs, ws = _operands(m, n, k, seed=11 + m)
+    y = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    st = ctypes.c_int(-1)
+    ext.check(lib.wf_w8a8_gemm_status(ctypes.byref(st)), "status")  # reading clears it
+    ext.check(lib.wf_w8a8_gemm_set_wait_limit(1), "wf_w8a8_gemm_set_wait_limit")
+    try:
+        ext.check(lib.wf_w8a8_gemm(xq.data_ptr(), wq.data_ptr(), xs.data_ptr(), ws.data_ptr(), y.data_ptr(), None,
+                                   m, n, k, ext.stream_of(xq.device)), "wf_w8a8_gemm")
+        torch.cuda.synchronize()
+    finally:
+        ext.check(lib.wf_w8a8_gemm_set_wait_limit(0), "wf_w8a8_gemm_set_wait_limit")
+    ext.check(lib.wf_w8a8_gemm_status(ctypes.byref(st)), "status")
+    assert st.value in (1, 2, 3), f"no wait ran out (status {st.value})"
+    y2, acc = _gemm(xq, wq, xs, ws)  # asserts the status reads 0 again
+    _check(xq, wq, xs, ws, y2, acc)

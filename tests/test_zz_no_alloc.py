@@ -65,4 +65,5 @@ def test_noalloc_linear_refuses_beyond_its_buffer(cuda):
     assert ext.lib().wf_w8a8_linear_noalloc(p, p, p, p, 8193, 16, 2048, st) == -5   # m * k > 16,777,216
     assert ext.lib().wf_w8a8_linear_noalloc(p, p, p, p, 65537, 16, 16, st) == -5    # m > 65,536
     assert ext.lib().wf_w8a8_linear_noalloc(p, p, p, p, 2, 16, 1 << 62, st) == -5   # m * k would overflow int64
+    assert ext.lib().wf_w8a8_linear_noalloc(p, p, p, p, 2, 16, 51216, st) == -2     # k beyond the quantiser's row
     assert "fixed buffer" in ext.status_string(-5)
