@@ -29,12 +29,12 @@ import numpy as np
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from the ncu captures summarised in
-# profiles/ (None until captured). Keyed by workload; scaled to the bench's launch as described in the profile.
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from one ncu capture of the same
+# kernel (None until captured). Keyed by workload, scaled to the bench's launch.
 NCU_TRAFFIC = {
-    # profiles/dequant_q4k_sweep.md: one-block capture (221.20 MB read + 729.71 MB written) x 36 blocks
+    # one-block capture of the batched Q4_K dequantisation (221.20 MB read + 729.71 MB written) x 36 blocks
     "sweep": 34_232_680_000,
-    # profiles/w8a8_gemm.md: one configs[2] launch, 34.17 MB read + 87.15 MB written (the rest of Y still in L2)
+    # one configs[2] GEMM launch: 34.17 MB read + 87.15 MB written (the rest of Y still in L2 when the kernel ends)
     "w8a8": 121_317_632,
     "q8": None, "q4k": None, "prologue": None,
 }
