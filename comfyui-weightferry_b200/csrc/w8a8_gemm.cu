@@ -106,13 +106,17 @@ __device__ __forceinline__ void mbar_drain_wait(uint32_t a, uint32_t parity) {
 // Wait for the phase of the given parity, at most g_wait_limit_ns; gives up early when another role aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile int *abort_flag, int code) {
     if (mbar_try(a, parity)) return true;
+    const uint64_t limit = g_wait_limit_ns;
+    // try_wait suspends for a while inside each try, so 32 tries can outlast a short wait: a shortened limit (the
+    // test hook) is checked after every try
+    const int spins = limit < 1000000ull ? 1 : 32;
     const uint64_t t0 = global_ns();
     while (true) {
 #pragma unroll 1
-        for (int i = 0; i < 32; ++i)
+        for (int i = 0; i < spins; ++i)
             if (mbar_try(a, parity)) return true;
         if (*abort_flag) return false;
-        if (global_ns() - t0 > g_wait_limit_ns) {
+        if (global_ns() - t0 > limit) {
             *abort_flag = 1;
             atomicCAS(&g_gemm_status, 0, code);
             return false;

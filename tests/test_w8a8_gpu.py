@@ -141,7 +141,7 @@ def test_int8_linear_entry_points(cuda):
     xq, xs = fk.quantize_rows(x.reshape(-1, 1024), rotate=False)
     y2 = fi.gemm(xq, wq, xs, ws)
     assert torch.equal(y.reshape(-1, 768), y2)
-    fs._tls.qkv = {}
+    fs._tls.qkv = fi._QuantScope()
     try:
         a = fi._int8_linear_shared(x, (wq, ws), None)
         b = fi._int8_linear_shared(x, (wq, ws), None)
@@ -223,7 +223,7 @@ def test_int8_linear_residual_entry_point(cuda, five_d):
     xr = torch.randn((*x.shape[:-1], D), device="cuda", generator=g).to(torch.bfloat16)
     gshape = (B, T, 1, 1, D) if five_d else (B, 1, D)
     gate = (torch.randn(gshape, device="cuda", generator=g) * 0.3).to(torch.bfloat16)
-    fs._tls.qkv = {}
+    fs._tls.qkv = fi._QuantScope()
     try:
         out = fi._int8_linear_residual(x, (wq, ws), None, {"x": xr, "gate": gate})
         plain = fi._int8_linear_shared(x, (wq, ws), None)
@@ -235,7 +235,7 @@ def test_int8_linear_residual_entry_point(cuda, five_d):
     assert torch.equal(out, want)
 
 
-@pytest.mark.parametrize("m,n,k", [(128, 512, 4096), (512, 512, 4096)])  # the one-CTA kernel, the CTA-pair kernel
+@pytest.mark.parametrize("m,n,k", [(128, 512, 8192), (512, 512, 8192)])  # the one-CTA kernel, the CTA-pair kernel
 def test_gemm_wait_expiry_reports_and_recovers(cuda, m, n, k):
     """A pipeline wait made to run out on purpose: with the wait limit shortened to 1 ns (the library's test hook), the
     kernel stops issuing, drains the copies and MMAs it started, frees its tensor memory and reports the wait's code
