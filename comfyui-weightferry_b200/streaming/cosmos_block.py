@@ -366,24 +366,6 @@ def block_forward(x_rows, emb, ctx, rope, W, cfg, tp, batch, tokens, lora_term=N
     return _residual(x_rows, gate, o, row0, tokens)
 
 
-def block_forward_fused(self, x_B_T_H_W_D, emb_B_T_D, crossattn_emb, rope_emb_L_1_1_D=None, adaln_lora_B_T_3D=None,
-                        extra_per_block_pos_emb=None, transformer_options={}):
-    """ComfyUI Block.forward semantics on a block module with ComfyUI's attribute names (single GPU): the fused
-    parts' body used by fused_block._block_forward."""
-    if extra_per_block_pos_emb is not None:
-        x_B_T_H_W_D = x_B_T_H_W_D + extra_per_block_pos_emb
-    B, T, H, Wd, D = x_B_T_H_W_D.shape
-    W = {k: v.data for k, v in self.named_parameters()}
-    lora = None if adaln_lora_B_T_3D is None else adaln_lora_B_T_3D.reshape(B, -1)
-    cfg = getattr(self, "_wf_cfg", None) or CosmosConfig(hidden=D, heads=D // 128)
-    rope = rope_emb_L_1_1_D
-    if rope is not None and rope.dim() != 6:
-        rope = rope.reshape(1, T * H * Wd, 1, 64, 2, 2).float()
-    out = block_forward(x_B_T_H_W_D.reshape(B * T * H * Wd, D), emb_B_T_D.reshape(B, D), crossattn_emb, rope, W, cfg,
-                        TP(), B, T * H * Wd, lora_term=lora)
-    return out.view(B, T, H, Wd, D)
-
-
 def flops_per_block(cfg, batch, tokens, ctx_tokens):
     """Dense GEMM + attention FLOPs of one block (all ranks together)."""
     M, D, Mh = batch * tokens, cfg.hidden, cfg.mlp
