@@ -8,8 +8,8 @@ file system that refuses ``O_DIRECT`` (tmpfs, some network mounts) falls back to
 ``os.pwritev`` release the GIL for the system call, so several reader threads overlap their reads."""
 
 import json
+from concurrent.futures import ThreadPoolExecutor
 import os
-import threading
 import time
 import weakref
 
@@ -114,76 +114,76 @@ _PROBE_VERSION = 1
 
 
 def _timed_parallel_read(path, nbytes, chunk_bytes, threads):
-    """GB/s of reading ``nbytes`` of ``path`` in ``chunk_bytes`` pieces with ``threads`` readers (chunk i -> thread
-    i % threads)."""
-    errors = []
+    """GB/s of an unbuffered read of the first ``nbytes`` of ``path`` by ``threads`` readers at once, each reading
+    its own contiguous share in ``chunk_bytes`` pieces into its own aligned buffer."""
+    pieces = list(range(0, nbytes, chunk_bytes))
+    shares = [pieces[len(pieces) * t // threads:len(pieces) * (t + 1) // threads] for t in range(threads)]
 
-    def work(t):
-        reader = None
+    def read_share(offsets):
+        buf, _holder = aligned_host(chunk_bytes, pin=False)
+        reader = _UnbufferedReader(path)
         try:
-            buf, _ = aligned_host(chunk_bytes, pin=False)
-            reader = _UnbufferedReader(path)
-            for i, off in enumerate(range(0, nbytes, chunk_bytes)):
-                if i % threads == t:
-                    reader.read_into(off, chunk_bytes, buf.data_ptr())
-        except Exception as exc:  # noqa: BLE001 -- re-raised below once every thread ended
-            errors.append(exc)
+            for off in offsets:
+                reader.read_into(off, min(chunk_bytes, nbytes - off), buf.data_ptr())
         finally:
-            if reader is not None:
-                reader.close()
+            reader.close()
 
-    workers = [threading.Thread(target=work, args=(t,), daemon=True) for t in range(threads)]
-    t0 = time.perf_counter()
-    for w in workers:
-        w.start()
-    for w in workers:
-        w.join()
-    dt = time.perf_counter() - t0
-    if errors:
-        raise errors[0]
-    return nbytes / dt / 1e9
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        start = time.perf_counter()
+        for fut in [pool.submit(read_share, share) for share in shares]:
+            fut.result()  # re-raises a reader's error
+        elapsed = time.perf_counter() - start
+    return nbytes / elapsed / 1e9
+
+
+def _cached_probe(cache_path, size_mb, chunk_mb, thread_counts, max_age_s):
+    """{threads: GB/s} from an earlier probe of the same sizes younger than max_age_s, or None."""
+    try:
+        with open(cache_path, encoding="utf-8") as f:
+            rec = json.load(f)
+        fresh = time.time() - float(rec["time"]) < max_age_s
+        same = (rec["version"], rec["size_mb"], rec["chunk_mb"]) == (_PROBE_VERSION, size_mb, chunk_mb)
+        by = {int(k): float(v) for k, v in rec["by_threads"].items()}
+        if fresh and same and sorted(by) == sorted(thread_counts):
+            return by, rec.get("direct")
+    except (OSError, ValueError, KeyError, TypeError):  # none, old or damaged: measure again
+        pass
+    return None
 
 
 def probe_disk(directory, size_mb=512, chunk_mb=32, thread_counts=(1, 2, 4), max_age_s=7 * 24 * 3600):
-    """Unbuffered read rate of the drive holding ``directory`` with 1 / 2 / 4 reader threads (the reference's
-    probe_disk), cached in the directory for a week: {"gbps": best GB/s, "threads": its thread count,
-    "by_threads": {threads: GB/s}, "direct": O_DIRECT used}."""
+    """Unbuffered read rate of the drive holding ``directory`` with 1 / 2 / 4 reader threads (the role of the
+    reference's probe_disk, core/tiers/disk_io.py:165-203), kept in the directory for a week: {"gbps": best GB/s,
+    "threads": its thread count, "by_threads": {threads: GB/s}, "direct": O_DIRECT used}."""
     os.makedirs(directory, exist_ok=True)
     cache_path = os.path.join(directory, _PROBE_FILE)
-    try:
-        with open(cache_path, encoding="utf-8") as f:
-            cached = json.load(f)
-        if (time.time() - cached.get("time", 0) < max_age_s and cached.get("version") == _PROBE_VERSION
-                and cached.get("size_mb") == size_mb and cached.get("chunk_mb") == chunk_mb
-                and sorted(int(k) for k in cached.get("by_threads", {})) == sorted(thread_counts)):
-            by = {int(k): v for k, v in cached["by_threads"].items()}
-            best = max(by, key=by.get)
-            return {"gbps": by[best], "threads": best, "by_threads": by, "direct": cached.get("direct")}
-    except (OSError, ValueError, KeyError, TypeError):  # no, old or damaged cache: measure again
-        pass
-    path = os.path.join(directory, f"weightferry_b200_disk_probe_{os.getpid()}.bin")
-    nbytes = size_mb * MB
-    block = os.urandom(MB)
-    with open(path, "wb") as f:
-        for _ in range(size_mb):
-            f.write(block)
-        f.flush()
-        os.fsync(f.fileno())
-    try:
-        probe_reader = _UnbufferedReader(path)
-        direct = probe_reader.direct
-        probe_reader.close()
-        by = {n: round(_timed_parallel_read(path, nbytes, chunk_mb * MB, n), 2) for n in thread_counts}
-    finally:
+    hit = _cached_probe(cache_path, size_mb, chunk_mb, thread_counts, max_age_s)
+    if hit is None:
+        path = os.path.join(directory, f"weightferry_b200_disk_probe_{os.getpid()}.bin")
+        nbytes = size_mb * MB
         try:
-            os.remove(path)
-        except OSError:
+            with open(path, "wb") as f:  # incompressible bytes, on the drive before the timed reads
+                pattern = os.urandom(MB)
+                for _ in range(size_mb):
+                    f.write(pattern)
+                f.flush()
+                os.fsync(f.fileno())
+            check = _UnbufferedReader(path)
+            direct = check.direct
+            check.close()
+            by = {n: round(_timed_parallel_read(path, nbytes, chunk_mb * MB, n), 2) for n in thread_counts}
+        finally:
+            try:
+                os.remove(path)
+            except OSError:
+                pass
+        try:
+            with open(cache_path, "w", encoding="utf-8") as f:
+                json.dump({"version": _PROBE_VERSION, "time": time.time(), "size_mb": size_mb, "chunk_mb": chunk_mb,
+                           "by_threads": by, "direct": direct}, f)
+        except OSError:  # kept only to skip the probe next time
             pass
+    else:
+        by, direct = hit
     best = max(by, key=by.get)
-    try:
-        with open(cache_path, "w", encoding="utf-8") as f:
-            json.dump({"version": _PROBE_VERSION, "by_threads": by, "size_mb": size_mb, "chunk_mb": chunk_mb,
-                       "time": time.time(), "direct": direct}, f)
-    except OSError:  # the result is cached only to skip the probe next time
-        pass
     return {"gbps": by[best], "threads": best, "by_threads": by, "direct": direct}

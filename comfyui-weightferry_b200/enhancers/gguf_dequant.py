@@ -35,11 +35,9 @@ _FORMATS = {2: ("Q4_0", 18, False, -1, 2, 8, False), 3: ("Q4_1", 20, True, -1, 4
 _KFORMATS = {10: ("Q2_K", 84), 11: ("Q3_K", 110), 12: ("Q4_K", 144), 13: ("Q5_K", 176), 14: ("Q6_K", 210)}
 _KQUANTS = None  # None = WEIGHTFERRY_GGUF_KQUANTS; True / False pin it (benchmarks, tests)
 _DT = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
-_state = {"orig": None, "ops": None, "orig_gw": None, "stats": {"used": 0, "fallback": 0}}
+_state = {"orig": None, "ops": None, "orig_gw": None}  # ComfyUI-GGUF's module and its replaced functions
 _LORA = True      # LoRA patches inside the dequantisation too (GGMLLayer.get_weight)
 _FACTORS = None   # "pin" / "0"; None = WEIGHTFERRY_GGUF_LORA_FACTORS
-_factors = {}     # pinned LoRA factors: id(factor) -> (weakref, key, pinned copy)
-_cache = {"pin_freed": False}
 
 
 def _env_get(name):
@@ -147,32 +145,48 @@ def dequantize_many(items, qtype, mid_dtype=None, out_dtype=None):
 
 
 # --------------------------------------------------------------------------------------------------------------- LoRA
+def _number(v):
+    return isinstance(v, (int, float)) and not isinstance(v, bool)
+
+
+def _plain_lora(patch, n_out, n_in):
+    """(up, down, scale) of one ComfyUI weight patch when it is a plain LoRA on a 2-D [n_out, n_in] weight, which
+    comfy.lora.calculate_weight applies as weight += (scale * (up @ down)).type(weight.dtype) with scale = strength *
+    alpha / rank (strength when alpha is None); None for anything else."""
+    if not (isinstance(patch, tuple) and len(patch) == 5):
+        return None
+    strength, adapter, strength_model, offset, function = patch
+    if type(adapter).__name__ != "LoRAAdapter" or strength_model != 1.0 or offset is not None or function is not None:
+        return None
+    if not _number(strength):
+        return None
+    parts = getattr(adapter, "weights", None)
+    if not isinstance(parts, (tuple, list)) or len(parts) < 6:
+        return None
+    up, down, alpha, mid, dora_scale, reshape = parts[:6]
+    if mid is not None or dora_scale is not None or reshape is not None:  # LoCon mid weight, DoRA, reshape
+        return None
+    if not (torch.is_tensor(up) and torch.is_tensor(down) and up.dim() == 2 and down.dim() == 2):
+        return None
+    rank = down.shape[0]
+    if tuple(up.shape) != (n_out, rank) or down.shape[1] != n_in:
+        return None
+    if alpha is None:
+        return up, down, strength
+    if not _number(alpha):
+        return None
+    return up, down, strength * (alpha / rank)
+
+
 def lora_factors(patch_list, n_out, n_in):
-    """[(up, down, strength * alpha)] when every patch is a plain LoRA that comfy.lora.calculate_weight applies as
-    weight += ((strength * alpha) * (up @ down)).type(weight.dtype) on a 2-D weight, else None (reference :329-355:
-    no DoRA, mid weight, reshape, offset, function or strength_model; alpha / rank when alpha is given)."""
+    """[(up, down, strength * alpha / rank)] when every patch is a plain LoRA of a 2-D weight (reference :329-355),
+    else None: one patch of another kind sends the whole weight to ComfyUI-GGUF's own code."""
     out = []
-    for p in patch_list:
-        if not isinstance(p, tuple) or len(p) != 5:
+    for patch in patch_list:
+        lora = _plain_lora(patch, n_out, n_in)
+        if lora is None:
             return None
-        strength, v, strength_model, offset, function = p
-        if strength_model != 1.0 or offset is not None or function is not None or type(v).__name__ != "LoRAAdapter":
-            return None
-        w = getattr(v, "weights", None)
-        if not isinstance(w, (tuple, list)) or len(w) < 6 or any(x is not None for x in w[3:6]):
-            return None
-        up, down, alpha_raw = w[0], w[1], w[2]
-        if (not torch.is_tensor(up) or not torch.is_tensor(down) or up.dim() != 2 or down.dim() != 2
-                or up.shape[0] != n_out or down.shape[1] != n_in or up.shape[1] != down.shape[0]
-                or not isinstance(strength, (int, float)) or isinstance(strength, bool)):
-            return None
-        if alpha_raw is None:
-            alpha = 1.0
-        elif isinstance(alpha_raw, (int, float)) and not isinstance(alpha_raw, bool):
-            alpha = alpha_raw / down.shape[0]
-        else:
-            return None
-        out.append((up, down, strength * alpha))
+        out.append(lora)
     return out
 
 
@@ -234,126 +248,188 @@ def _add_loras(raw, res, loras, qtype, mid):
 
 
 def _factor_mode():
+    """"pin": LoRA factors copied to the GPU from pinned host copies (WEIGHTFERRY_GGUF_LORA_FACTORS, default);
+    "0": straight from where they are, as comfy does -- also when ComfyUI runs with pinned memory disabled."""
     if _FACTORS is not None:
         return _FACTORS
-    mode = (_env_get("WEIGHTFERRY_GGUF_LORA_FACTORS") or "pin").strip().lower()
-    try:  # ComfyUI with pinned memory disabled: no pinned copies here either
-        import comfy.model_management as _mm
+    wanted = (_env_get("WEIGHTFERRY_GGUF_LORA_FACTORS") or "pin").strip().lower()
+    try:
+        import comfy.model_management as mm
         from comfy.cli_args import args
-        if getattr(_mm, "DISABLE_PINNED_MEMORY", False) or getattr(args, "disable_pinned_memory", False):
+        if getattr(args, "disable_pinned_memory", False) or getattr(mm, "DISABLE_PINNED_MEMORY", False):
             return "0"
     except Exception:  # noqa: BLE001 -- outside ComfyUI
         pass
-    return mode if mode == "pin" else "0"
+    return "pin" if wanted == "pin" else "0"
 
 
-def _version(t):
-    try:
-        return t._version
-    except RuntimeError:  # inference tensors keep no version counter
-        return None
+class _PinnedFactors:
+    """Pinned host copies of CPU LoRA factors, one per factor tensor while it lives and stays unchanged (same storage
+    and version). ComfyUI-GGUF keeps the patches on the host, and a copy from pageable memory waits for the GPU queue
+    to drain; from a pinned copy it does not. An entry goes away with its factor (a weak reference's callback)."""
+
+    def __init__(self):
+        self._by_id = {}
+        self.freed = False
+
+    @staticmethod
+    def _stamp(t, dev):
+        try:
+            version = t._version
+        except RuntimeError:  # inference tensors keep no version counter
+            version = None
+        return (t.data_ptr(), version, str(dev))
+
+    def pinned(self, t, dev):
+        stamp = self._stamp(t, dev)
+        entry = self._by_id.get(id(t))
+        if entry is not None and entry[0]() is t and entry[1] == stamp:
+            return entry[2]
+        copy = t.pin_memory()
+        key = id(t)
+        self._by_id[key] = (weakref.ref(t, lambda _ref, k=key: self._forget(k)), stamp, copy)
+        return copy
+
+    def _forget(self, key):
+        if self._by_id.pop(key, None) is not None:
+            self.freed = True
+
+    def __len__(self):
+        return len(self._by_id)
 
 
-def _pin_dropped(i):
-    if _factors.pop(i, None) is not None:
-        _cache["pin_freed"] = True
+_factors = _PinnedFactors()
 
 
 def _factor(t, dev, mode):
-    """t.to(dev, float32) as comfy casts a LoRA factor. mode "pin": a pinned copy made once per factor (kept while
-    the factor lives and its storage / version are unchanged) so the upload does not wait for the GPU queue to drain
-    (reference :426-446)."""
+    """t.to(dev, float32), the LoRA factor as comfy casts it; in mode "pin" through a kept pinned copy."""
     if mode == "0" or t.device.type != "cpu":
         return t.to(dev, torch.float32)
-    key = (t.data_ptr(), _version(t), str(dev))
-    hit = _factors.get(id(t))
-    if hit is not None and hit[0]() is t and hit[1] == key:
-        held = hit[2]
-    else:
-        held = t.pin_memory()
-        _factors[id(t)] = (weakref.ref(t, lambda _r, i=id(t): _pin_dropped(i)), key, held)
-    return held.to(dev, non_blocking=True).to(torch.float32)
+    return _factors.pinned(t, dev).to(dev, non_blocking=True).to(torch.float32)
 
 
 # ------------------------------------------------------------------------------------------------------------ install
+class _Tally:
+    """Calls of the patched entry points: ``used`` / ``fallback`` (dequantize_tensor), ``lora_used`` /
+    ``lora_fallback`` (get_weight with LoRA patches)."""
+
+    def __init__(self):
+        self.reset()
+
+    def reset(self):
+        self.counts = {"used": 0, "fallback": 0}
+
+    def add(self, key):
+        self.counts[key] = self.counts.get(key, 0) + 1
+
+
+_TALLY = _Tally()
+
+
+def _intermediate(dequant_dtype, dtype):
+    """ComfyUI-GGUF's precision of the dequantisation: the target dtype for "target", else dequant_dtype (None:
+    the default). Returns False when it is not a dtype this path takes."""
+    mid = dtype if dequant_dtype == "target" else dequant_dtype
+    return mid if mid is None or isinstance(mid, torch.dtype) else False
+
+
+def _logical_shape(tensor):
+    return tuple(getattr(tensor, "tensor_shape", tensor.shape))
+
+
+def _one_kernel(tensor, dtype, dequant_dtype):
+    """The dequantised weight of a GGUF tensor by one kernel, or None (the caller runs ComfyUI-GGUF's code)."""
+    qtype = getattr(tensor, "tensor_type", None)
+    if qtype is None or not isinstance(tensor, torch.Tensor) or not _supported(qtype):
+        return None
+    mid = _intermediate(dequant_dtype, dtype)
+    if mid is False:
+        return None
+    return dequantize(tensor.data, qtype, _logical_shape(tensor), mid, dtype)
+
+
+def _lora_weight(layer, tensor, dtype):
+    """A GGUF layer's weight with its LoRA patches by one kernel per LoRA, or None (ComfyUI-GGUF's code runs)."""
+    qtype = getattr(tensor, "tensor_type", None)
+    if (getattr(layer, "patch_dtype", None) is not None or qtype is None or not _supported(qtype)
+            or not isinstance(dtype, torch.dtype) or not getattr(tensor, "is_cuda", False)):
+        return None
+    mid = _intermediate(layer.dequant_dtype, dtype)
+    shape = _logical_shape(tensor)
+    if mid is False or len(shape) != 2:
+        return None
+    loras = lora_factors([p for group, _key in tensor.patches for p in group], *shape)
+    return dequantize_lora(tensor.data, qtype, shape, mid, dtype, loras) if loras else None
+
+
 def _patched(orig):
+    """ComfyUI-GGUF's ops.dequantize_tensor with the one-kernel dequantisation in front (reference :521-541)."""
     def dequantize_tensor(tensor, dtype=None, dequant_dtype=None):
-        qtype = getattr(tensor, "tensor_type", None)
-        if qtype is not None and _supported(qtype) and isinstance(tensor, torch.Tensor):
-            mid = dtype if dequant_dtype == "target" else dequant_dtype
-            if mid is None or isinstance(mid, torch.dtype):
-                oshape = getattr(tensor, "tensor_shape", tensor.shape)
-                out = dequantize(tensor.data, qtype, oshape, mid, dtype)
-                if out is not None:
-                    _state["stats"]["used"] += 1
-                    return out
-        _state["stats"]["fallback"] += 1
-        return orig(tensor, dtype, dequant_dtype)
+        out = _one_kernel(tensor, dtype, dequant_dtype)
+        _TALLY.add("used" if out is not None else "fallback")
+        return out if out is not None else orig(tensor, dtype, dequant_dtype)
     dequantize_tensor._weightferry = True
     return dequantize_tensor
 
 
 def _patched_get_weight(orig):
+    """GGMLLayer.get_weight with LoRA patches added inside the dequantisation (reference :464-492)."""
     def get_weight(self, tensor, dtype):
-        if tensor is None:
-            return None
-        pats = getattr(tensor, "patches", None)
-        qtype = getattr(tensor, "tensor_type", None)
-        if (pats and getattr(self, "patch_dtype", None) is None and qtype is not None and _supported(qtype)
-                and isinstance(dtype, torch.dtype) and getattr(tensor, "is_cuda", False)):
-            mid = dtype if self.dequant_dtype == "target" else self.dequant_dtype
-            if mid is None or isinstance(mid, torch.dtype):
-                oshape = getattr(tensor, "tensor_shape", tensor.shape)
-                patch_list = []
-                for patches, _key in pats:
-                    patch_list += list(patches)
-                loras = lora_factors(patch_list, *oshape) if len(oshape) == 2 else None
-                if loras:
-                    out = dequantize_lora(tensor.data, qtype, oshape, mid, dtype, loras)
-                    if out is not None:
-                        _state["stats"]["lora_used"] = _state["stats"].get("lora_used", 0) + 1
-                        return out
-                _state["stats"]["lora_fallback"] = _state["stats"].get("lora_fallback", 0) + 1
-        return orig(self, tensor, dtype)
+        if tensor is not None and getattr(tensor, "patches", None):
+            out = _lora_weight(self, tensor, dtype)
+            _TALLY.add("lora_used" if out is not None else "lora_fallback")
+            if out is not None:
+                return out
+        return orig(self, tensor, dtype) if tensor is not None else None
     get_weight._weightferry = True
     return get_weight
 
 
+def _gguf_ops():
+    """ComfyUI-GGUF's ops module (ComfyUI loads custom nodes under path-derived names ending in ComfyUI-GGUF.ops)."""
+    for name, mod in list(sys.modules.items()):
+        if mod is not None and name.endswith("ComfyUI-GGUF.ops") and hasattr(mod, "dequantize_tensor"):
+            return mod
+    return None
+
+
 def install(force=False):
-    """Replace ComfyUI-GGUF's ops.dequantize_tensor (and GGMLLayer.get_weight for LoRA) with the B200 kernels, unless
-    WEIGHTFERRY_GGUF_TRITON=0 (force: always), when ComfyUI-GGUF is loaded. Idempotent; True when installed. Raises
-    ExtensionMissing when the CUDA library is not built (no silent fallback)."""
+    """Put the B200 kernels in front of ComfyUI-GGUF's ops.dequantize_tensor (and GGMLLayer.get_weight for LoRA
+    patches) when ComfyUI-GGUF is loaded, unless WEIGHTFERRY_GGUF_TRITON=0 (force: always). Idempotent; True when
+    installed. Raises ExtensionMissing when the CUDA library is not built (no silent fallback)."""
     from ..utils.logging import log_info
     if not force and _env_get("WEIGHTFERRY_GGUF_TRITON") != "1":
         return False
-    ops = next((m for n, m in sys.modules.items() if n.endswith("ComfyUI-GGUF.ops") and m is not None), None)
-    if ops is None or not hasattr(ops, "dequantize_tensor"):
+    ops = _gguf_ops()
+    if ops is None:
         return False
-    _ext.lib()  # fail loudly now rather than at the first weight
-    if getattr(ops.dequantize_tensor, "_weightferry", False):
-        return True
-    _state["orig"], _state["ops"] = ops.dequantize_tensor, ops
-    ops.dequantize_tensor = _patched(ops.dequantize_tensor)
-    layer = getattr(ops, "GGMLLayer", None)
-    if _LORA and layer is not None and not getattr(layer.get_weight, "_weightferry", False):
-        _state["orig_gw"] = layer.get_weight
-        layer.get_weight = _patched_get_weight(layer.get_weight)
-    log_info("GGUF dequant on B200: ComfyUI-GGUF's Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q8_0 "
-             + ("and Q2_K .. Q6_K " if _kquants() else "") + "dequantisation in one kernel (WEIGHTFERRY_GGUF_TRITON).")
+    _ext.lib()  # fail now rather than at the first weight
+    if not getattr(ops.dequantize_tensor, "_weightferry", False):
+        _state["orig"], _state["ops"] = ops.dequantize_tensor, ops
+        ops.dequantize_tensor = _patched(ops.dequantize_tensor)
+        layer = getattr(ops, "GGMLLayer", None)
+        if _LORA and layer is not None and not getattr(layer.get_weight, "_weightferry", False):
+            _state["orig_gw"] = layer.get_weight
+            layer.get_weight = _patched_get_weight(layer.get_weight)
+        kinds = "Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q8_0" + (" and Q2_K .. Q6_K" if _kquants() else "")
+        log_info(f"GGUF dequant on B200: ComfyUI-GGUF's {kinds} in one kernel per weight (WEIGHTFERRY_GGUF_TRITON).")
     return True
 
 
 def uninstall():
-    if _state["ops"] is not None and _state.get("orig_gw") is not None:
-        _state["ops"].GGMLLayer.get_weight = _state["orig_gw"]
-        _state["orig_gw"] = None
-    if _state["ops"] is not None and _state["orig"] is not None:
-        _state["ops"].dequantize_tensor = _state["orig"]
-    _state["orig"] = _state["ops"] = None
+    """Give ComfyUI-GGUF its own functions back."""
+    ops = _state["ops"]
+    if ops is not None:
+        if _state.get("orig_gw") is not None:
+            ops.GGMLLayer.get_weight = _state["orig_gw"]
+        if _state["orig"] is not None:
+            ops.dequantize_tensor = _state["orig"]
+    _state.update(orig=None, ops=None, orig_gw=None)
 
 
 def stats(reset=False):
-    out = dict(_state["stats"])
+    """{"used", "fallback"[, "lora_used", "lora_fallback"]}: calls of the patched entry points."""
+    out = dict(_TALLY.counts)
     if reset:
-        _state["stats"] = {"used": 0, "fallback": 0}
+        _TALLY.reset()
     return out
