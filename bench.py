@@ -9,6 +9,9 @@ Workloads (seeded synthetic inputs with the configs' shap
            step through one batched launch (wf_dequant_gguf_batch). Inputs are larger than L2, so no flush.
   q8       configs[0]: Q8_0 5120x5120 -> bf16 (one launch per step; L2 flushed between steps).
   q4k      configs[1]'s single FFN weight, Q4_K 5120x13824 -> bf16 (one launch per step; L2 flushed).
+The default line also carries `stack`: configs[4], the streamed 14B block stack (the second half of BASELINE's metric,
+s/step at this N, tensor-parallel over the ranks), timed after the sweep in the same run with its H2D GB/s against
+the run's own pinned-copy probe, dequant-on-arrival ms per block and compute ms per forward (--stack-blocks 0: off).
 Metric: GGUF dequant output GB/s (bf16 bytes written per second, all ranks). `e2e` is the same metric through the
 reference-facing entry point (gguf_dequant.dequantize) with pinned host buffers: every step copies the packed
 bytes host -> device, dequantises and copies the bf16 weight device -> host, for one block's 16 tensors.
@@ -324,7 +327,14 @@ def run_sweep(torch, args, world, rank, dist):
         e2e = e2e_block(torch, gd, dev, args)
         e2e["value"] = round(sum_over_ranks(torch, dist, e2e["value"]), 2)
     launches = int(sum_over_ranks(torch, dist, launches_per_step * args.steps))
+    stack = None
+    if args.stack_blocks > 0:
+        torch.cuda.empty_cache()
+        barrier(torch, dist)
+        sr = stack_measure(torch, world, rank, dist, args.stack_blocks, args.stack_steps, args.stack_warmup)
+        stack = stack_subrecord(sr, world, args.stack_steps)
     return {
+        "stack": stack,
         "value": value, "ms_per_step": total_ms / args.steps, "kern_ms": kern_ms,
         "alg_bytes_per_launch": (in_bytes + out_bytes) / launches_per_step, "clk": clk.summary(), "e2e": e2e,
         "gpu_launches": launches, "mix_gbs": mix,
@@ -603,10 +613,12 @@ def h2d_probe(torch, dev, nbytes=1 << 30, reps=5):
     return best
 
 
-def run_stack(torch, args, world, rank, dist):
-    """a Cosmos-Predict2-14B-shaped stack of 36 blocks, Q8_0 weights in pinned host RAM streamed through
-    3 GPU slots and dequantised on arrival, batch 2 x 4096 tokens (+ 512 context tokens), tensor-parallel over the
-    ranks (column / row split, NCCL all-gather / reduce-scatter of the token rows). One step = one forward."""
+def stack_measure(torch, world, rank, dist, blocks, steps, warmup, slots=3, e2e=False):
+    """a Cosmos-Predict2-14B-shaped stack of `blocks` blocks, Q8_0 weights in pinned host RAM streamed
+    through `slots` GPU slots and dequantised on arrival, batch 2 x 4096 tokens (+ 512 context tokens), tensor-parallel
+    over the ranks (column / row split, NCCL all-gather / reduce-scatter of the token rows). One step = one forward;
+    `steps` forwards timed with CUDA events on the compute stream, max over ranks; then one more forward with the
+    streaming profiler's event timeline on (not timed)."""
     cb = _pkg("streaming.cosmos_block")
     stk = _pkg("streaming.stack")
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -618,7 +630,7 @@ def run_stack(torch, args, world, rank, dist):
     numa_cpus = _pkg("core.tiers.pinned").bind_to_gpu_numa(dev.index) if world > 1 else None
     probe = h2d_probe(torch, dev)
     t_build = time.perf_counter()
-    stack = stk.StreamedStack(cfg, args.blocks, dev, tp, seed=20261201 + 4, num_slots=args.slots)
+    stack = stk.StreamedStack(cfg, blocks, dev, tp, seed=20261201 + 4, num_slots=slots)
     build_s = time.perf_counter() - t_build
     g = torch.Generator(device=dev)
     g.manual_seed(20261201 + 4)
@@ -634,7 +646,7 @@ def run_stack(torch, args, world, rank, dist):
     def step():
         return stack.forward(x, emb, ctx, rope, batch, tokens, lora)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         out = step()
     barrier(torch, dist)
     stream = torch.cuda.current_stream(dev)
@@ -642,44 +654,68 @@ def run_stack(torch, args, world, rank, dist):
         barrier(torch, dist)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             out = step()
         e1.record(stream)
         barrier(torch, dist)
-    ms = max_over_ranks(torch, dist, e0.elapsed_time(e1) / args.steps)
+    ms = max_over_ranks(torch, dist, e0.elapsed_time(e1) / steps)
     finite = bool(torch.isfinite(out.float()).all().item())
-    h2d_rank = args.blocks * stack.bytes_per_block
+    h2d_rank = blocks * stack.bytes_per_block
     h2d_rate = h2d_rank / (ms / 1e3) / 1e9
-    # one more forward with the event timeline on (not timed)
-    from importlib import import_module
-    prof_mod = import_module("comfyui-weightferry_b200.streaming.profiler")
+    prof_mod = _pkg("streaming.profiler")
     stack.state.profiler = prof_mod._StreamProfiler(stack.state.num_stream, stack.bytes_per_block)
     step()
     summ = stack.state.profile_summary()["per_forward"][-1]
     stack.state.profiler = None
-    flops = cb.flops_per_block(cfg, batch, tokens, S) * args.blocks
-    e2e = None
-    if not args.no_e2e:
+    flops = cb.flops_per_block(cfg, batch, tokens, S) * blocks
+    e2e_rec = None
+    if e2e:
         hx = x.cpu().pin_memory()
         hy = torch.empty_like(hx).pin_memory()
         dx = torch.empty_like(x)
         torch.cuda.synchronize()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
-        for _ in range(max(1, args.steps // 2)):
+        for _ in range(max(1, steps // 2)):
             dx.copy_(hx, non_blocking=True)
             y = stack.forward(dx, emb, ctx, rope, batch, tokens, lora)
             hy.copy_(y, non_blocking=True)
         t1.record()
         torch.cuda.synchronize()
-        e_ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / max(1, args.steps // 2))
-        e2e = {"value": round(e_ms / 1e3, 4), "unit": "s/step", "h2d_bytes_per_step": hx.numel() * 2 + h2d_rank,
-               "d2h_bytes_per_step": hy.numel() * 2,
-               "note": "activation rows H2D + D2H per step around the streamed forward; weights stream H2D inside"}
+        e_ms = max_over_ranks(torch, dist, t0.elapsed_time(t1) / max(1, steps // 2))
+        e2e_rec = {"value": round(e_ms / 1e3, 4), "unit": "s/step", "h2d_bytes_per_step": hx.numel() * 2 + h2d_rank,
+                   "d2h_bytes_per_step": hy.numel() * 2,
+                   "note": "activation rows H2D + D2H per step around the streamed forward; weights stream H2D inside"}
     stack.close()
-    return {"ms": ms, "clk": clk.summary(), "e2e": e2e, "finite": finite, "probe": probe, "h2d_rate": h2d_rate,
-            "h2d_rank": h2d_rank, "flops": flops, "summary": summ, "build_s": build_s,
-            "slots": stack.state.num_slots, "numa_cpus": None if numa_cpus is None else len(numa_cpus)}
+    del stack
+    torch.cuda.empty_cache()
+    return {"ms": ms, "clk": clk.summary(), "e2e": e2e_rec, "finite": finite, "probe": probe, "h2d_rate": h2d_rate,
+            "h2d_rank": h2d_rank, "flops": flops, "summary": summ, "build_s": build_s, "blocks": blocks,
+            "slots": slots, "numa_cpus": None if numa_cpus is None else len(numa_cpus)}
+
+
+def stack_subrecord(r, world, steps):
+    """The stack's half of BASELINE's metric as a sub-record of the default line."""
+    summ = r["summary"]
+    return {
+        "metric": "streamed 14B DiT block-stack s/step", "value": round(r["ms"] / 1e3, 5), "unit": "s/step",
+        "higher_is_better": False, "scaling": "strong", "steps": steps, "n_gpus": world,
+        "parallelism": f"tp{world} (column/row split, sequence-sharded residual)", "blocks": r["blocks"],
+        "h2d_gbs_per_rank": round(r["h2d_rate"], 2), "h2d_probe_gbs_per_rank": round(r["probe"], 2),
+        "h2d_frac_of_probe": round(r["h2d_rate"] / r["probe"], 4),
+        "h2d_bytes_per_block_per_rank": r["h2d_rank"] // r["blocks"],
+        "dequant_on_arrival_ms_per_block_per_rank": round(summ["dequant_lora_ms"] / max(1, summ["streamed_blocks"]),
+                                                           4),
+        "compute_ms_per_forward": summ["streamed_compute_ms"], "dma_ms_per_forward": summ["dma_ms"],
+        "stall_ms_per_forward": summ["stall_ms"], "forward_ms_profiled": summ["forward_ms"],
+        "tflops_per_gpu": round(r["flops"] / world / (r["ms"] / 1e3) / 1e12, 1), "finite_output": r["finite"],
+        "build_s": round(r["build_s"], 1), "clocks": r["clk"],
+        "note": "timed after the sweep in the same run; profiled timeline from one extra (untimed) forward"}
+
+
+def run_stack(torch, args, world, rank, dist):
+    return stack_measure(torch, world, rank, dist, args.blocks, args.steps, args.warmup, slots=args.slots,
+                         e2e=not args.no_e2e)
 
 
 def cpu_baseline_stack(seconds=10.0):
@@ -1192,6 +1228,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--blocks", type=int, default=36, help="sweep: checkpoint blocks per rank (36 = Cosmos-14B)")
+    ap.add_argument("--stack-blocks", type=int, default=36,
+                    help="sweep: blocks of the streamed-stack sub-record timed after the sweep (0: none)")
+    ap.add_argument("--stack-steps", type=int, default=3, help="sweep: timed forwards of the stack sub-record")
+    ap.add_argument("--stack-warmup", type=int, default=2, help="sweep: untimed forwards before them")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -1238,6 +1278,8 @@ def main():
                          else "dequant_kernel (single weight)"},
             "cpu_baseline": cpu, "e2e": r["e2e"], "gpu_launches": r["gpu_launches"], "clocks": r["clk"],
         }
+        if r.get("stack") is not None:
+            line["stack"] = r["stack"]
         if r.get("mix_gbs"):
             # the copy-based peak assumes read = write; this traffic is write-heavy (in : out about 1 : 3.6), and a
             # plain streaming kernel with the same byte counts (wf_hbm_probe) is the ceiling it is measured against too
