@@ -448,8 +448,11 @@ def install(parts=None):
     if parts:
         _get_kernels()  # raises when the CUDA library is missing: no silent fallback
     if _state["orig"] is None:
-        _state["orig"] = {"forward": p2.Block.forward, "compute_qkv": p2.Attention.compute_qkv,
-                          "mlp_forward": p2.GPT2FeedForward.forward}
+        current = {"forward": p2.Block.forward, "compute_qkv": p2.Attention.compute_qkv,
+                   "mlp_forward": p2.GPT2FeedForward.forward}
+        if any(fn in (_block_forward, _compute_qkv, _mlp_forward) for fn in current.values()):
+            raise RuntimeError("Cosmos fused block: ComfyUI's classes are patched but their own methods were lost")
+        _state["orig"] = current
     orig = _state["orig"]
     _state["parts"] = parts
     p2.Block.forward = _block_forward if "mod" in parts else orig["forward"]

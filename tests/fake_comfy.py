@@ -229,6 +229,10 @@ class Block(torch.nn.Module):
 
     def __init__(self, x_dim, context_dim, num_heads, mlp_dim, use_adaln_lora, adaln_lora_dim, make, norm_w):
         super().__init__()
+        # the sub-layer classes of the registered module, as a block of the real module uses its own module's classes
+        # (which is what install() patches)
+        p2 = sys.modules["comfy.ldm.cosmos.predict2"]
+        Attention, GPT2FeedForward = p2.Attention, p2.GPT2FeedForward
         hd = x_dim // num_heads
         self.use_adaln_lora = use_adaln_lora
         for sub in ("self_attn", "cross_attn", "mlp"):

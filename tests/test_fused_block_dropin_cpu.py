@@ -12,8 +12,8 @@ from conftest import wf
 
 @pytest.fixture()
 def p2():
+    fb = wf("enhancers.fused_block")  # imported before the stand-in exists: no install at import
     mod = fake_comfy.register()
-    fb = wf("enhancers.fused_block")
     saved = (fb._state["parts"], fb._state["orig"])
     fb._state["orig"] = None
     yield mod

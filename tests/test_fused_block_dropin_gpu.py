@@ -27,8 +27,8 @@ NO_NORMS = ("mod", "qkv", "modq", "gelu", "res")
 
 @pytest.fixture()
 def p2(cuda):
+    fb = wf("enhancers.fused_block")  # imported before the stand-in exists: no install at import
     mod = fake_comfy.register()
-    fb = wf("enhancers.fused_block")
     saved = (fb._state["parts"], fb._state["orig"])
     fb._state["orig"] = None
     yield mod
