@@ -23,4 +23,4 @@ def test_tp_stack_matches_single_gpu(cuda):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     res = subprocess.run(cmd, cwd=REPO, capture_output=True, text=True, env=env)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
-    assert "relative L2 error" in res.stdout
+    assert res.stdout.count("vs single GPU") == world

@@ -1,6 +1,16 @@
 """torchrun worker of the tensor-parallel GPU test (tests/test_tp_gpu.py): each rank streams its shards of a small
-Cosmos stack and runs it tensor-parallel over NCCL; rank 0 gathers the token rows and compares them with the same
-stack run on one GPU with the full weights (same seeds). Exit code 0 = within tolerance."""
+Cosmos stack and runs it tensor-parallel over NCCL; rank 0 also runs the same stack on one GPU with the full weights
+(same seeds) and broadcasts the result, and every rank checks its own token rows (its shard) against it:
+
+  |y - y_ref| <= 0.05 * rms(y_ref row)             per element (the three reduce-scatters of a block each add one
+                                                   bf16 rounding of two partial sums to the row-parallel outputs,
+                                                   which the following sub-layers carry on), and
+  ||(y - x) - (y_ref - x)|| <= 1e-2 ||y_ref - x||  for the shard's update (x its input rows): a head group or MLP
+                                                   slice taken from the wrong shard changes about 1 / world of a
+                                                   sub-layer's output, far above this bound.
+
+The overlapped row-chunk form (WEIGHTFERRY_TP_CHUNKS=4) must agree with the unchunked one within 1e-2 relative L2.
+Exit code 0 = every rank within tolerance."""
 
 import datetime
 import os
@@ -38,17 +48,22 @@ def main():
     chunked = stack.forward(x[rank * rows:(rank + 1) * rows].contiguous(), emb, ctx, rope, batch, tokens, lora)
     os.environ.pop("WEIGHTFERRY_TP_CHUNKS")
     chunk_err = ((chunked.float() - out.float()).norm() / out.float().norm()).item()
-    full = tp.all_gather_rows(out)
-    ok = torch.ones(1, device="cuda")
+    ref = torch.empty((batch * tokens, cfg.hidden), dtype=torch.bfloat16, device="cuda")
     if rank == 0:
         single = stk.StreamedStack(cfg, 3, "cuda", cb.TP(single=True), seed=77, num_slots=2)
-        ref = single.forward(x, emb, ctx, rope, batch, tokens, lora)
-        err = ((full.float() - ref.float()).norm() / ref.float().norm()).item()
-        print(f"tp{world} vs single-GPU relative L2 error {err:.3e}; row chunks vs none {chunk_err:.3e}", flush=True)
-        if not (err < 2e-2 and chunk_err < 1e-2 and torch.isfinite(full.float()).all()):
-            ok.zero_()
+        ref.copy_(single.forward(x, emb, ctx, rope, batch, tokens, lora))
         single.close()
-    dist.broadcast(ok, 0)
+    dist.broadcast(ref, 0)
+    mine = slice(rank * rows, (rank + 1) * rows)
+    y, yr, x0 = out.double(), ref[mine].double(), x[mine].double()
+    rel = ((y - yr).abs() / yr.pow(2).mean(dim=1, keepdim=True).sqrt()).max().item()
+    upd = (((y - x0) - (yr - x0)).norm() / (yr - x0).norm()).item()
+    print(f"rank {rank}: tp{world} vs single GPU: max |d| / row rms {rel:.4f}, update rel-L2 {upd:.3e}; "
+          f"row chunks vs none {chunk_err:.3e}", flush=True)
+    ok = torch.ones(1, device="cuda")
+    if not (rel <= 0.05 and upd <= 1e-2 and chunk_err < 1e-2 and torch.isfinite(y).all()):
+        ok.zero_()
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     stack.close()
     dist.barrier()
     dist.destroy_process_group()
