@@ -15,10 +15,12 @@ reference restates for ComfyUI's Cosmos-Predict2 block (enhancers/fused_block.py
 * ``comfy.quant_ops``: a TensorWiseINT8Layout ``QuantizedTensor`` that ``F.linear`` dispatches to the stand-in of
   comfy_kitchen's int8 linear, ``QUANT_ALGOS``, and ``ck`` with that linear and ``rms_rope_split_half``.
 
-The stand-in kitchen int8 linear quantises each token with the oracle's restatement of the quantiser (the reference's
-reproduction of comfy_kitchen's ConvRot quantiser, pinned by the golden vectors), multiplies exactly (float64 sums of
-int8 products) and rescales in float32 as (acc * x_s) * w_s before the bf16 rounding -- this library's epilogue order
-(comfy_kitchen's own is closed). Its ``rms_rope_split_half`` is plain PyTorch float32 arithmetic, not kitchen's exact
+The stand-in kitchen int8 linear quantises each token as the reference's reproduction of comfy_kitchen's ConvRot
+quantiser does (on CUDA tensors this library's quantiser, which the golden vectors pin to that reproduction bit for
+bit, approximate float32 division included; on CPU tensors the oracle's restatement), multiplies exactly (float64
+sums of int8 products) and rescales in float32 as (acc * x_s) * w_s before the bf16 rounding -- this library's
+epilogue order (comfy_kitchen's own is closed). A drop-in test thus checks the library's GEMM, its pending inputs and
+its shared quantisation against an exact product, not the quantiser itself (the golden tests do that). Its ``rms_rope_split_half`` is plain PyTorch float32 arithmetic, not kitchen's exact
 summation order: only paths that both use it can be compared bit for bit."""
 
 import sys
@@ -37,16 +39,26 @@ def _oracle():
     return importlib.import_module("oracle.oracle")
 
 
+def _quantise(x2, convrot):
+    """Per-token int8 quantisation as comfy_kitchen's ConvRot quantiser does it: on CUDA tensors the library's quantiser
+    (pinned bit for bit to the reference's reproduction of kitchen's, whose float32 division is the GPU's
+    approximate one), on CPU tensors the oracle's restatement (exact division)."""
+    if x2.is_cuda:
+        import importlib
+        fk = importlib.import_module("comfyui-weightferry_b200.enhancers.fused_kernels")
+        q, sc = fk.quantize_rows(x2.contiguous(), rotate=convrot)
+        return q, sc.view(-1)
+    bits = x2.contiguous().view(torch.int16).numpy().view(np.uint16)
+    q, sc = _oracle().quant_rows(bits, pre=0, rotate=convrot)
+    return torch.from_numpy(q), torch.from_numpy(sc)
+
+
 def kitchen_int8_linear(x, qt, bias=None):
-    """bf16(((float(q(x) @ w_q^T)) * x_s) * w_s) with q(x) the oracle's per-token quantisation (ConvRot when the
-    weight says so)."""
+    """bf16(((float(q(x) @ w_q^T)) * x_s) * w_s) with q(x) the per-token quantisation of _quantise (ConvRot when
+    the weight says so) and the product summed exactly."""
     w_q, w_s = TensorWiseINT8Layout.get_plain_tensors(qt)
     k = x.shape[-1]
-    x2 = x.reshape(-1, k)
-    bits = x2.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
-    q, sc = _oracle().quant_rows(bits, pre=0, rotate=qt._params.convrot)
-    q = torch.from_numpy(q).to(x.device)
-    sc = torch.from_numpy(sc).to(x.device)
+    q, sc = _quantise(x.reshape(-1, k), qt._params.convrot)
     acc = q.double() @ w_q.double().t()           # exact: integer sums far below 2^53
     ws = w_s.reshape(-1).float()
     ws = ws if ws.numel() == w_q.shape[0] else ws.expand(w_q.shape[0])
