@@ -16,6 +16,7 @@
 #include <atomic>
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace wf {
 namespace {
@@ -296,6 +297,8 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
     const int t = threadIdx.x;
     int64_t row = blockIdx.x;
     if (row >= rows) return;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent: x is ready here
+    allow_dependents();
     uint2 raw[NV];
 #pragma unroll
     for (int j = 0; j < NV; ++j) raw[j] = __ldg(reinterpret_cast<const uint2 *>(x + row * K) + t + 128 * j);
@@ -351,6 +354,22 @@ int persistent_grid(int threads, size_t smem, int64_t items) {
     }
     const int64_t g = std::min<int64_t>(items, static_cast<int64_t>(o) * device_sm_count());
     return static_cast<int>(std::max<int64_t>(g, 1));
+}
+
+// A launch as a programmatic dependent of the previous kernel in the stream: its CTAs may be scheduled while that
+// kernel finishes; the kernel executes griddepcontrol.wait before its first global access.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int threads, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
 // ------------------------------------------------------------------------------------------------- RMSNorm-128
@@ -536,6 +555,118 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rms_rope_kernel(const __grid_
         __syncwarp();  // every lane has read this buffer before it is refilled (the next iteration's issue)
     }
     cp_async_wait<0>();
+}
+
+// ------------------------------------------------------------------------------------------------- kernel B (v2)
+// The same arithmetic as rms_rope_kernel, laid out for fewer instructions per value: one (tensor, batch-token) item
+// per warp (its rotations and weights read once for all its heads), one row per half-warp at a time, and lane p of a
+// half holding the reference's lanes 2p and 2p + 1 -- values 2p + 32 j and 2p + 1 + 32 j (j = 0..3), i.e. the 32-bit
+// words p + 16 j of the row, read and written with coalesced 4-byte accesses straight from / to global memory. The
+// reference's reduction tree maps onto xor shuffles with the same two operands at every node: level t + 16 is lane
+// p + 8 (xor 8) for the even and the odd lane sums, t + 8 xor 4, t + 4 xor 2, t + 2 xor 1, and the last level t + 1
+// is the lane's own even + odd sum. The RoPE pairs (d, d + 64) are words j and j + 2 of the lane: no exchange.
+// Launched as a programmatic dependent (griddepcontrol.wait before the first load).
+template <int WDT>
+__device__ __forceinline__ float2 load_w2(const void *w, int i) {  // weights i, i + 1 (i even)
+    if constexpr (WDT == WF_BF16) {
+        const uint32_t u = __ldg(reinterpret_cast<const uint32_t *>(static_cast<const __nv_bfloat16 *>(w) + i));
+        return make_float2(bf_lo(u), bf_hi(u));
+    } else if constexpr (WDT == WF_F16) {
+        const __half2 h = __ldg(reinterpret_cast<const __half2 *>(static_cast<const __half *>(w) + i));
+        return __half22float2(h);
+    } else {
+        return __ldg(reinterpret_cast<const float2 *>(static_cast<const float *>(w) + i));
+    }
+}
+
+constexpr int kRope2Warps = 8;  // warps (items) per CTA
+
+template <int WDT, bool F4, int R>
+__global__ void __launch_bounds__(kRope2Warps * 32) rms_rope_v2_kernel(const __grid_constant__ RopeTensors t,
+                                                                       int n_items, int n_tok, int heads, int tokens,
+                                                                       const float *__restrict__ f, float eps,
+                                                                       int64_t s_tok, int64_t s_d, int64_t s_i,
+                                                                       int64_t s_j) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    allow_dependents();
+    const int lane = threadIdx.x & 31, hf = lane >> 4, p = lane & 15;
+    const int item = blockIdx.x * kRope2Warps + (threadIdx.x >> 5);
+    if (item >= n_items) return;  // whole warps: the shuffles below involve both halves of a warp that runs
+    const int ti = item >= n_tok ? 1 : 0;
+    const int bt = item - ti * n_tok;
+    const int tok = bt % tokens;
+    // rotations of d = 2p + 32 m2 + e (m = 2 m2 + e: d = 2p, 2p + 1, 2p + 32, 2p + 33), as f00, f01, f10, f11
+    float rot[4][4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const float *fd = f + tok * s_tok + (2 * p + 32 * (m >> 1) + (m & 1)) * s_d;
+        if constexpr (F4) {
+            const float4 q = __ldg(reinterpret_cast<const float4 *>(fd));
+            rot[m][0] = q.x; rot[m][1] = q.y; rot[m][2] = q.z; rot[m][3] = q.w;
+        } else {
+            rot[m][0] = __ldg(fd); rot[m][1] = __ldg(fd + s_j); rot[m][2] = __ldg(fd + s_i);
+            rot[m][3] = __ldg(fd + s_i + s_j);
+        }
+    }
+    float2 w[4];  // weights at 2p + 32 j, 2p + 1 + 32 j
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = load_w2<WDT>(t.w[ti], 2 * p + 32 * j);
+    const uint32_t *x = reinterpret_cast<const uint32_t *>(t.x[ti]) + static_cast<size_t>(bt) * heads * 64 + p;
+    uint32_t *out = reinterpret_cast<uint32_t *>(t.out[ti]) + static_cast<size_t>(bt) * heads * 64 + p;
+    // both halves run the same iterations (full-warp shuffles); a half whose row is past the last head computes on
+    // the last row again and does not store
+    for (int h0 = 0; h0 < heads; h0 += 2 * R) {
+        uint32_t u[R][4];
+        int row[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            row[r] = h0 + 2 * r + hf;  // rows h0 .. h0 + 2R - 1, the halves interleaved
+            const int rr = row[r] < heads ? row[r] : heads - 1;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) u[r][j] = __ldg(x + rr * 64 + 16 * j);
+        }
+        float ev[R], od[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {  // the reference's lanes 2p (even) and 2p + 1 (odd): fma of squares from 0
+            float a = __fmul_rn(bf_lo(u[r][0]), bf_lo(u[r][0])), b = __fmul_rn(bf_hi(u[r][0]), bf_hi(u[r][0]));
+#pragma unroll
+            for (int j = 1; j < 4; ++j) {
+                a = __fmaf_rn(bf_lo(u[r][j]), bf_lo(u[r][j]), a);
+                b = __fmaf_rn(bf_hi(u[r][j]), bf_hi(u[r][j]), b);
+            }
+            ev[r] = a;
+            od[r] = b;
+        }
+#pragma unroll
+        for (int off = 8; off >= 1; off >>= 1) {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                ev[r] = __fadd_rn(ev[r], __shfl_xor_sync(0xFFFFFFFFu, ev[r], off));
+                od[r] = __fadd_rn(od[r], __shfl_xor_sync(0xFFFFFFFFu, od[r], off));
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const float rs = rsqrt_approx(__fadd_rn(__fmul_rn(__fadd_rn(ev[r], od[r]), 0.0078125f), eps));
+            float2 n[4];  // R16((x * rs) * w) at 2p + 32 j, 2p + 1 + 32 j
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                n[j] = r16x2(__fmul_rn(__fmul_rn(bf_lo(u[r][j]), rs), w[j].x),
+                             __fmul_rn(__fmul_rn(bf_hi(u[r][j]), rs), w[j].y));
+            if (row[r] < heads) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {  // pairs (d, d + 64): words j and j + 2
+                    const float *re = rot[2 * j], *ro = rot[2 * j + 1];
+                    out[row[r] * 64 + 16 * j] =
+                        pack2(__fmaf_rn(re[0], n[j].x, __fmul_rn(re[1], n[j + 2].x)),
+                              __fmaf_rn(ro[0], n[j].y, __fmul_rn(ro[1], n[j + 2].y)));
+                    out[row[r] * 64 + 16 * (j + 2)] =
+                        pack2(__fmaf_rn(re[2], n[j].x, __fmul_rn(re[3], n[j + 2].x)),
+                              __fmaf_rn(ro[2], n[j].y, __fmul_rn(ro[3], n[j + 2].y)));
+                }
+            }
+        }
+    }
 }
 
 // ------------------------------------------------------------------------------------------------- quantiser
@@ -1117,10 +1248,11 @@ extern "C" WF_API int wf_ln_modulate(const void *x, const void *s1, const void *
     auto S = static_cast<const __nv_bfloat16 *>(s1);
     auto H = static_cast<const __nv_bfloat16 *>(shift);
     auto O = static_cast<__nv_bfloat16 *>(out);
+    cudaError_t e = cudaSuccess;
 #define WF_LN(NV)                                                                                    \
     case NV: {                                                                                       \
         const int g = persistent_grid<ln_modulate_kernel<NV>>(128, 0, rows);                         \
-        ln_modulate_kernel<NV><<<g, 128, 0, s>>>(X, S, H, O, rows, K, rows_per_group, eps);          \
+        e = launch_pdl(ln_modulate_kernel<NV>, g, 128, s, X, S, H, O, rows, K, rows_per_group, eps);  \
         break;                                                                                       \
     }
     switch (K / 512) {
@@ -1128,7 +1260,7 @@ extern "C" WF_API int wf_ln_modulate(const void *x, const void *s1, const void *
 #undef WF_LN
         default: return WF_ERR_UNSUPPORTED;
     }
-    return static_cast<int>(cudaGetLastError());
+    return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 extern "C" WF_API int wf_rms_norm_128(const void *x, const void *w, int w_dtype, void *out, int64_t n_rows, float eps,
@@ -1145,6 +1277,23 @@ extern "C" WF_API int wf_rms_norm_128(const void *x, const void *w, int w_dtype,
 
 namespace wf {
 namespace {
+
+// WEIGHTFERRY_ROPE_V1=1 keeps the shared-memory kernel (rms_rope_kernel) for every launch
+bool rope_v2() {
+    static const bool v2 = [] {
+        const char *v = getenv("WEIGHTFERRY_ROPE_V1");
+        return !(v != nullptr && v[0] == '1');
+    }();
+    return v2;
+}
+
+int rope_rows() {
+    static const int r = [] {
+        const char *v = getenv("WEIGHTFERRY_ROPE_ROWS");
+        return (v != nullptr && v[0] == '4') ? 4 : 2;
+    }();
+    return r;
+}
 
 int rope_launch(const RopeTensors &t, int n_tensors, const float *freqs, int64_t f_stride_token, int64_t f_stride_d,
                 int64_t f_stride_i, int64_t f_stride_j, int w_dtype, int64_t batch, int64_t tokens, int64_t heads,
@@ -1163,6 +1312,40 @@ int rope_launch(const RopeTensors &t, int n_tensors, const float *freqs, int64_t
     const bool f4 = f_stride_j == 1 && f_stride_i == 2 && f_stride_d % 4 == 0 && f_stride_token % 4 == 0 &&
                     al(freqs, 16);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t n_items = n_tensors * n_tok;
+    // v2 reads weight pairs as one 4-byte (bf16 / f16) or 8-byte (f32) word
+    bool w_pairs = true;
+    for (int i = 0; i < n_tensors; ++i) w_pairs = w_pairs && al(t.w[i], 2 * dtype_size(w_dtype));
+    if (n_items <= INT32_MAX / 2 && heads <= 65536 && n_tok * heads * 64 <= INT32_MAX && tokens <= INT32_MAX &&
+        w_pairs && rope_v2()) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>((n_items + kRope2Warps - 1) / kRope2Warps), 1, 1);
+        cfg.blockDim = dim3(kRope2Warps * 32, 1, 1);
+        cfg.stream = s;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr.val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        const int ni = static_cast<int>(n_items), nt = static_cast<int>(n_tok), hd = static_cast<int>(heads),
+                  tk = static_cast<int>(tokens);
+        cudaError_t e;
+#define WF_RV2(WD, F)                                                                                             \
+    e = rope_rows() == 4                                                                                        \
+            ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 4>, t, ni, nt, hd, tk, freqs, eps,              \
+                                 f_stride_token, f_stride_d, f_stride_i, f_stride_j)                            \
+            : cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 2>, t, ni, nt, hd, tk, freqs, eps,              \
+                                 f_stride_token, f_stride_d, f_stride_i, f_stride_j)
+        if (w_dtype == WF_BF16) {
+            if (f4) WF_RV2(WF_BF16, true); else WF_RV2(WF_BF16, false);
+        } else if (w_dtype == WF_F16) {
+            if (f4) WF_RV2(WF_F16, true); else WF_RV2(WF_F16, false);
+        } else {
+            if (f4) WF_RV2(WF_F32, true); else WF_RV2(WF_F32, false);
+        }
+#undef WF_RV2
+        return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
+    }
     constexpr int kT = kRopeWarps * 32;
     if (f4) {
         rms_rope_kernel<true><<<persistent_grid<rms_rope_kernel<true>>(kT, 0, blocks), kT, 0, s>>>(
