@@ -613,7 +613,49 @@ def h2d_probe(torch, dev, nbytes=1 << 30, reps=5):
     return best
 
 
-def stack_measure(torch, world, rank, dist, blocks, steps, warmup, slots=3, e2e=False):
+_KERNEL_KINDS = (("nccl", ("nccl",)), ("gemm", ("gemm", "cutlass", "xmma", "nvjet", "sm100", "cublas")),
+                 ("attention", ("flash", "fmha", "attention", "sdpa", "softmax")),
+                 ("dequant", ("dequant_kernel",)), ("prologue", ("ln_modulate", "rms_rope", "rms128", "gated_residual")))
+
+
+def kernel_breakdown(torch, step, dist):
+    """GPU time of one (untimed) forward per kind of kernel on this rank, from torch.profiler's CUDA activity (names
+    matched by substring: NCCL collectives, GEMMs, attention, the dequantisation on arrival, the prologue kernels,
+    other) plus the host-to-device copies; each rank's figures are gathered to rank 0."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    kinds = {k: 0.0 for k, _ in _KERNEL_KINDS}
+    kinds.update(other=0.0, h2d_copy=0.0)
+    for ev in prof.events():
+        dt = getattr(ev, "device_time_total", None)
+        if dt is None:
+            dt = getattr(ev, "cuda_time_total", 0.0)
+        if not dt or ev.device_type is None or "cuda" not in str(ev.device_type).lower():
+            continue
+        name = ev.name.lower()
+        if "memcpy" in name and ("htod" in name or "host to device" in name or "h2d" in name):
+            kinds["h2d_copy"] += dt
+            continue
+        if "memcpy" in name or "memset" in name:
+            continue
+        for kind, keys in _KERNEL_KINDS:
+            if any(k in name for k in keys):
+                kinds[kind] += dt
+                break
+        else:
+            kinds["other"] += dt
+    mine = {k: round(v / 1e3, 2) for k, v in kinds.items()}  # ms
+    if dist is None:
+        return [mine]
+    every = [None] * dist.get_world_size()
+    dist.all_gather_object(every, mine)
+    return every
+
+
+def stack_measure(torch, world, rank, dist, blocks, steps, warmup, slots=3, e2e=False, profile=False):
     """a Cosmos-Predict2-14B-shaped stack of `blocks` blocks, Q8_0 weights in pinned host RAM streamed
     through `slots` GPU slots and dequantised on arrival, batch 2 x 4096 tokens (+ 512 context tokens), tensor-parallel
     over the ranks (column / row split, NCCL all-gather / reduce-scatter of the token rows). One step = one forward;
@@ -667,6 +709,7 @@ def stack_measure(torch, world, rank, dist, blocks, steps, warmup, slots=3, e2e=
     step()
     summ = stack.state.profile_summary()["per_forward"][-1]
     stack.state.profiler = None
+    breakdown = kernel_breakdown(torch, step, dist) if profile else None
     flops = cb.flops_per_block(cfg, batch, tokens, S) * blocks
     e2e_rec = None
     if e2e:
@@ -691,6 +734,7 @@ def stack_measure(torch, world, rank, dist, blocks, steps, warmup, slots=3, e2e=
     torch.cuda.empty_cache()
     return {"ms": ms, "clk": clk.summary(), "e2e": e2e_rec, "finite": finite, "probe": probe, "h2d_rate": h2d_rate,
             "h2d_rank": h2d_rank, "flops": flops, "summary": summ, "build_s": build_s, "blocks": blocks,
+            "breakdown": breakdown,
             "slots": slots, "numa_cpus": None if numa_cpus is None else len(numa_cpus)}
 
 
@@ -715,7 +759,7 @@ def stack_subrecord(r, world, steps):
 
 def run_stack(torch, args, world, rank, dist):
     return stack_measure(torch, world, rank, dist, args.blocks, args.steps, args.warmup, slots=args.slots,
-                         e2e=not args.no_e2e)
+                         e2e=not args.no_e2e, profile=args.profile)
 
 
 def cpu_baseline_stack(seconds=10.0):
@@ -774,7 +818,8 @@ def finish_stack(torch, args, world, rank, dist, r):
                        "h2d_probe_gbs_per_rank": round(r["probe"], 2), "finite_output": r["finite"],
                        "numa_local_cpus_per_rank": r.get("numa_cpus"),
                        "build_s": round(r["build_s"], 1),
-                       "timeline_one_forward": r["summary"]},
+                       "timeline_one_forward": r["summary"],
+                       "kernel_ms_per_rank_one_forward": r.get("breakdown")},
             "roofline": {"bound": "pcie_h2d", "achieved": round(r["h2d_rate"], 2), "peak": round(r["probe"], 2),
                          "unit": "GB/s per rank", "frac": round(frac, 4), "traffic": None,
                          "peak_source": "pinned 1 GiB cudaMemcpyAsync H2D measured in this run",
@@ -1224,6 +1269,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="stack: GPU time per kind of kernel of one extra forward (torch.profiler), every rank")
     ap.add_argument("--blocks", type=int, default=36, help="sweep: checkpoint blocks per rank (36 = Cosmos-14B)")
     ap.add_argument("--stack-blocks", type=int, default=36,
                     help="sweep: blocks of the streamed-stack sub-record timed after the sweep (0: none)")
