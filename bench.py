@@ -331,7 +331,8 @@ def run_sweep(torch, args, world, rank, dist):
     if args.stack_blocks > 0:
         torch.cuda.empty_cache()
         barrier(torch, dist)
-        sr = stack_measure(torch, world, rank, dist, args.stack_blocks, args.stack_steps, args.stack_warmup)
+        sr = stack_measure(torch, world, rank, dist, args.stack_blocks, args.stack_steps, args.stack_warmup,
+                           parallel=args.parallel)
         stack = stack_subrecord(sr, world, args.stack_steps)
     return {
         "stack": stack,
@@ -655,7 +656,8 @@ def kernel_breakdown(torch, step, dist):
     return every
 
 
-def stack_measure(torch, world, rank, dist, blocks, steps, warmup, slots=3, e2e=False, profile=False):
+def stack_measure(torch, world, rank, dist, blocks, steps, warmup, slots=3, e2e=False, profile=False,
+                  parallel="sp"):
     """a Cosmos-Predict2-14B-shaped stack of `blocks` blocks, Q8_0 weights in pinned host RAM streamed
     through `slots` GPU slots and dequantised on arrival, batch 2 x 4096 tokens (+ 512 context tokens), tensor-parallel
     over the ranks (column / row split, NCCL all-gather / reduce-scatter of the token rows). One step = one forward;
@@ -672,7 +674,8 @@ def stack_measure(torch, world, rank, dist, blocks, steps, warmup, slots=3, e2e=
     numa_cpus = _pkg("core.tiers.pinned").bind_to_gpu_numa(dev.index) if world > 1 else None
     probe = h2d_probe(torch, dev)
     t_build = time.perf_counter()
-    stack = stk.StreamedStack(cfg, blocks, dev, tp, seed=20261201 + 4, num_slots=slots)
+    sp = cb.SP(batch, tokens) if parallel == "sp" else None
+    stack = stk.StreamedStack(cfg, blocks, dev, tp, seed=20261201 + 4, num_slots=slots, parallel=parallel, sp=sp)
     build_s = time.perf_counter() - t_build
     g = torch.Generator(device=dev)
     g.manual_seed(20261201 + 4)
@@ -734,8 +737,15 @@ def stack_measure(torch, world, rank, dist, blocks, steps, warmup, slots=3, e2e=
     torch.cuda.empty_cache()
     return {"ms": ms, "clk": clk.summary(), "e2e": e2e_rec, "finite": finite, "probe": probe, "h2d_rate": h2d_rate,
             "h2d_rank": h2d_rank, "flops": flops, "summary": summ, "build_s": build_s, "blocks": blocks,
-            "breakdown": breakdown,
+            "breakdown": breakdown, "parallel": parallel,
             "slots": slots, "numa_cpus": None if numa_cpus is None else len(numa_cpus)}
+
+
+def _parallel_text(parallel, world):
+    if parallel == "sp":
+        return (f"sp{world} (each rank streams 1/{world} of every block's bytes, all-gathered over NVLink into "
+                "whole blocks; token rows split over the ranks; keys / values gathered within a sample)")
+    return f"tp{world} (column/row split, sequence-sharded residual)"
 
 
 def stack_subrecord(r, world, steps):
@@ -744,7 +754,7 @@ def stack_subrecord(r, world, steps):
     return {
         "metric": "streamed 14B DiT block-stack s/step", "value": round(r["ms"] / 1e3, 5), "unit": "s/step",
         "higher_is_better": False, "scaling": "strong", "steps": steps, "n_gpus": world,
-        "parallelism": f"tp{world} (column/row split, sequence-sharded residual)", "blocks": r["blocks"],
+        "parallelism": _parallel_text(r["parallel"], world), "blocks": r["blocks"],
         "h2d_gbs_per_rank": round(r["h2d_rate"], 2), "h2d_probe_gbs_per_rank": round(r["probe"], 2),
         "h2d_frac_of_probe": round(r["h2d_rate"] / r["probe"], 4),
         "h2d_bytes_per_block_per_rank": r["h2d_rank"] // r["blocks"],
@@ -759,7 +769,7 @@ def stack_subrecord(r, world, steps):
 
 def run_stack(torch, args, world, rank, dist):
     return stack_measure(torch, world, rank, dist, args.blocks, args.steps, args.warmup, slots=args.slots,
-                         e2e=not args.no_e2e, profile=args.profile)
+                         e2e=not args.no_e2e, profile=args.profile, parallel=args.parallel)
 
 
 def cpu_baseline_stack(seconds=10.0):
@@ -813,7 +823,7 @@ def finish_stack(torch, args, world, rank, dist, r):
             "config": {"workload": "Cosmos-Predict2-14B-shaped stack (configs[4]): 36 blocks, hidden 5120, 40 x 128 "
                                    "heads, MLP 20480, Q8_0 weights in pinned host RAM, batch 2 x 4096 tokens + 512 "
                                    "context tokens", "blocks": args.blocks, "slots": r["slots"],
-                       "parallelism": f"tp{world} (column/row split, sequence-sharded residual)",
+                       "parallelism": _parallel_text(r["parallel"], world),
                        "h2d_bytes_per_block_per_rank": r["h2d_rank"] // args.blocks,
                        "h2d_probe_gbs_per_rank": round(r["probe"], 2), "finite_output": r["finite"],
                        "numa_local_cpus_per_rank": r.get("numa_cpus"),
@@ -1269,6 +1279,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--parallel", default="sp", choices=["sp", "tp"],
+                    help="stack over N GPUs: sp = whole blocks per rank on its token rows, weights gathered; tp = "
+                         "tensor parallel")
     ap.add_argument("--profile", action="store_true",
                     help="stack: GPU time per kind of kernel of one extra forward (torch.profiler), every rank")
     ap.add_argument("--blocks", type=int, default=36, help="sweep: checkpoint blocks per rank (36 = Cosmos-14B)")

@@ -366,6 +366,106 @@ def block_forward(x_rows, emb, ctx, rope, W, cfg, tp, batch, tokens, lora_term=N
     return _residual(x_rows, gate, o, row0, tokens)
 
 
+class SP:
+    """The sequence-parallel ranks of the streamed stack (streaming/stack.py, parallel="sp"): the (batch * tokens, D)
+    token rows split into equal ranges in rank order, each rank running whole blocks on its range. A range either
+    holds whole samples or lies inside one sample; the ranks that share a sample (``kv_ranks`` of them) gather
+    their keys and values for the self-attention, within a process group of their own."""
+
+    def __init__(self, batch, tokens, group=None):
+        import torch.distributed as dist
+        self.dist = dist if dist.is_available() and dist.is_initialized() else None
+        self.world_group = group
+        self.world = self.dist.get_world_size(group) if self.dist else 1
+        self.rank = self.dist.get_rank(group) if self.dist else 0
+        self.gloo = bool(self.dist) and self.dist.get_backend(group) == "gloo"
+        rows = batch * tokens
+        if rows % self.world:
+            raise ValueError(f"{self.world} ranks do not divide {rows} token rows")
+        self.rows = rows // self.world
+        if self.rows >= tokens:
+            if self.rows % tokens:
+                raise ValueError(f"a rank's {self.rows} rows are not whole samples of {tokens} tokens")
+            self.kv_ranks = 1
+        else:
+            if tokens % self.rows:
+                raise ValueError(f"{self.rows} rows per rank do not divide a sample of {tokens} tokens")
+            self.kv_ranks = tokens // self.rows
+        self.kv_group = None
+        if self.kv_ranks > 1:
+            members = None
+            for g in range(self.world // self.kv_ranks):  # every rank creates every group, in one order
+                ranks = list(range(g * self.kv_ranks, (g + 1) * self.kv_ranks))
+                pg = self.dist.new_group(ranks)
+                if self.rank in ranks:
+                    members = pg
+            self.kv_group = members
+
+    def gather_kv(self, k, v):
+        """This sample's keys and values of every rank that holds part of it, in token order: (1, L_local, H, d)
+        each -> (1, L, H, d) each."""
+        if self.kv_ranks == 1:
+            return k, v
+        out = []
+        for t in (k, v):
+            t = t.contiguous()
+            shape = (t.shape[0], t.shape[1] * self.kv_ranks) + tuple(t.shape[2:])
+            if self.gloo:
+                parts = [torch.empty_like(t) for _ in range(self.kv_ranks)]
+                self.dist.all_gather(parts, t, group=self.kv_group)
+                out.append(torch.cat(parts, dim=1))
+            else:
+                full = torch.empty(shape, dtype=t.dtype, device=t.device)
+                self.dist.all_gather_into_tensor(full, t, group=self.kv_group)
+                out.append(full)
+        return out[0], out[1]
+
+
+def block_forward_sp(x_rows, emb, ctx, rope, W, cfg, sp, batch, tokens, lora_term=None):
+    """One block with whole weights on this rank's token rows x_rows (n, D) -- rows [rank * n, (rank + 1) * n) of
+    the (batch * tokens, D) stream; emb (B, D), ctx (B, S, ctx_dim), rope (1, tokens, 1, 64, 2, 2), lora_term
+    (B, 3D) or None as in block_forward. Only the self-attention's keys and values cross ranks (SP.gather_kv)."""
+    n, D = x_rows.shape
+    row0 = sp.rank * n
+    hd, H, eps = cfg.head_dim, cfg.heads, cfg.eps
+    b0 = row0 // tokens
+    if n >= tokens:
+        nb, L, t0 = n // tokens, tokens, 0
+    else:
+        nb, L, t0 = 1, n, row0 % tokens
+    emb_b, ctx_b = emb[b0:b0 + nb], ctx[b0:b0 + nb]
+    lora_b = emb.new_zeros(()) if lora_term is None else lora_term[b0:b0 + nb]
+    rope_b = rope[:, t0:t0 + L]
+
+    # --- self-attention: local q; keys and values of the whole sample
+    shift, scale, gate = adaln(W, "self_attn", emb_b, lora_b)
+    normed = _ln_mod_rows(x_rows, scale, shift, 0, L, eps)
+    q = F.linear(normed, W["self_attn.q_proj.weight"]).view(nb, L, H, hd)
+    k = F.linear(normed, W["self_attn.k_proj.weight"]).view(nb, L, H, hd)
+    v = F.linear(normed, W["self_attn.v_proj.weight"]).view(nb, L, H, hd)
+    q, k = _sf.rms_rope_pair(q, k, rope_b, W["self_attn.q_norm.weight"], W["self_attn.k_norm.weight"], eps)
+    k, v = sp.gather_kv(k, v)
+    a = _attention(q, k, v).view(n, D)
+    x_rows = _residual(x_rows, gate, F.linear(a, W["self_attn.output_proj.weight"]), 0, L)
+
+    # --- cross-attention
+    shift, scale, gate = adaln(W, "cross_attn", emb_b, lora_b)
+    normed = _ln_mod_rows(x_rows, scale, shift, 0, L, eps)
+    q = _fb.rms_norm_128(F.linear(normed, W["cross_attn.q_proj.weight"]).view(nb, L, H, hd).contiguous(),
+                         W["cross_attn.q_norm.weight"], eps)
+    S = ctx_b.shape[1]
+    kc = _fb.rms_norm_128(F.linear(ctx_b, W["cross_attn.k_proj.weight"]).view(nb, S, H, hd).contiguous(),
+                          W["cross_attn.k_norm.weight"], eps)
+    vc = F.linear(ctx_b, W["cross_attn.v_proj.weight"]).view(nb, S, H, hd)
+    a = _attention(q, kc, vc).view(n, D)
+    x_rows = _residual(x_rows, gate, F.linear(a, W["cross_attn.output_proj.weight"]), 0, L)
+
+    # --- MLP
+    shift, scale, gate = adaln(W, "mlp", emb_b, lora_b)
+    h = F.gelu(F.linear(_ln_mod_rows(x_rows, scale, shift, 0, L, eps), W["mlp.layer1.weight"]))
+    return _residual(x_rows, gate, F.linear(h, W["mlp.layer2.weight"]), 0, L)
+
+
 def flops_per_block(cfg, batch, tokens, ctx_tokens):
     """Dense GEMM + attention FLOPs of one block (all ranks together)."""
     M, D, Mh = batch * tokens, cfg.hidden, cfg.mlp

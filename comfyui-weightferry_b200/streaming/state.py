@@ -64,10 +64,13 @@ class BlockLayout:
     """Where each parameter of a block lives: in the flat packed buffer (host and slot, 256-byte aligned) and, for
     GGUF parameters, in the slot's dequantised weight buffer (compute dtype, 256-byte aligned)."""
 
-    def __init__(self, specs, compute_dtype=torch.bfloat16):
+    def __init__(self, specs, compute_dtype=torch.bfloat16, pad_to=1):
         self.specs = list(specs)
         self.compute_dtype = compute_dtype
         self.offsets, self.flat_bytes = flat_layout([p.packed_bytes for p in self.specs])
+        # a flat size that splits into `pad_to` equal, 256-byte aligned ranges (the gathered transfer's shards)
+        unit = 256 * max(1, int(pad_to))
+        self.flat_bytes = (self.flat_bytes + unit - 1) // unit * unit
         q = [p for p in self.specs if p.qtype is not None]
         self.q_specs = q
         self.w_offsets, self.weight_bytes = flat_layout([p.numel * compute_dtype.itemsize for p in q])
@@ -80,10 +83,19 @@ class BlockLayout:
 class _StreamState:
     """GPU slots, transfer / dequant streams and events of one streamed block list (one owner, one device)."""
 
-    def __init__(self, device, host_flats, layout, num_slots=None, profile=None, ring=None):
+    def __init__(self, device, host_flats, layout, num_slots=None, profile=None, ring=None, gather=None):
         self.device = torch.device(device)
         self.host_flats = host_flats          # per block: flat pinned uint8 tensor (DMA source), None: SSD tier
         self.layout = layout
+        # gather = (process group, rank, world): each host flat holds only this rank's equal byte range of the block;
+        # the ranks' ranges are all-gathered into the slot after the copy (streaming/stack.py's "sp" mode)
+        self.gather = gather if gather is not None and gather[2] > 1 else None
+        if self.gather is not None:
+            _g, grank, gworld = self.gather
+            if layout.flat_bytes % gworld or ring is not None:
+                raise ValueError("a gathered transfer needs a flat size divisible by the ranks and no SSD tier")
+            self.shard_bytes = layout.flat_bytes // gworld
+            self.shard_lo = grank * self.shard_bytes
         self.num_stream = len(host_flats)
         # SSD tier: the blocks without a host flat are read by `ring` (core/tiers/sources.DiskRing) in block order
         disk = [s for s, f in enumerate(host_flats) if f is None]
@@ -122,6 +134,9 @@ class _StreamState:
         want_prof = profile if profile is not None else _env.get("WEIGHTFERRY_PROFILE") == "1"
         self.profiler = _StreamProfiler(self.num_stream, layout.flat_bytes) if want_prof else None
         self.uploader = None
+        if self.gather is not None:
+            import torch.distributed as dist
+            self._dist = dist
         if self.ring is not None:
             from .ssd_uploader import _SsdUploader
             self.uploader = _SsdUploader(self)
@@ -177,9 +192,20 @@ class _StreamState:
             cs.wait_event(self.computed_events[slot_idx])
             if prof is not None:
                 prof.record(s_idx, "dma0", cs)
-            self.slot_flats[slot_idx].copy_(self.host_flats[s_idx], non_blocking=True)
+            if self.gather is None:
+                self.slot_flats[slot_idx].copy_(self.host_flats[s_idx], non_blocking=True)
+            else:
+                mine = self.slot_flats[slot_idx][self.shard_lo:self.shard_lo + self.shard_bytes]
+                mine.copy_(self.host_flats[s_idx], non_blocking=True)
             if prof is not None:
                 prof.record(s_idx, "dma1", cs)
+            if self.gather is not None:
+                # the other ranks' ranges over NVLink, in place (NCCL runs it on its own stream after this one's
+                # copy; the wait puts the copy stream behind it without blocking the host)
+                group = self.gather[0]
+                work = self._dist.all_gather_into_tensor(self.slot_flats[slot_idx], mine, group=group,
+                                                         async_op=True)
+                work.wait()
             self.transferred_events[s_idx].record(cs)
         ds.wait_event(self.transferred_events[s_idx])
         self.dequant_slot(slot_idx, ds)
@@ -265,6 +291,9 @@ class _StreamState:
             self.uploader.drain()
             self.uploader.close()
             self.uploader = None
+        if self.gather is not None:
+            import torch.distributed as dist
+            self._dist = dist
         if self.ring is not None:
             self.ring.close()
             self.ring = None

@@ -1,0 +1,66 @@
+"""torchrun worker of the sequence-parallel GPU test (tests/test_tp_gpu.py): the streamed stack with parallel="sp"
+-- each rank streams its byte range of every block, the ranges are all-gathered into whole blocks, and each rank runs
+them on its token rows -- against the same stack on one GPU (rank 0, broadcast), once with the batch split by sample
+(no key / value exchange) and once with one sample split over the ranks (keys and values gathered). Every rank checks
+its own rows with the tensor-parallel test's bounds (0.05 of the row's RMS per element, 1e-2 relative L2 on the
+update). Exit code 0 = every rank within them."""
+
+import datetime
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def main():
+    import importlib
+    cb = importlib.import_module("comfyui-weightferry_b200.streaming.cosmos_block")
+    stk = importlib.import_module("comfyui-weightferry_b200.streaming.stack")
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    cfg = cb.CosmosConfig(hidden=1024, heads=8, head_dim=128, mlp=4096, ctx_dim=256, lora=64)
+    ok = torch.ones(1, device="cuda")
+    for batch in (2, 1):
+        T, H, W = 1, 16, 16
+        tokens = T * H * W
+        g = torch.Generator(device="cuda").manual_seed(19 + batch)
+        x = torch.randn((batch * tokens, cfg.hidden), device="cuda", generator=g).to(torch.bfloat16)
+        emb = (torch.randn((batch, cfg.hidden), device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+        lora = (torch.randn((batch, 3 * cfg.hidden), device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+        ctx = torch.randn((batch, 64, cfg.ctx_dim), device="cuda", generator=g).to(torch.bfloat16)
+        rope = cb.rope3d_table(T, H, W, device="cuda")
+        sp = cb.SP(batch, tokens)
+        rows = batch * tokens // world
+        stack = stk.StreamedStack(cfg, 3, "cuda", seed=81, num_slots=2, parallel="sp", sp=sp)
+        out = stack.forward(x[rank * rows:(rank + 1) * rows].contiguous(), emb, ctx, rope, batch, tokens, lora)
+        again = stack.forward(x[rank * rows:(rank + 1) * rows].contiguous(), emb, ctx, rope, batch, tokens, lora)
+        ref = torch.empty((batch * tokens, cfg.hidden), dtype=torch.bfloat16, device="cuda")
+        if rank == 0:
+            single = stk.StreamedStack(cfg, 3, "cuda", cb.TP(single=True), seed=81, num_slots=2)
+            ref.copy_(single.forward(x, emb, ctx, rope, batch, tokens, lora))
+            single.close()
+        dist.broadcast(ref, 0)
+        mine = slice(rank * rows, (rank + 1) * rows)
+        y, yr, x0 = out.double(), ref[mine].double(), x[mine].double()
+        rel = ((y - yr).abs() / yr.pow(2).mean(dim=1, keepdim=True).sqrt()).max().item()
+        upd = (((y - x0) - (yr - x0)).norm() / (yr - x0).norm()).item()
+        exact = torch.equal(out, ref[mine])
+        print(f"rank {rank}: sp{world} batch {batch} (kv ranks {sp.kv_ranks}) vs single GPU: max |d| / row rms "
+              f"{rel:.4f}, update rel-L2 {upd:.3e}, bit-identical {exact}, second forward equal "
+              f"{torch.equal(out, again)}", flush=True)
+        if not (rel <= 0.05 and upd <= 1e-2 and torch.isfinite(y).all() and torch.equal(out, again)):
+            ok.zero_()
+        stack.close()
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if ok.item() == 1 else 1)
+
+
+if __name__ == "__main__":
+    main()

@@ -86,3 +86,53 @@ def test_tp_plumbing_and_sweep_sharding_gloo():
         assert ok, f"rank {rank}: TP all-gather / reduce-scatter mismatch"
         assert partition, "bin-packing is not a partition of the tensor table"
         assert balanced
+
+
+def _sp_worker(rank, world, port, q):
+    import datetime
+    import importlib
+
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, REPO)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        cb = importlib.import_module("comfyui-weightferry_b200.streaming.cosmos_block")
+        ok = True
+        # two samples over two ranks: one sample each, nothing exchanged
+        sp = cb.SP(2, 8)
+        ok = ok and sp.rows == 8 and sp.kv_ranks == 1 and sp.kv_group is None
+        k = torch.full((1, 8, 2, 4), float(rank))
+        ok = ok and sp.gather_kv(k, k)[0] is k
+        # one sample over two ranks: keys / values gathered in token order
+        sp = cb.SP(1, 8)
+        ok = ok and sp.rows == 4 and sp.kv_ranks == 2
+        k = torch.arange(4 * 2 * 4, dtype=torch.float32).view(1, 4, 2, 4) + 100 * rank
+        v = -k
+        ka, va = sp.gather_kv(k, v)
+        want = torch.cat([torch.arange(32, dtype=torch.float32).view(1, 4, 2, 4) + 100 * r for r in range(world)], 1)
+        ok = ok and torch.equal(ka, want) and torch.equal(va, -want)
+        try:  # 6 rows per rank: neither whole samples of 4 tokens nor a divisor of one
+            cb.SP(3, 4)
+            ok = False
+        except ValueError:
+            pass
+        q.put((rank, bool(ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sp_rows_and_kv_gather_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    world, port = 2, 29612
+    procs = [ctx.Process(target=_sp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok in results:
+        assert ok, f"rank {rank}: SP rows / key-value gather wrong"
