@@ -614,8 +614,8 @@ def h2d_probe(torch, dev, nbytes=1 << 30, reps=5):
     return best
 
 
-_KERNEL_KINDS = (("nccl", ("nccl",)), ("gemm", ("gemm", "cutlass", "xmma", "nvjet", "sm100", "cublas")),
-                 ("attention", ("flash", "fmha", "attention", "sdpa", "softmax")),
+_KERNEL_KINDS = (("nccl", ("nccl",)), ("attention", ("flash", "fmha", "attention", "sdpa", "softmax", "cudnn")),
+                 ("gemm", ("gemm", "cutlass", "xmma", "nvjet", "sm100", "cublas")),
                  ("dequant", ("dequant_kernel",)), ("prologue", ("ln_modulate", "rms_rope", "rms128", "gated_residual")))
 
 

@@ -1287,10 +1287,14 @@ bool rope_v2() {
     return v2;
 }
 
+// rows per half-warp in flight in rms_rope_v2_kernel (WEIGHTFERRY_ROPE_ROWS 2 / 4 / 8; measured at configs[3], q and
+// k of (2, 4096, 16, 128): 2 rows 29.0 us, 4 rows 27.4 us)
 int rope_rows() {
     static const int r = [] {
         const char *v = getenv("WEIGHTFERRY_ROPE_ROWS");
-        return (v != nullptr && v[0] == '4') ? 4 : 2;
+        if (v != nullptr && v[0] == '2') return 2;
+        if (v != nullptr && v[0] == '8') return 8;
+        return 4;
     }();
     return r;
 }
@@ -1331,11 +1335,12 @@ int rope_launch(const RopeTensors &t, int n_tensors, const float *freqs, int64_t
                   tk = static_cast<int>(tokens);
         cudaError_t e;
 #define WF_RV2(WD, F)                                                                                             \
-    e = rope_rows() == 4                                                                                        \
-            ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 4>, t, ni, nt, hd, tk, freqs, eps,              \
-                                 f_stride_token, f_stride_d, f_stride_i, f_stride_j)                            \
-            : cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 2>, t, ni, nt, hd, tk, freqs, eps,              \
-                                 f_stride_token, f_stride_d, f_stride_i, f_stride_j)
+    e = rope_rows() == 4   ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 4>, t, ni, nt, hd, tk, freqs, eps, \
+                                                f_stride_token, f_stride_d, f_stride_i, f_stride_j)             \
+        : rope_rows() == 8 ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 8>, t, ni, nt, hd, tk, freqs, eps, \
+                                                f_stride_token, f_stride_d, f_stride_i, f_stride_j)             \
+                           : cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 2>, t, ni, nt, hd, tk, freqs, eps, \
+                                                f_stride_token, f_stride_d, f_stride_i, f_stride_j)
         if (w_dtype == WF_BF16) {
             if (f4) WF_RV2(WF_BF16, true); else WF_RV2(WF_BF16, false);
         } else if (w_dtype == WF_F16) {
