@@ -137,6 +137,8 @@ class _StreamState:
         if self.gather is not None:
             import torch.distributed as dist
             self._dist = dist
+            with torch.cuda.device(self.device):
+                self.gather_stream = torch.cuda.Stream(device=self.device)
         if self.ring is not None:
             from .ssd_uploader import _SsdUploader
             self.uploader = _SsdUploader(self)
@@ -199,14 +201,18 @@ class _StreamState:
                 mine.copy_(self.host_flats[s_idx], non_blocking=True)
             if prof is not None:
                 prof.record(s_idx, "dma1", cs)
-            if self.gather is not None:
-                # the other ranks' ranges over NVLink, in place (NCCL runs it on its own stream after this one's
-                # copy; the wait puts the copy stream behind it without blocking the host)
-                group = self.gather[0]
-                work = self._dist.all_gather_into_tensor(self.slot_flats[slot_idx], mine, group=group,
+            self.transferred_events[s_idx].record(cs)
+        if self.gather is not None:
+            # the other ranks' ranges over NVLink, in place, on a stream of its own so that the copy stream goes on
+            # with the next block's bytes; NCCL runs it after this block's copy, the wait puts the gather stream
+            # behind it without blocking the host, and the dequantisation waits for the gather stream
+            gs = self.gather_stream
+            with torch.cuda.stream(gs):
+                gs.wait_event(self.transferred_events[s_idx])
+                work = self._dist.all_gather_into_tensor(self.slot_flats[slot_idx], mine, group=self.gather[0],
                                                          async_op=True)
                 work.wait()
-            self.transferred_events[s_idx].record(cs)
+                self.transferred_events[s_idx].record(gs)
         ds.wait_event(self.transferred_events[s_idx])
         self.dequant_slot(slot_idx, ds)
         if prof is not None:
@@ -294,10 +300,14 @@ class _StreamState:
         if self.gather is not None:
             import torch.distributed as dist
             self._dist = dist
+            with torch.cuda.device(self.device):
+                self.gather_stream = torch.cuda.Stream(device=self.device)
         if self.ring is not None:
             self.ring.close()
             self.ring = None
         self.copy_stream.synchronize()
+        if self.gather is not None:
+            self.gather_stream.synchronize()
         self.dequant_stream.synchronize()
 
     def profile_summary(self):
