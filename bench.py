@@ -596,14 +596,17 @@ def cpu_baseline_w8a8(seconds=10.0):
     return ops / el / 1e12, torch.get_num_threads(), f"{reps} x 64 rows of configs[2] in {el:.1f} s"
 
 
-def h2d_probe(torch, dev, nbytes=1 << 30, reps=5):
-    """Pinned -> device cudaMemcpyAsync of 1 GiB, best of `reps` (the measured PCIe H2D bandwidth)."""
+def h2d_probe(torch, dev, nbytes=1 << 30, reps=5, dist=None):
+    """Pinned -> device cudaMemcpyAsync of 1 GiB, best of `reps` (the measured PCIe H2D bandwidth). Under several
+    ranks every rank copies at the same time (a barrier before each copy), so the figure is this rank's share of
+    what the host delivers to all its GPUs at once -- the bandwidth the streamed stack's ranks actually share."""
     host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
     dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     dst.copy_(host, non_blocking=True)
     torch.cuda.synchronize()
     best = 0.0
     for _ in range(reps):
+        barrier(torch, dist)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         dst.copy_(host, non_blocking=True)
@@ -672,7 +675,7 @@ def stack_measure(torch, world, rank, dist, blocks, steps, warmup, slots=3, e2e=
     tokens = T * H * W
     # each rank's pinned weights on its GPU's NUMA node (first touch after binding): no cross-socket DMA
     numa_cpus = _pkg("core.tiers.pinned").bind_to_gpu_numa(dev.index) if world > 1 else None
-    probe = h2d_probe(torch, dev)
+    probe = h2d_probe(torch, dev, dist=dist)
     t_build = time.perf_counter()
     sp = cb.SP(batch, tokens) if parallel == "sp" else None
     stack = stk.StreamedStack(cfg, blocks, dev, tp, seed=20261201 + 4, num_slots=slots, parallel=parallel, sp=sp)
@@ -756,6 +759,7 @@ def stack_subrecord(r, world, steps):
         "higher_is_better": False, "scaling": "strong", "steps": steps, "n_gpus": world,
         "parallelism": _parallel_text(r["parallel"], world), "blocks": r["blocks"],
         "h2d_gbs_per_rank": round(r["h2d_rate"], 2), "h2d_probe_gbs_per_rank": round(r["probe"], 2),
+        "h2d_probe_note": "1 GiB pinned copies on every rank at once: this rank's share of the host's bandwidth",
         "h2d_frac_of_probe": round(r["h2d_rate"] / r["probe"], 4),
         "h2d_bytes_per_block_per_rank": r["h2d_rank"] // r["blocks"],
         "dequant_on_arrival_ms_per_block_per_rank": round(summ["dequant_lora_ms"] / max(1, summ["streamed_blocks"]),
@@ -832,7 +836,8 @@ def finish_stack(torch, args, world, rank, dist, r):
                        "kernel_ms_per_rank_one_forward": r.get("breakdown")},
             "roofline": {"bound": "pcie_h2d", "achieved": round(r["h2d_rate"], 2), "peak": round(r["probe"], 2),
                          "unit": "GB/s per rank", "frac": round(frac, 4), "traffic": None,
-                         "peak_source": "pinned 1 GiB cudaMemcpyAsync H2D measured in this run",
+                         "peak_source": "pinned 1 GiB cudaMemcpyAsync H2D measured in this run, every rank copying "
+                                        "at once",
                          "tflops_per_gpu": round(r["flops"] / world / (r["ms"] / 1e3) / 1e12, 1)},
             "cpu_baseline": cpu, "e2e": r["e2e"], "gpu_launches": None, "clocks": r["clk"]}), flush=True)
     if dist is not None:
