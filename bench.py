@@ -979,68 +979,70 @@ def finish_prologue(torch, args, world, rank, dist, r):
 
 
 def run_single_weight(torch, args, world, rank, dist, which):
-    """configs[0] (Q8_0 5120x5120) or configs[1]'s weight (Q4_K 5120x13824): one launch per step, L2 flushed."""
-    gd = _pkg("enhancers.gguf_dequant")
+    """configs[0] (Q8_0 5120x5120) or configs[1]'s weight (Q4_K 5120x13824): one launch per weight, as a GGUF layer
+    dequantises its weight on every use. Timed as a run of launches over rotating sets of weights whose bytes exceed
+    L2 five times over (so each launch reads from HBM and no flush is needed), between two CUDA events."""
     ext = _pkg("_ext")
     dev = torch.device("cuda", torch.cuda.current_device())
     gen = torch.Generator(device=dev)
     if which == "q8":
-        shape, qt, ts, vpb = (5120, 5120), 8, Q8_TS, 32
+        shape, qt = (5120, 5120), 8
         gen.manual_seed(20261201 + 0 + rank)
-        src = fill_q8(torch, shape[0] * shape[1] // 32, dev, gen)
+        fill = lambda: fill_q8(torch, shape[0] * shape[1] // 32, dev, gen)  # noqa: E731
     else:
-        shape, qt, ts, vpb = (5120, 13824), 12, Q4K_TS, 256
+        shape, qt = (5120, 13824), 12
         gen.manual_seed(20261201 + 1 + rank)
-        src = fill_q4k(torch, shape[0] * shape[1] // 256, dev, gen)
+        fill = lambda: fill_q4k(torch, shape[0] * shape[1] // 256, dev, gen)  # noqa: E731
     n = shape[0] * shape[1]
-    dst = torch.empty(shape, dtype=torch.bfloat16, device=dev)
-    flush = L2Flush(torch, dev)
+    per_set = fill().numel() + 2 * n
+    n_sets = max(2, -(-640 * 1024 * 1024 // per_set))
+    sets = [(fill(), torch.empty(shape, dtype=torch.bfloat16, device=dev)) for _ in range(n_sets)]
     lib = ext.lib()
     stream = torch.cuda.current_stream(dev)
 
-    def step():
+    def launch(i):
+        src, dst = sets[i % n_sets]
         rc = lib.wf_dequant_gguf(src.data_ptr(), src.numel(), dst.data_ptr(), n, qt, 0, 1, stream.cuda_stream)
         if rc:
             ext.check(rc, "wf_dequant_gguf")
 
-    for _ in range(args.warmup):
-        flush()
-        step()
+    def probe(i):  # the same byte counts through a no-arithmetic streaming kernel
+        src, dst = sets[i % n_sets]
+        ext.check(lib.wf_hbm_probe(src.data_ptr(), src.numel() // 16 * 16, dst.data_ptr(), 2 * n // 16 * 16,
+                                   stream.cuda_stream), "wf_hbm_probe")
+
+    def timed(fn, count):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(count):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / count
+
+    count = n_sets * max(1, args.steps // 2)
+    for i in range(max(args.warmup, 1) * n_sets):
+        launch(i)
     barrier(torch, dist)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with ClockSampler(torch.cuda.current_device()) as clk:
         barrier(torch, dist)
-        for s in range(args.steps):
-            flush()
-            ev[s][0].record(stream)
-            step()
-            ev[s][1].record(stream)
+        kern_ms = timed(launch, count)
         barrier(torch, dist)
-    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    probe_ms = timed(probe, count)
     ms = max_over_ranks(torch, dist, kern_ms)
+    src0 = sets[0][0]
     out_bytes = n * 2
     value = sum_over_ranks(torch, dist, out_bytes / (ms / 1e3) / 1e9)
-    # the same read / write byte counts through wf_hbm_probe after the same flush: what a no-arithmetic kernel of this
-    # shape reaches for a launch this short
-    pin, pout = src.numel() // 16 * 16, out_bytes // 16 * 16
-    pev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for i in range(args.steps + 2):
-        flush()
-        if i >= 2:
-            pev[i - 2][0].record(stream)
-        ext.check(lib.wf_hbm_probe(src.data_ptr(), pin, dst.data_ptr(), pout, stream.cuda_stream), "wf_hbm_probe")
-        if i >= 2:
-            pev[i - 2][1].record(stream)
-    torch.cuda.synchronize()
-    probe_ms = statistics.mean(a.elapsed_time(b) for a, b in pev)
-    mix = (pin + pout) / (probe_ms / 1e3) / 1e9
+    mix = (src0.numel() // 16 * 16 + out_bytes // 16 * 16) / (probe_ms / 1e3) / 1e9
     return {
-        "value": value, "ms_per_step": ms, "kern_ms": kern_ms, "alg_bytes_per_launch": src.numel() + out_bytes,
-        "clk": clk.summary(), "e2e": None, "gpu_launches": int(sum_over_ranks(torch, dist, args.steps)),
+        "value": value, "ms_per_step": ms, "kern_ms": kern_ms, "alg_bytes_per_launch": src0.numel() + out_bytes,
+        "clk": clk.summary(), "e2e": None, "gpu_launches": int(sum_over_ranks(torch, dist, count)),
         "mix_gbs": mix,
         "config": {"workload": f"GGUF {'Q8_0' if qt == 8 else 'Q4_K'} {shape[0]}x{shape[1]} -> bf16 (one weight)",
-                   "mid_dtype": "f16", "l2": L2_NOTE,
-                   "timing": "sum of per-launch CUDA-event durations"},
+                   "mid_dtype": "f16",
+                   "l2": f"inputs larger than L2: a run of {count} launches over {n_sets} rotating weights "
+                         f"({n_sets * per_set / 1e9:.2f} GB); no flush",
+                   "timing": "CUDA events around the run / launches (a step = one launch)"},
     }
 
 
@@ -1347,7 +1349,7 @@ def main():
             # plain streaming kernel with the same byte counts (wf_hbm_probe) is the ceiling it is measured against too
             line["roofline"]["mix_ceiling"] = {"gbs": round(r["mix_gbs"], 1), "frac": round(achieved / r["mix_gbs"], 4),
                                                "probe": "wf_hbm_probe over the same in / out byte counts"
-                                                        + (" after the same L2 flush" if args.workload != "sweep"
+                                                        + (" over the same rotation" if args.workload != "sweep"
                                                            else "")}
         print(json.dumps(line), flush=True)
     if dist is not None:

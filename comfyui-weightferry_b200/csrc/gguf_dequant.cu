@@ -563,6 +563,10 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
     const int64_t n_chunks = total_chunks(p);
     int64_t c = blockIdx.x;
     if (c >= n_chunks) return;
+    // launched as a programmatic dependent: the previous kernel of the stream has finished and its writes are
+    // visible once this returns (at once for a plain launch). No early trigger of this grid's own dependents: it runs
+    // many waves, whose CTAs they would compete with.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // LORA && ALIGNED: the chunks' differences ride in the same double buffer, after the packed bytes
     constexpr bool kStageDiff = LORA && ALIGNED;
     float *sdiff = reinterpret_cast<float *>(smem + 2 * kStride);
@@ -622,8 +626,18 @@ int launch(const P &p, int64_t n_chunks, cudaStream_t stream) {
     const int64_t resident = static_cast<int64_t>(occ[dev].load(std::memory_order_acquire)) * device_sm_count();
     const int64_t grid =
         std::min<int64_t>(n_chunks, std::max<int64_t>(resident, (n_chunks + kChunksPerCta - 1) / kChunksPerCta));
-    kern<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);
-    return static_cast<int>(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 template <int QT>
