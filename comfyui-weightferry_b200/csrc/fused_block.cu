@@ -581,8 +581,8 @@ __device__ __forceinline__ float2 load_w2(const void *w, int i) {  // weights i,
 
 constexpr int kRope2Warps = 8;  // warps (items) per CTA
 
-template <int WDT, bool F4, int R>
-__global__ void __launch_bounds__(kRope2Warps * 32) rms_rope_v2_kernel(const __grid_constant__ RopeTensors t,
+template <int WDT, bool F4, int R, int MINB = 1>
+__global__ void __launch_bounds__(kRope2Warps * 32, MINB) rms_rope_v2_kernel(const __grid_constant__ RopeTensors t,
                                                                        int n_items, int n_tok, int heads, int tokens,
                                                                        const float *__restrict__ f, float eps,
                                                                        int64_t s_tok, int64_t s_d, int64_t s_i,
@@ -1294,6 +1294,7 @@ int rope_rows() {
         const char *v = getenv("WEIGHTFERRY_ROPE_ROWS");
         if (v != nullptr && v[0] == '2') return 2;
         if (v != nullptr && v[0] == '8') return 8;
+        if (v != nullptr && v[0] == '5') return 5;  // 4 rows, registers bounded for 4 CTAs per SM
         return 4;
     }();
     return r;
@@ -1335,7 +1336,9 @@ int rope_launch(const RopeTensors &t, int n_tensors, const float *freqs, int64_t
                   tk = static_cast<int>(tokens);
         cudaError_t e;
 #define WF_RV2(WD, F)                                                                                             \
-    e = rope_rows() == 4   ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 4>, t, ni, nt, hd, tk, freqs, eps, \
+    e = rope_rows() == 5   ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 4, 4>, t, ni, nt, hd, tk, freqs, eps, \
+                                                f_stride_token, f_stride_d, f_stride_i, f_stride_j)             \
+        : rope_rows() == 4 ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 4>, t, ni, nt, hd, tk, freqs, eps, \
                                                 f_stride_token, f_stride_d, f_stride_i, f_stride_j)             \
         : rope_rows() == 8 ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 8>, t, ni, nt, hd, tk, freqs, eps, \
                                                 f_stride_token, f_stride_d, f_stride_i, f_stride_j)             \

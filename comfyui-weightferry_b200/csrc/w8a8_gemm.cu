@@ -201,6 +201,23 @@ __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// Output tile `tile` -> (tile row, tile column). group_m == 0: tiles walk down the M direction first (column by
+// column); group_m > 0: bands of group_m tile rows, each walked column by column, so that the tiles in flight at once
+// share fewer operand rows and columns.
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int group_m, int &mi, int &ni) {
+    if (group_m <= 0) {
+        mi = tile % tiles_m;
+        ni = tile / tiles_m;
+        return;
+    }
+    const int band = tile / (group_m * tiles_n);
+    const int first = band * group_m;
+    const int rows = min(tiles_m - first, group_m);
+    const int r = tile - band * group_m * tiles_n;
+    mi = first + r % rows;
+    ni = r / rows;
+}
+
 // w_s of 32 output columns starting at col0 (a multiple of 32; N is a multiple of 8, so each group of 8 columns is
 // wholly inside or wholly outside [0, N)); same address in every lane
 struct Ws32 {
@@ -362,7 +379,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                  const __grid_constant__ CUtensorMap tma_y, const float *__restrict__ xs,
                  const float *__restrict__ ws, int32_t *__restrict__ acc_out, ResidualArgs res, int M, int N,
-                 int K) {
+                 int K, int group_m) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned ring (the 128-byte swizzle pattern repeats every 8 rows of 128 bytes), then the epilogue
     // warps' output chunks (4 KB per warp), then the barriers
@@ -418,7 +435,9 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
             for (int s = 0; s < STAGES; ++s) pending[s] = false, issued_phase[s] = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-                const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+                int mi, ni;
+                tile_coords(tile, tiles_m, tiles_n, group_m, mi, ni);
+                const int m0 = mi * BM, n0 = ni * BN;
                 for (int kb = 0; kb < kb_count; ++kb) {
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, abort_flag, 1)) { ok = false; break; }
                     const uint32_t fb = full0 + 8 * stage;
@@ -485,7 +504,9 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         int acc = 0;
         uint32_t acc_phase = 0, chunk = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-            const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+            int mi, ni;
+            tile_coords(tile, tiles_m, tiles_n, group_m, mi, ni);
+            const int m0 = mi * BM, n0 = ni * BN;
             const int row0 = m0 + quarter * 32;
             const float xsr = row0 + lane < M ? __ldg(xs + row0 + lane) : 0.f;
             if (RES) prefetch_res_l2(res, row0 + lane, n0 + half * 128, M, N);
@@ -565,7 +586,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_y, const float *__restrict__ xs,
                      const float *__restrict__ ws, int32_t *__restrict__ acc_out, ResidualArgs res, int M, int N,
-                     int K) {
+                     int K, int group_m) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *out_chunks = ring + S2 * STAGE2;
@@ -622,8 +643,10 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
             int issued = 0;
             bool ok = true;
             for (int tile = cluster_id; tile < n_tiles && ok; tile += n_clusters) {
-                const int m0 = (tile % tiles_m) * 256 + static_cast<int>(rank) * 128;
-                const int n0 = (tile / tiles_m) * 256 + static_cast<int>(rank) * 128;
+                int mi, ni;
+                tile_coords(tile, tiles_m, tiles_n, group_m, mi, ni);
+                const int m0 = mi * 256 + static_cast<int>(rank) * 128;
+                const int n0 = ni * 256 + static_cast<int>(rank) * 128;
                 for (int kb = 0; kb < kb_count; ++kb) {
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, abort_flag, 1)) { ok = false; break; }
                     const uint32_t leader_full = (full0 + 8 * stage) & kPeerBitMask;
@@ -691,7 +714,9 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
         int acc = 0;
         uint32_t acc_phase = 0, chunk = 0;
         for (int tile = cluster_id; tile < n_tiles; tile += n_clusters) {
-            const int m0 = (tile % tiles_m) * 256 + static_cast<int>(rank) * 128, n0 = (tile / tiles_m) * 256;
+            int mi, ni;
+            tile_coords(tile, tiles_m, tiles_n, group_m, mi, ni);
+            const int m0 = mi * 256 + static_cast<int>(rank) * 128, n0 = ni * 256;
             const int row0 = m0 + quarter * 32;
             const float xsr = row0 + lane < M ? __ldg(xs + row0 + lane) : 0.f;
             if (RES) prefetch_res_l2(res, row0 + lane, n0 + half * 128, M, N);
@@ -781,6 +806,15 @@ cudaError_t launch_dependent(void (*kern)(KArgs...), int grid, int threads, size
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// WEIGHTFERRY_W8A8_GROUP_M: tile rows per band of the tile order (0 or unset: down M first)
+int tile_group_m() {
+    static const int g = [] {
+        const char *v = getenv("WEIGHTFERRY_W8A8_GROUP_M");
+        return v != nullptr ? std::max(0, atoi(v)) : 0;
+    }();
+    return g;
+}
+
 bool use_pair_kernel() {
     static const bool pair = [] {
         const char *v = getenv("WEIGHTFERRY_W8A8_1SM");
@@ -852,7 +886,7 @@ int launch(const CUtensorMap &ma, const void *wq, const CUtensorMap &my, const f
             2 * static_cast<int>(std::min<int64_t>(tiles, clusters[dev].load(std::memory_order_acquire)));
         const cudaError_t e = launch_dependent(w8a8_gemm_2sm_kernel<RES>, grid, THREADS, SMEM2_BYTES, stream, ma, mb2,
                                                my, xs, ws, acc_out, res, static_cast<int>(M), static_cast<int>(N),
-                                               static_cast<int>(K));
+                                               static_cast<int>(K), tile_group_m());
         return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
     }
     CUtensorMap mb;
@@ -867,7 +901,8 @@ int launch(const CUtensorMap &ma, const void *wq, const CUtensorMap &my, const f
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, device_sm_count()));
     const cudaError_t e = launch_dependent(w8a8_gemm_kernel<RES>, grid, THREADS, SMEM_BYTES, stream, ma, mb, my, xs, ws,
-                                           acc_out, res, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+                                           acc_out, res, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                                           tile_group_m());
     return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
