@@ -35,6 +35,8 @@ the fp8 storage host format -- are accepted and logged as not used here. residen
 resident blocks' GGUF weights once and binds them for each whole forward. "Single Buffer (Synchronous)" issues each block's transfer when the block starts (no look-ahead). A VRAM budget
 (vram_budget_gb or WEIGHTFERRY_VRAM_BUDGET_GB) bounds what the automatic resident-block choice counts as usable."""
 
+import weakref
+
 import torch
 
 from ..core import env as _env
@@ -206,6 +208,21 @@ class _NodeState:
         self.ring = None
         self.captures = 0
         self.bound = set()  # streamed blocks whose parameters are bound to their slot (between pre and post hook)
+
+    def start(self):
+        """Capture the streamed blocks, build the resident ones and hook the model (any earlier configuration of the
+        model is torn down first)."""
+        teardown(self.dit)
+        self.capture()
+        self.build_resident()
+        self.install_hooks()
+        setattr(self.dit, _STATE_ATTR, self)
+        n_deq = sum(1 for _p, _n, d, _r, _t in self.entries[0] if d)
+        log_info(f"DiT Layer Streaming: {len(self.stream_idx)} streaming blocks, pin_memory={self.pin_memory}, "
+                 f"double_buffer={self.lookahead}, slots={self.ring.num_slots}; per block "
+                 f"{self.layout.flat_bytes / 1024 ** 2:.1f} MB host, {n_deq} GGUF weights dequantised on arrival"
+                 + (f"; self-managed resident blocks: {len(self.res_entries)} GGUF weights dequantised once."
+                    if self.self_resident else "."))
 
     # ------------------------------------------------------------------------------------------------ capture
     def capture(self):
@@ -435,6 +452,57 @@ class _NodeState:
             setattr(self.dit, _STATE_ATTR, None)
 
 
+_WRAPPER_KEY = "weightferry_b200_streaming"
+
+
+def _patcher_extension(patcher):
+    """ComfyUI's patcher_extension module when ``patcher`` is a ComfyUI ModelPatcher that takes callbacks (the
+    capture then waits for ComfyUI's model load), else None (the capture happens now)."""
+    if not (hasattr(patcher, "add_callback") and isinstance(getattr(patcher, "model_options", None), dict)):
+        return None
+    try:
+        import comfy.patcher_extension as ext
+    except ImportError:
+        return None
+    return ext
+
+
+def _hook_patcher(patcher, dit, st, ext):
+    """The reference's ModelPatcher integration (streaming/dit_node.py:298-490): the capture runs in ComfyUI's ON_LOAD
+    callback, when the model's weights are on the GPU with their LoRA / quantisation patches applied; ON_DETACH
+    tears it down; a DIFFUSION_MODEL wrapper captures lazily when ComfyUI ran a forward without an ON_LOAD for this
+    configuration (a switch back to a clone whose weights were already in place skips the load). The per-forward
+    bracket itself is the diffusion model's forward hooks (install_hooks)."""
+    def on_load(mp, device_to=None, lowvram_model_memory=0, force_patch_weights=False, full_load=False):
+        target = torch.device(device_to if device_to is not None else getattr(mp, "load_device", st.device))
+        if target.type != "cuda":
+            return
+        st.start()
+
+    def on_detach(mp, unpatch_all=True, *args, **kwargs):
+        if getattr(dit, _STATE_ATTR, None) is st:
+            teardown(dit)
+
+    # the wrapper lives in the patcher's model_options: a weak reference avoids a patcher -> options -> patcher cycle
+    patcher_ref = weakref.ref(patcher)
+
+    def wrapper(executor, *args, **kwargs):
+        if getattr(dit, _STATE_ATTR, None) is not st:
+            mp = patcher_ref()
+            if mp is not None:
+                on_load(mp, getattr(mp, "load_device", None))
+                if getattr(dit, _STATE_ATTR, None) is st:
+                    log_info("DiT Layer Streaming: ON_LOAD was skipped by ComfyUI; captured at the forward.")
+        return executor(*args, **kwargs)
+
+    patcher.add_callback(ext.CallbacksMP.ON_LOAD, on_load)
+    patcher.add_callback(ext.CallbacksMP.ON_DETACH, on_detach)
+    wrappers = patcher.model_options.setdefault("transformer_options", {}).setdefault("wrappers", {})
+    wrappers.setdefault(ext.WrappersMP.DIFFUSION_MODEL, {}).pop(_WRAPPER_KEY, None)
+    ext.add_wrapper_with_key(ext.WrappersMP.DIFFUSION_MODEL, _WRAPPER_KEY, wrapper, patcher.model_options,
+                             is_model_options=True)
+
+
 def teardown(dit):
     """Undo apply_streaming on a diffusion model (the reference's streaming/teardown.py for one model)."""
     st = getattr(dit, _STATE_ATTR, None)
@@ -532,16 +600,13 @@ class WeightFerryDiT:
         st = _NodeState(object(), dit, stream_idx, device, pin_memory, num_slots, is_double, compute_dtype,
                         tiering_auto=tiering_auto, ram_budget_bytes=ram_budget_bytes,
                         self_resident=resident_mode == RESIDENT_MODE_SELF)
-        st.capture()
-        st.build_resident()
-        st.install_hooks()
-        setattr(dit, _STATE_ATTR, st)
-        n_deq = sum(1 for _p, _n, d, _r, _t in st.entries[0] if d)
-        log_info(f"DiT Layer Streaming: {resident_k}/{num_blocks} resident, {len(stream_idx)} streaming blocks, "
-                 f"pin_memory={pin_memory}, double_buffer={is_double}, slots={st.ring.num_slots}; per block "
-                 f"{st.layout.flat_bytes / 1024 ** 2:.1f} MB host, {n_deq} GGUF weights dequantised on arrival"
-                 + (f"; self-managed resident blocks: {len(st.res_entries)} GGUF weights dequantised once."
-                    if st.self_resident else "."))
+        ext = _patcher_extension(patcher)
+        if ext is not None:
+            _hook_patcher(patcher, dit, st, ext)
+            log_info(f"DiT Layer Streaming: {resident_k}/{num_blocks} resident, {len(stream_idx)} streaming blocks; "
+                     "hooked to the ModelPatcher, the blocks are captured when ComfyUI loads the model.")
+            return (patcher,)
+        st.start()
         return (patcher,)
 
     @staticmethod

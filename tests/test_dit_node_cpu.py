@@ -141,3 +141,41 @@ def test_apply_streaming_passthrough():
     assert node.apply_streaming(nob)[0].model.diffusion_model is nob.model.diffusion_model
     none = type("P", (), {"model": None, "clone": lambda self: self})()
     assert node.apply_streaming(none)[0] is none                      # no diffusion model
+
+
+def test_comfyui_patcher_defers_capture_to_on_load():
+    """Given a ComfyUI ModelPatcher, the node registers the ON_LOAD / ON_DETACH callbacks and a DIFFUSION_MODEL
+    wrapper on its clone and captures nothing yet (the capture needs ComfyUI's load); a re-application replaces the
+    wrapper instead of stacking a second one; a detach before any load does nothing."""
+    import sys
+
+    import torch
+
+    import fake_patcher as fp
+    had_comfy = "comfy" in sys.modules
+    fp.register()
+    try:
+        dn = wf("streaming.dit_node")
+
+        class Blk(torch.nn.Module):
+            def __init__(self):
+                super().__init__()
+                self.lin = torch.nn.Linear(8, 8)
+
+        dit = torch.nn.Module()
+        dit.blocks = torch.nn.ModuleList([Blk() for _ in range(3)])
+        base = fp.ModelPatcher(dit, torch.device("cuda", 0), torch.bfloat16)
+        (patcher,) = dn.WeightFerryDiT().apply_streaming(base, resident_blocks=1)
+        assert patcher is not base and not base.callbacks
+        assert len(patcher.callbacks[fp.CallbacksMP.ON_LOAD]) == 1
+        assert len(patcher.callbacks[fp.CallbacksMP.ON_DETACH]) == 1
+        wrappers = patcher.model_options["transformer_options"]["wrappers"][fp.WrappersMP.DIFFUSION_MODEL]
+        assert list(wrappers) == [dn._WRAPPER_KEY] and len(wrappers[dn._WRAPPER_KEY]) == 1
+        assert getattr(dit, "_weightferry_stream_state", None) is None
+        (again,) = dn.WeightFerryDiT().apply_streaming(patcher, resident_blocks=1)
+        w2 = again.model_options["transformer_options"]["wrappers"][fp.WrappersMP.DIFFUSION_MODEL]
+        assert len(w2[dn._WRAPPER_KEY]) == 1
+        again.detach()
+        assert getattr(dit, "_weightferry_stream_state", None) is None
+    finally:
+        fp.unregister(drop_comfy=not had_comfy)

@@ -276,3 +276,39 @@ def test_streamed_gguf_dit_with_ssd_tier(gguf_patch, tmp_path, monkeypatch, n_bl
     assert not os.path.exists(path)
     with torch.inference_mode():
         assert torch.equal(dit(x), ref)
+
+
+def test_comfyui_patcher_captures_on_load(gguf_patch):
+    """With a ComfyUI ModelPatcher (the stand-in of tests/fake_patcher.py) the blocks are captured in the ON_LOAD
+    callback, as the reference does, not when the node runs; ON_DETACH gives the model back; a forward that comes
+    without a load (ComfyUI switching back to a clone whose weights are in place) captures lazily in the wrapper.
+    Every streamed forward equals the un-streamed one bit for bit."""
+    import sys
+    import torch
+    import fake_patcher as fp
+    had_comfy = "comfy" in sys.modules
+    fp.register()
+    try:
+        dn = wf("streaming.dit_node")
+        dit = _dit(torch)
+        x = _x(torch)
+        with torch.inference_mode():
+            ref = dit(x)
+            base = fp.ModelPatcher(dit, torch.device("cuda", 0), torch.bfloat16)
+            (patcher,) = dn.WeightFerryDiT().apply_streaming(base, resident_blocks=1)
+            assert patcher is not base and not base.callbacks
+            assert getattr(dit, "_weightferry_stream_state", None) is None       # nothing captured yet
+            patcher.load()                                                        # ComfyUI loads the model
+            st = dit._weightferry_stream_state
+            assert st is not None and all(not p.is_cuda for i in st.stream_idx for p in dit.blocks[i].parameters())
+            out1 = patcher.apply_model(x)
+            patcher.detach()                                                      # ComfyUI unloads it
+            assert dit._weightferry_stream_state is None and all(p.is_cuda for p in dit.parameters())
+            out2 = patcher.apply_model(x)                                         # no ON_LOAD: captured lazily
+            assert dit._weightferry_stream_state is not None
+            out3 = patcher.apply_model(x)
+            torch.cuda.synchronize()
+        assert torch.equal(out1, ref) and torch.equal(out2, ref) and torch.equal(out3, ref)
+        dn.teardown(dit)
+    finally:
+        fp.unregister(drop_comfy=not had_comfy)
