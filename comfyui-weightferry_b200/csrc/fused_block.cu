@@ -43,6 +43,33 @@ __device__ __forceinline__ float div_full(float a, float b) {
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// Two float32 lanes in one 64-bit register and Blackwell's packed float32 arithmetic on them: each lane is rounded
+// exactly as the scalar instruction rounds it (IEEE round to nearest), so a pair of scalar operations and one packed
+// one give the same bits -- in half the instructions.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+    return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ float f2lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ uint64_t bf_pair(uint32_t w) {  // the two bf16 of a word as float32 lanes (exact)
+    return (static_cast<uint64_t>(w & 0xFFFF0000u) << 32) | (w << 16);
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 // four bf16 (8 bytes) -> float
 __device__ __forceinline__ void unpack4(uint2 w, float v[4]) {
     v[0] = bf_lo(w.x);
@@ -327,13 +354,14 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
         float mu, var;
         ln_stats_n<NV * 4>(v, K, mu, var, red[parity]);  // its two barriers are the row's only ones
         const float rstd = rsqrt_approx(__fadd_rn(var, eps));
+        const uint64_t neg_mu = f2pack(-mu, -mu), rstd2 = f2pack(rstd, rstd);  // x - mu == x + (-mu), exactly
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
             const int64_t c = static_cast<int64_t>(t + 128 * j) * 4;
-            const uint32_t n01 = pack2(__fmul_rn(__fsub_rn(v[4 * j], mu), rstd),
-                                       __fmul_rn(__fsub_rn(v[4 * j + 1], mu), rstd));
-            const uint32_t n23 = pack2(__fmul_rn(__fsub_rn(v[4 * j + 2], mu), rstd),
-                                       __fmul_rn(__fsub_rn(v[4 * j + 3], mu), rstd));
+            const uint64_t a = mul2(add2(f2pack(v[4 * j], v[4 * j + 1]), neg_mu), rstd2);
+            const uint64_t b = mul2(add2(f2pack(v[4 * j + 2], v[4 * j + 3]), neg_mu), rstd2);
+            const uint32_t n01 = pack2(f2lo(a), f2hi(a));
+            const uint32_t n23 = pack2(f2lo(b), f2hi(b));
             *reinterpret_cast<uint2 *>(out + row * K + c) =
                 make_uint2(mod_bf16x2(n01, sraw[j].x, hraw[j].x), mod_bf16x2(n23, sraw[j].y, hraw[j].y));
         }
@@ -581,8 +609,10 @@ __device__ __forceinline__ float2 load_w2(const void *w, int i) {  // weights i,
 
 constexpr int kRope2Warps = 8;  // warps (items) per CTA
 
-template <int WDT, bool F4, int R, int MINB = 1>
-__global__ void __launch_bounds__(kRope2Warps * 32, MINB) rms_rope_v2_kernel(const __grid_constant__ RopeTensors t,
+// Up to 4 rows in flight the kernel fits in 85 registers, which leaves 3 CTAs of 256 threads per SM (the bound is
+// explicit: left to itself ptxas took 89 registers, 2 CTAs per SM, and the launch 15 % longer); 8 rows need more.
+template <int WDT, bool F4, int R>
+__global__ void __launch_bounds__(kRope2Warps * 32, R <= 4 ? 3 : 1) rms_rope_v2_kernel(const __grid_constant__ RopeTensors t,
                                                                        int n_items, int n_tok, int heads, int tokens,
                                                                        const float *__restrict__ f, float eps,
                                                                        int64_t s_tok, int64_t s_d, int64_t s_i,
@@ -608,9 +638,21 @@ __global__ void __launch_bounds__(kRope2Warps * 32, MINB) rms_rope_v2_kernel(con
             rot[m][3] = __ldg(fd + s_i + s_j);
         }
     }
-    float2 w[4];  // weights at 2p + 32 j, 2p + 1 + 32 j
+    uint64_t w[4];  // weights at 2p + 32 j (low lane), 2p + 1 + 32 j (high lane)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) w[j] = load_w2<WDT>(t.w[ti], 2 * p + 32 * j);
+    for (int j = 0; j < 4; ++j) {
+        const float2 wj = load_w2<WDT>(t.w[ti], 2 * p + 32 * j);
+        w[j] = f2pack(wj.x, wj.y);
+    }
+    // the rotations of the pairs (d, d + 64) with d = 2p + 32 j (low lane) and 2p + 1 + 32 j (high lane)
+    uint64_t r00[2], r01[2], r10[2], r11[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        r00[j] = f2pack(rot[2 * j][0], rot[2 * j + 1][0]);
+        r01[j] = f2pack(rot[2 * j][1], rot[2 * j + 1][1]);
+        r10[j] = f2pack(rot[2 * j][2], rot[2 * j + 1][2]);
+        r11[j] = f2pack(rot[2 * j][3], rot[2 * j + 1][3]);
+    }
     const uint32_t *x = reinterpret_cast<const uint32_t *>(t.x[ti]) + static_cast<size_t>(bt) * heads * 64 + p;
     uint32_t *out = reinterpret_cast<uint32_t *>(t.out[ti]) + static_cast<size_t>(bt) * heads * 64 + p;
     // both halves run the same iterations (full-warp shuffles); a half whose row is past the last head computes on
@@ -625,44 +667,44 @@ __global__ void __launch_bounds__(kRope2Warps * 32, MINB) rms_rope_v2_kernel(con
 #pragma unroll
             for (int j = 0; j < 4; ++j) u[r][j] = __ldg(x + rr * 64 + 16 * j);
         }
-        float ev[R], od[R];
+        uint64_t acc[R];  // the reference's lanes 2p (low) and 2p + 1 (high): fma of squares from 0
 #pragma unroll
-        for (int r = 0; r < R; ++r) {  // the reference's lanes 2p (even) and 2p + 1 (odd): fma of squares from 0
-            float a = __fmul_rn(bf_lo(u[r][0]), bf_lo(u[r][0])), b = __fmul_rn(bf_hi(u[r][0]), bf_hi(u[r][0]));
+        for (int r = 0; r < R; ++r) {
+            const uint64_t v0 = bf_pair(u[r][0]);
+            acc[r] = mul2(v0, v0);
 #pragma unroll
             for (int j = 1; j < 4; ++j) {
-                a = __fmaf_rn(bf_lo(u[r][j]), bf_lo(u[r][j]), a);
-                b = __fmaf_rn(bf_hi(u[r][j]), bf_hi(u[r][j]), b);
+                const uint64_t vj = bf_pair(u[r][j]);
+                acc[r] = fma2(vj, vj, acc[r]);
             }
-            ev[r] = a;
-            od[r] = b;
         }
 #pragma unroll
         for (int off = 8; off >= 1; off >>= 1) {
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                ev[r] = __fadd_rn(ev[r], __shfl_xor_sync(0xFFFFFFFFu, ev[r], off));
-                od[r] = __fadd_rn(od[r], __shfl_xor_sync(0xFFFFFFFFu, od[r], off));
+                const float e = __shfl_xor_sync(0xFFFFFFFFu, f2lo(acc[r]), off);
+                const float o = __shfl_xor_sync(0xFFFFFFFFu, f2hi(acc[r]), off);
+                acc[r] = add2(acc[r], f2pack(e, o));
             }
         }
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-            const float rs = rsqrt_approx(__fadd_rn(__fmul_rn(__fadd_rn(ev[r], od[r]), 0.0078125f), eps));
-            float2 n[4];  // R16((x * rs) * w) at 2p + 32 j, 2p + 1 + 32 j
+            const float rs = rsqrt_approx(__fadd_rn(__fmul_rn(__fadd_rn(f2lo(acc[r]), f2hi(acc[r])), 0.0078125f), eps));
+            const uint64_t rs2 = f2pack(rs, rs);
+            uint64_t n[4];  // R16((x * rs) * w) at 2p + 32 j, 2p + 1 + 32 j
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                n[j] = r16x2(__fmul_rn(__fmul_rn(bf_lo(u[r][j]), rs), w[j].x),
-                             __fmul_rn(__fmul_rn(bf_hi(u[r][j]), rs), w[j].y));
+            for (int j = 0; j < 4; ++j) {
+                const uint64_t m = mul2(mul2(bf_pair(u[r][j]), rs2), w[j]);
+                const float2 nn = r16x2(f2lo(m), f2hi(m));
+                n[j] = f2pack(nn.x, nn.y);
+            }
             if (row[r] < heads) {
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {  // pairs (d, d + 64): words j and j + 2
-                    const float *re = rot[2 * j], *ro = rot[2 * j + 1];
-                    out[row[r] * 64 + 16 * j] =
-                        pack2(__fmaf_rn(re[0], n[j].x, __fmul_rn(re[1], n[j + 2].x)),
-                              __fmaf_rn(ro[0], n[j].y, __fmul_rn(ro[1], n[j + 2].y)));
-                    out[row[r] * 64 + 16 * (j + 2)] =
-                        pack2(__fmaf_rn(re[2], n[j].x, __fmul_rn(re[3], n[j + 2].x)),
-                              __fmaf_rn(ro[2], n[j].y, __fmul_rn(ro[3], n[j + 2].y)));
+                    const uint64_t y0 = fma2(r00[j], n[j], mul2(r01[j], n[j + 2]));
+                    const uint64_t y1 = fma2(r10[j], n[j], mul2(r11[j], n[j + 2]));
+                    out[row[r] * 64 + 16 * j] = pack2(f2lo(y0), f2hi(y0));
+                    out[row[r] * 64 + 16 * (j + 2)] = pack2(f2lo(y1), f2hi(y1));
                 }
             }
         }
@@ -1294,7 +1336,6 @@ int rope_rows() {
         const char *v = getenv("WEIGHTFERRY_ROPE_ROWS");
         if (v != nullptr && v[0] == '2') return 2;
         if (v != nullptr && v[0] == '8') return 8;
-        if (v != nullptr && v[0] == '5') return 5;  // 4 rows, registers bounded for 4 CTAs per SM
         return 4;
     }();
     return r;
@@ -1336,9 +1377,7 @@ int rope_launch(const RopeTensors &t, int n_tensors, const float *freqs, int64_t
                   tk = static_cast<int>(tokens);
         cudaError_t e;
 #define WF_RV2(WD, F)                                                                                             \
-    e = rope_rows() == 5   ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 4, 4>, t, ni, nt, hd, tk, freqs, eps, \
-                                                f_stride_token, f_stride_d, f_stride_i, f_stride_j)             \
-        : rope_rows() == 4 ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 4>, t, ni, nt, hd, tk, freqs, eps, \
+    e = rope_rows() == 4   ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 4>, t, ni, nt, hd, tk, freqs, eps, \
                                                 f_stride_token, f_stride_d, f_stride_i, f_stride_j)             \
         : rope_rows() == 8 ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 8>, t, ni, nt, hd, tk, freqs, eps, \
                                                 f_stride_token, f_stride_d, f_stride_i, f_stride_j)             \
