@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
                                                           const __nv_bfloat16 *__restrict__ s1,
                                                           const __nv_bfloat16 *__restrict__ sh,
                                                           __nv_bfloat16 *__restrict__ out, int64_t rows, int64_t K,
-                                                          int64_t rows_per_group, float eps) {
+                                                          int64_t rows_per_group, float eps, int pf) {
     __shared__ float red[2][16];  // two buffers: row i + 1's statistics never overwrite what row i still reads
     const int t = threadIdx.x;
     int64_t row = blockIdx.x;
@@ -341,6 +341,10 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
 #pragma unroll
             for (int j = 0; j < NV; ++j) raw[j] = __ldg(reinterpret_cast<const uint2 *>(x + nrow * K) + t + 128 * j);
         }
+        // past the register prefetch of the next row, pull row nrow + pf into L2 (K x 2 bytes, 16-byte aligned)
+        if (pf > 0 && t == 0 && nrow + pf < rows)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(x + (nrow + pf) * K),
+                         "r"(static_cast<uint32_t>(K * 2)) : "memory");
         // the modulation rows of this row's group (kept while consecutive rows stay in one group)
         const int64_t group = static_cast<int64_t>(static_cast<uint32_t>(row) / static_cast<uint32_t>(rows_per_group));
         if (group != cached_group) {
@@ -370,7 +374,7 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
 
 // resident CTAs per SM of a kernel (cached per kernel and device) times the SMs: a persistent grid's width
 template <auto KERN>
-int persistent_grid(int threads, size_t smem, int64_t items) {
+int wave_ctas(int threads, size_t smem) {
     auto kern = KERN;
     static std::atomic<int> occ[64];  // one cache per kernel (KERN is a template parameter); any host thread
     int dev = 0;
@@ -380,7 +384,12 @@ int persistent_grid(int threads, size_t smem, int64_t items) {
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, threads, smem) != cudaSuccess || o < 1) o = 1;
         if (dev >= 0 && dev < 64) occ[dev].store(o, std::memory_order_relaxed);
     }
-    const int64_t g = std::min<int64_t>(items, static_cast<int64_t>(o) * device_sm_count());
+    return o * device_sm_count();
+}
+
+template <auto KERN>
+int persistent_grid(int threads, size_t smem, int64_t items) {
+    const int64_t g = std::min<int64_t>(items, wave_ctas<KERN>(threads, smem));
     return static_cast<int>(std::max<int64_t>(g, 1));
 }
 
@@ -616,12 +625,20 @@ __global__ void __launch_bounds__(kRope2Warps * 32, R <= 4 ? 3 : 1) rms_rope_v2_
                                                                        int n_items, int n_tok, int heads, int tokens,
                                                                        const float *__restrict__ f, float eps,
                                                                        int64_t s_tok, int64_t s_d, int64_t s_i,
-                                                                       int64_t s_j) {
+                                                                       int64_t s_j, int pf) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     allow_dependents();
     const int lane = threadIdx.x & 31, hf = lane >> 4, p = lane & 15;
     const int item = blockIdx.x * kRope2Warps + (threadIdx.x >> 5);
     if (item >= n_items) return;  // whole warps: the shuffles below involve both halves of a warp that runs
+    if (pf > 0 && lane == 0 && item + pf < n_items) {
+        // pull into L2 the rows of the item that the warp in this position one wave of CTAs later handles: more
+        // bytes in flight than the registers of the resident warps hold, at no register or shared-memory cost
+        // (a token's heads x 256 bytes, 16-byte aligned like the tensor)
+        const int nx = item + pf, tn = nx >= n_tok ? 1 : 0;
+        const __nv_bfloat16 *src = t.x[tn] + static_cast<size_t>(nx - tn * n_tok) * heads * 128;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(heads * 256) : "memory");
+    }
     const int ti = item >= n_tok ? 1 : 0;
     const int bt = item - ti * n_tok;
     const int tok = bt % tokens;
@@ -1277,6 +1294,21 @@ extern "C" WF_API int wf_gated_residual(const void *x, const void *gate, const v
     return static_cast<int>(cudaGetLastError());
 }
 
+namespace wf {
+namespace {
+// L2 prefetch distance of ln_modulate_kernel past its register prefetch, in quarter waves of the persistent grid
+// (WEIGHTFERRY_LN_PREFETCH 0 - 9, 0 = off; default 1. Measured on 8192 rows of 2048: 12.6 us at a quarter wave,
+// 13.1 us without)
+int ln_prefetch() {
+    static const int w = [] {
+        const char *v = getenv("WEIGHTFERRY_LN_PREFETCH");
+        return (v != nullptr && v[0] >= '0' && v[0] <= '9') ? v[0] - '0' : 1;
+    }();
+    return w;
+}
+}  // namespace
+}  // namespace wf
+
 extern "C" WF_API int wf_ln_modulate(const void *x, const void *s1, const void *shift, void *out, int64_t rows,
                                     int64_t K, int64_t rows_per_group, float eps, wf_stream_t stream) {
     if (rows < 0 || rows > INT32_MAX || K <= 0 || K % 512 != 0 || K > 512 * 16 || rows_per_group <= 0)
@@ -1291,11 +1323,12 @@ extern "C" WF_API int wf_ln_modulate(const void *x, const void *s1, const void *
     auto H = static_cast<const __nv_bfloat16 *>(shift);
     auto O = static_cast<__nv_bfloat16 *>(out);
     cudaError_t e = cudaSuccess;
-#define WF_LN(NV)                                                                                    \
-    case NV: {                                                                                       \
-        const int g = persistent_grid<ln_modulate_kernel<NV>>(128, 0, rows);                         \
-        e = launch_pdl(ln_modulate_kernel<NV>, g, 128, s, X, S, H, O, rows, K, rows_per_group, eps);  \
-        break;                                                                                       \
+#define WF_LN(NV)                                                                                        \
+    case NV: {                                                                                           \
+        const int g = persistent_grid<ln_modulate_kernel<NV>>(128, 0, rows);                             \
+        const int pf = static_cast<int>(static_cast<int64_t>(g) * ln_prefetch() / 4);                    \
+        e = launch_pdl(ln_modulate_kernel<NV>, g, 128, s, X, S, H, O, rows, K, rows_per_group, eps, pf);  \
+        break;                                                                                           \
     }
     switch (K / 512) {
         WF_LN(1) WF_LN(2) WF_LN(3) WF_LN(4) WF_LN(5) WF_LN(6) WF_LN(8) WF_LN(10) WF_LN(12) WF_LN(16)
@@ -1341,6 +1374,28 @@ int rope_rows() {
     return r;
 }
 
+// L2 prefetch distance of rms_rope_v2_kernel in quarter waves of resident CTAs (WEIGHTFERRY_ROPE_PREFETCH 0 - 9,
+// 0 = off; default 1. Measured on q and k of (2, 4096, 16, 128): 24.4 us at a quarter wave, 24.7 at a half, 26.0 at
+// one wave, 26.6 without, 28 - 30 us at one and a half waves or more: prefetched rows that wait longer in L2 lose)
+int rope_prefetch() {
+    static const int w = [] {
+        const char *v = getenv("WEIGHTFERRY_ROPE_PREFETCH");
+        return (v != nullptr && v[0] >= '0' && v[0] <= '9') ? v[0] - '0' : 1;
+    }();
+    return w;
+}
+
+template <int WD, bool F, int R>
+cudaError_t rope_v2_launch(cudaLaunchConfig_t &cfg, const RopeTensors &t, int ni, int nt, int hd, int tk,
+                           const float *freqs, float eps, int64_t s_tok, int64_t s_d, int64_t s_i, int64_t s_j) {
+    const int64_t pf64 = hd <= 256 ? static_cast<int64_t>(rope_prefetch()) *
+                                         wave_ctas<rms_rope_v2_kernel<WD, F, R>>(kRope2Warps * 32, 0) * kRope2Warps / 4
+                                   : 0;
+    const int pf = static_cast<int>(std::min<int64_t>(pf64, INT32_MAX / 2));
+    return cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, R>, t, ni, nt, hd, tk, freqs, eps, s_tok, s_d, s_i, s_j,
+                              pf);
+}
+
 int rope_launch(const RopeTensors &t, int n_tensors, const float *freqs, int64_t f_stride_token, int64_t f_stride_d,
                 int64_t f_stride_i, int64_t f_stride_j, int w_dtype, int64_t batch, int64_t tokens, int64_t heads,
                 float eps, wf_stream_t stream) {
@@ -1376,13 +1431,13 @@ int rope_launch(const RopeTensors &t, int n_tensors, const float *freqs, int64_t
         const int ni = static_cast<int>(n_items), nt = static_cast<int>(n_tok), hd = static_cast<int>(heads),
                   tk = static_cast<int>(tokens);
         cudaError_t e;
-#define WF_RV2(WD, F)                                                                                             \
-    e = rope_rows() == 4   ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 4>, t, ni, nt, hd, tk, freqs, eps, \
-                                                f_stride_token, f_stride_d, f_stride_i, f_stride_j)             \
-        : rope_rows() == 8 ? cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 8>, t, ni, nt, hd, tk, freqs, eps, \
-                                                f_stride_token, f_stride_d, f_stride_i, f_stride_j)             \
-                           : cudaLaunchKernelEx(&cfg, rms_rope_v2_kernel<WD, F, 2>, t, ni, nt, hd, tk, freqs, eps, \
-                                                f_stride_token, f_stride_d, f_stride_i, f_stride_j)
+#define WF_RV2(WD, F)                                                                                          \
+    e = rope_rows() == 4   ? rope_v2_launch<WD, F, 4>(cfg, t, ni, nt, hd, tk, freqs, eps, f_stride_token, f_stride_d, \
+                                                      f_stride_i, f_stride_j)                                      \
+        : rope_rows() == 8 ? rope_v2_launch<WD, F, 8>(cfg, t, ni, nt, hd, tk, freqs, eps, f_stride_token, f_stride_d, \
+                                                      f_stride_i, f_stride_j)                                      \
+                           : rope_v2_launch<WD, F, 2>(cfg, t, ni, nt, hd, tk, freqs, eps, f_stride_token, f_stride_d, \
+                                                      f_stride_i, f_stride_j)
         if (w_dtype == WF_BF16) {
             if (f4) WF_RV2(WF_BF16, true); else WF_RV2(WF_BF16, false);
         } else if (w_dtype == WF_F16) {
