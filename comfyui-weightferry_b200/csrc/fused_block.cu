@@ -374,20 +374,6 @@ __global__ void __launch_bounds__(128) ln_modulate_kernel(const __nv_bfloat16 *_
 
 // resident CTAs per SM of a kernel (cached per kernel and device) times the SMs: a persistent grid's width
 template <auto KERN>
-int wave_ctas(int threads, size_t smem) {
-    auto kern = KERN;
-    static std::atomic<int> occ[64];  // one cache per kernel (KERN is a template parameter); any host thread
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int o = (dev >= 0 && dev < 64) ? occ[dev].load(std::memory_order_relaxed) : 0;
-    if (o == 0) {
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, threads, smem) != cudaSuccess || o < 1) o = 1;
-        if (dev >= 0 && dev < 64) occ[dev].store(o, std::memory_order_relaxed);
-    }
-    return o * device_sm_count();
-}
-
-template <auto KERN>
 int persistent_grid(int threads, size_t smem, int64_t items) {
     const int64_t g = std::min<int64_t>(items, wave_ctas<KERN>(threads, smem));
     return static_cast<int>(std::max<int64_t>(g, 1));
@@ -1179,24 +1165,21 @@ int launch_quant_lnmod(const void *x, const void *s1, const void *sh, int8_t *q,
     return static_cast<int>(cudaGetLastError());
 }
 
+// the register quantiser's kernel for (PRE, NCH, WPR, ROT): the pipelined plain kernel where it applies
+template <int PRE, int NCH, int WPR, bool ROT>
+constexpr auto quant_reg_kernel() {
+    if constexpr (!ROT && WPR == 1 && NCH <= 8) return quant_rows_plain_kernel<PRE, NCH>;
+    else return quant_rows_reg_kernel<PRE, NCH, WPR, ROT>;
+}
+
 template <int PRE, int NCH, int WPR, bool ROT = false>
 int launch_quant_reg(const void *x, const void *s1, const void *sh, const void *gelu, int8_t *q, float *sc,
                      int64_t rows, int64_t rpg, cudaStream_t s) {
-    auto kern = [] {
-        if constexpr (!ROT && WPR == 1 && NCH <= 8) return quant_rows_plain_kernel<PRE, NCH>;
-        else return quant_rows_reg_kernel<PRE, NCH, WPR, ROT>;
-    }();
-    static int per_sm = 0;
-    if (per_sm == 0) {
-        int n = 0;
-        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 256, 0);
-        if (e != cudaSuccess) return static_cast<int>(e);
-        per_sm = std::max(n, 1);
-    }
+    constexpr auto kern = quant_reg_kernel<PRE, NCH, WPR, ROT>();
     const int64_t groups = (rows + (8 / WPR) - 1) / (8 / WPR);
     // the pipelined variant walks about two rows per warp; the others one row group per CTA while they fit
     const int64_t want = (WPR == 1 && NCH <= 8) ? (groups + 1) / 2 : groups;
-    const int grid = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(device_sm_count()) * per_sm));
+    const int grid = static_cast<int>(std::min<int64_t>(want, wave_ctas<kern>(256, 0)));
     kern<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(s1),
                               static_cast<const __nv_bfloat16 *>(sh), static_cast<const __nv_bfloat16 *>(gelu), q,
                               sc, rows, rpg);

@@ -12,7 +12,9 @@
 //     double-buffers them in shared memory with 16-byte cp.async (the next chunk's bytes are in flight while the
 //     current one is decoded);
 //   * a thread decodes 8 consecutive values of one block from shared memory and writes them with one 16-byte store
-//     (two for float32), so a warp writes 512 contiguous bytes per instruction.
+//     (two for float32), so a warp writes 512 contiguous bytes per instruction;
+//   * a launch of at most two waves (a single weight) also pulls the packed bytes of each CTA's chunk after next
+//     into L2 (cp.async.bulk.prefetch.L2).
 // The batched entry point walks the chunks of a table of tensors (checkpoint-wide sweep) with the same body.
 
 #include "wf_common.cuh"
@@ -557,7 +559,7 @@ __device__ __forceinline__ float lora_scale(const Batch &) { return 0.f; }
 __device__ __forceinline__ int64_t total_chunks(const Batch &p) { return p.first_chunk[p.n]; }
 
 template <int QT, int MID, int OUT, bool ALIGNED, bool LORA, typename P>
-__global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant__ P p) {
+__global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant__ P p, int64_t pf) {
     extern __shared__ __align__(16) uint8_t smem[];
     constexpr int kStride = buf_stride<QT>();
     const int64_t n_chunks = total_chunks(p);
@@ -583,6 +585,12 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
             if constexpr (kStageDiff) stage_diff(sdiff + ((it + 1) & 1) * kChunkValues, lora_diff(p, cn), nxt.nvalues);
         }
         cp_async_commit();
+        if (ALIGNED && pf > 0 && threadIdx.x == 0 && cn + pf < n_chunks) {
+            // pull into L2 the packed bytes of the chunk pf past the next one (whole 16-byte units)
+            const ChunkRef f = chunk_of<QT, OUT>(p, cn + pf);
+            const uint32_t nb = static_cast<uint32_t>(f.nbytes) & ~15u;
+            if (nb > 0) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(f.src), "r"(nb) : "memory");
+        }
         cp_async_wait<1>();  // this thread's copies of the current chunk have landed
         __syncthreads();     // ... and every other thread's
         const float *dchunk = nullptr;
@@ -596,6 +604,18 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
 }
 
 // ------------------------------------------------------------------------------------------------- host launch
+// L2 prefetch distance past the double-buffered next chunk, in quarter grids (WEIGHTFERRY_DEQUANT_PREFETCH 0 - 9,
+// 0 = off; unset: one grid -- the chunk after next of the same CTA -- when the launch is at most two waves of
+// resident CTAs, as a single weight's is, off otherwise). Measured over rotating single weights (one wave): Q8_0 5120 x 5120 0.863 -> 0.886 of the copy
+// peak, Q4_K 5120 x 13824 0.861 -> 0.878; on the multi-wave 36-block Q4_K sweep it costs (0.993 -> 0.959).
+int dequant_prefetch(bool short_launch) {
+    static const int w = [] {
+        const char *v = getenv("WEIGHTFERRY_DEQUANT_PREFETCH");
+        return (v != nullptr && v[0] >= '0' && v[0] <= '9') ? v[0] - '0' : -1;
+    }();
+    return w >= 0 ? w : (short_launch ? 4 : 0);
+}
+
 template <int QT, int MID, int OUT, bool ALIGNED, bool LORA = false, typename P>
 int launch(const P &p, int64_t n_chunks, cudaStream_t stream) {
     if (n_chunks <= 0) return WF_OK;
@@ -636,7 +656,7 @@ int launch(const P &p, int64_t n_chunks, cudaStream_t stream) {
     attr.val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, grid * dequant_prefetch(grid <= 2 * resident) / 4);
     return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 

@@ -51,17 +51,10 @@ extern "C" WF_API int wf_hbm_probe(const void *in, int64_t in_bytes, void *out, 
     if (rc != WF_OK) return rc;
     if (n_in > n_out) return WF_ERR_ARG;  // the probe models reads at most as large as writes (ratio_fp <= 2^32)
     const uint64_t ratio_fp = (static_cast<uint64_t>(n_in) << 32) / static_cast<uint64_t>(n_out);  // n_in < 2^31
-    static int per_sm = 0;
-    if (per_sm == 0) {
-        int n = 0;
-        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, wf::hbm_probe_kernel, 256, 0);
-        if (e != cudaSuccess) return static_cast<int>(e);
-        per_sm = n > 0 ? n : 1;
-    }
     // about four tiles per CTA, never fewer CTAs than fit at once (the dequantisation kernels' grid rule: the HBM
     // sustains more of a write-heavy mix with many short-lived CTAs than with one persistent wave)
     const int64_t n_tiles = (n_out + wf::kTileOut - 1) / wf::kTileOut;
-    const int64_t resident = static_cast<int64_t>(wf::device_sm_count()) * per_sm;
+    const int64_t resident = wf::wave_ctas<wf::hbm_probe_kernel>(256, 0);
     const int grid = static_cast<int>(std::min<int64_t>(n_tiles, std::max<int64_t>(resident, (n_tiles + 3) / 4)));
     wf::hbm_probe_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint4 *>(in), n_in, ratio_fp, static_cast<uint4 *>(out), n_out);

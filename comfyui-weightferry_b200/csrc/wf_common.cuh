@@ -7,6 +7,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "weightferry_b200.h"
 
 namespace wf {
@@ -137,5 +139,21 @@ __host__ __device__ constexpr int dtype_size(int d) { return d == WF_F32 ? 4 : 2
 int device_sm_count();
 // Returns WF_OK when the current device is usable (a compute capability 10.x part), else WF_ERR_DEVICE.
 int check_device();
+
+// Resident CTAs of KERN (threads per CTA, dynamic shared memory) on the whole current device: CTAs per SM times the
+// SMs. One cache per kernel (KERN is a template parameter) and device, read and written atomically, since several
+// host threads launch (the compute thread and the SSD uploader's); 1 per SM when the query fails.
+template <auto KERN>
+int wave_ctas(int threads, size_t smem) {
+    static std::atomic<int> occ[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int o = (dev >= 0 && dev < 64) ? occ[dev].load(std::memory_order_relaxed) : 0;
+    if (o == 0) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, KERN, threads, smem) != cudaSuccess || o < 1) o = 1;
+        if (dev >= 0 && dev < 64) occ[dev].store(o, std::memory_order_relaxed);
+    }
+    return o * device_sm_count();
+}
 
 }  // namespace wf
