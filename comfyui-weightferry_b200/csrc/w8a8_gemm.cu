@@ -198,7 +198,12 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t sr
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// every output store of this thread has finished reading its shared-memory source (the stores themselves complete
+// with the grid, before any later kernel of the stream -- or a programmatic dependent past griddepcontrol.wait --
+// can read the output)
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Output tile `tile` -> (tile row, tile column). group_m == 0: tiles walk down the M direction first (column by
@@ -518,7 +523,7 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
                                       row0, n0 + half * 128, M, N);
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
-        if (lane == 0) bulk_wait_all();  // this warp's output stores have finished with its shared memory
+        if (lane == 0) bulk_wait_read_all();  // this warp's output stores have finished with its shared memory
         __syncwarp();
     }
     fence_before();
@@ -729,7 +734,7 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
                                      res, row0, n0 + half * 128, M, N);
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
-        if (lane == 0) bulk_wait_all();
+        if (lane == 0) bulk_wait_read_all();
         __syncwarp();
     }
     fence_before();
