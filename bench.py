@@ -872,6 +872,10 @@ def run_prologue(torch, args, world, rank, dist):
     stream = torch.cuda.current_stream(dev)
     s1 = (1 + sc).contiguous()
     ln = fb._get_kernels()["lnmod"][(8192,)]
+    fk = _pkg("enhancers.fused_kernels")
+    kq = fk._get_kernels()["quant_row"][(8192,)]
+    xq = torch.empty((8192, 2048), dtype=torch.int8, device=dev)
+    xs = torch.empty((8192, 1), dtype=torch.float32, device=dev)
 
     def kernel_a(i):
         x, _q, _k, out = sets[i % n_sets]
@@ -880,6 +884,14 @@ def run_prologue(torch, args, world, rank, dist):
     def kernel_b(i):
         _x, q, k, _o = sets[i % n_sets]
         return sf.rms_rope_pair(q, k, rope, wq, wk, 1e-6)
+
+    # the int8 quantisers the W8A8 block runs on the same x (context, not part of the step): plain per-token, and
+    # with the LayerNorm + modulate pending (kernel A's arithmetic with a quantising epilogue)
+    def quant_plain(i):
+        kq(sets[i % n_sets][0], None, None, xq, xs, 1, 0.0, K=2048, PRE=fk.PRE_NONE, ROTATE=False)
+
+    def quant_lnmod(i):
+        kq(sets[i % n_sets][0], s1, sh, xq, xs, 4096, 1e-6, K=2048, PRE=fk.PRE_LNMOD, ROTATE=False)
 
     def timed(fn, n):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -907,6 +919,11 @@ def run_prologue(torch, args, world, rank, dist):
     copy_b = timed(lambda i: (dst_b[i % n_sets].copy_(sets[i % n_sets][1]),
                               dst_b[(i + 1) % n_sets].copy_(sets[i % n_sets][2])), n)
     del dst_a, dst_b
+    for i in range(n_sets):
+        quant_plain(i)
+        quant_lnmod(i)
+    qp_ms = timed(quant_plain, n)
+    ql_ms = timed(quant_lnmod, n)
     x, q, k, _o = sets[0]
     bytes_a = 2 * x.numel() * 2                          # read x + write out (+16 KB parameters)
     bytes_b = 2 * (q.numel() + k.numel()) * 2 + rope.numel() * 4  # q, k in + out; the table (one launch for both)
@@ -914,7 +931,8 @@ def run_prologue(torch, args, world, rank, dist):
     value = sum_over_ranks(torch, dist, (bytes_a + bytes_b) / (step_ms / 1e3) / 1e9)
     return {"value": value, "ms": step_ms, "a_ms": a_ms, "b_ms": b_ms, "bytes_a": bytes_a, "bytes_b": bytes_b,
             "clk": clk.summary(), "launches": int(sum_over_ranks(torch, dist, 2 * n)),
-            "copy_a_us": copy_a * 1e3, "copy_b_us": copy_b * 1e3}
+            "copy_a_us": copy_a * 1e3, "copy_b_us": copy_b * 1e3, "quant_plain_us": qp_ms * 1e3,
+            "quant_lnmod_us": ql_ms * 1e3, "quant_bytes": x.numel() * 3 + 8192 * 4}
 
 
 def cpu_baseline_prologue(seconds=10.0):
@@ -965,12 +983,17 @@ def finish_prologue(torch, args, world, rank, dist, r):
                        "kernel_a_bytes": r["bytes_a"], "kernel_b_us_q_and_k": round(r["b_ms"] * 1e3, 2),
                        "kernel_b_gbs": round(b_rate, 1), "kernel_b_bytes": r["bytes_b"],
                        "torch_copy_same_bytes_us": {"a": round(r["copy_a_us"], 2), "b_q_and_k": round(r["copy_b_us"], 2)},
+                       "int8_quantiser_us": {"plain": round(r["quant_plain_us"], 2),
+                                             "lnmod_pending": round(r["quant_lnmod_us"], 2),
+                                             "bytes": r["quant_bytes"],
+                                             "frac_plain": round(r["quant_bytes"] / r["quant_plain_us"] / 1e3 / peak, 4),
+                                             "frac_lnmod": round(r["quant_bytes"] / r["quant_lnmod_us"] / 1e3 / peak, 4)},
                        "l2": "inputs larger than L2: each launch of a run reads one of 8 rotating tensor sets "
                              "(1.6 GB); no flush"},
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(ach / peak, 4), "traffic": NCU_TRAFFIC.get("prologue"),
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})",
-                         "kernel": "rms_rope_kernel" if dominant == "B" else "ln_modulate_kernel<4>",
+                         "kernel": "rms_rope_v2_kernel" if dominant == "B" else "ln_modulate_kernel<4>",
                          "kernel_a_frac": round(a_rate / peak, 4), "kernel_b_frac": round(b_rate / peak, 4)},
             "cpu_baseline": cpu, "e2e": None, "gpu_launches": r["launches"], "clocks": r["clk"]}), flush=True)
     if dist is not None:

@@ -70,6 +70,24 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
     return d;
 }
 
+// packed bf16 pairs: absolute value, maximum and minimum of each lane (exact; max / min return the other operand
+// when one is NaN, as fmaxf / fminf do)
+__device__ __forceinline__ uint32_t bf2_abs(uint32_t a) {
+    uint32_t d;
+    asm("abs.bf16x2 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+__device__ __forceinline__ uint32_t bf2_max(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t bf2_min(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("min.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 // four bf16 (8 bytes) -> float
 __device__ __forceinline__ void unpack4(uint2 w, float v[4]) {
     v[0] = bf_lo(w.x);
@@ -868,14 +886,13 @@ __device__ __forceinline__ void quant_pre(uint4 (&v)[NCH], const __nv_bfloat16 *
 
 template <int NCH>
 __device__ __forceinline__ float chunk_amax(const uint4 (&v)[NCH]) {
-    float amax = 0.f;
+    uint32_t m = 0;  // the largest |value| so far in each bf16 lane (+0 to start, as fmaxf from 0)
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
-        const uint32_t xs[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) amax = fmaxf(amax, fmaxf(fabsf(bf_lo(xs[k])), fabsf(bf_hi(xs[k]))));
+        m = bf2_max(m, bf2_max(bf2_abs(v[j].x), bf2_abs(v[j].y)));
+        m = bf2_max(m, bf2_max(bf2_abs(v[j].z), bf2_abs(v[j].w)));
     }
-    return amax;
+    return fmaxf(bf_lo(m), bf_hi(m));
 }
 
 // clamp(rint(bf16(v / sb)), -128, 127) of the four values of two bf16 pairs, as four bytes. The bf16 rounding of
@@ -886,12 +903,14 @@ __device__ __forceinline__ float chunk_amax(const uint4 (&v)[NCH]) {
 __device__ __forceinline__ uint32_t quant_quad(uint32_t xa, uint32_t xb, float sb) {
     __nv_bfloat162 ta = __floats2bfloat162_rn(div_full(bf_lo(xa), sb), div_full(bf_hi(xa), sb));
     __nv_bfloat162 tb = __floats2bfloat162_rn(div_full(bf_lo(xb), sb), div_full(bf_hi(xb), sb));
-    const uint32_t ua = *reinterpret_cast<uint32_t *>(&ta), ub = *reinterpret_cast<uint32_t *>(&tb);
+    constexpr uint32_t kLo = 0xC300C300u, kHi = 0x42FE42FEu;  // -128 and 127 in both bf16 lanes (exact)
+    const uint32_t ua = bf2_min(bf2_max(*reinterpret_cast<uint32_t *>(&ta), kLo), kHi);
+    const uint32_t ub = bf2_min(bf2_max(*reinterpret_cast<uint32_t *>(&tb), kLo), kHi);
     constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-    const uint32_t r0 = __float_as_uint(__fadd_rn(fminf(fmaxf(bf_lo(ua), -128.0f), 127.0f), kMagic));
-    const uint32_t r1 = __float_as_uint(__fadd_rn(fminf(fmaxf(bf_hi(ua), -128.0f), 127.0f), kMagic));
-    const uint32_t r2 = __float_as_uint(__fadd_rn(fminf(fmaxf(bf_lo(ub), -128.0f), 127.0f), kMagic));
-    const uint32_t r3 = __float_as_uint(__fadd_rn(fminf(fmaxf(bf_hi(ub), -128.0f), 127.0f), kMagic));
+    const uint64_t M2 = f2pack(kMagic, kMagic);
+    const uint64_t ra = add2(bf_pair(ua), M2), rb = add2(bf_pair(ub), M2);
+    const uint32_t r0 = static_cast<uint32_t>(ra), r1 = static_cast<uint32_t>(ra >> 32);
+    const uint32_t r2 = static_cast<uint32_t>(rb), r3 = static_cast<uint32_t>(rb >> 32);
     return __byte_perm(__byte_perm(r0, r1, 0x0040), __byte_perm(r2, r3, 0x0040), 0x5410);
 }
 
@@ -982,10 +1001,13 @@ __device__ __forceinline__ void quant_rows_reg_body(const __nv_bfloat16 *__restr
                                                     const __nv_bfloat16 *__restrict__ sh,
                                                     const __nv_bfloat16 *__restrict__ gelu, int8_t *__restrict__ q,
                                                     float *__restrict__ scale_out, int64_t rows,
-                                                    int64_t rows_per_group) {
+                                                    int64_t rows_per_group, int64_t pf) {
     constexpr int K = 256 * NCH * WPR;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     allow_dependents();
+    // launched as a programmatic dependent: the previous kernel's writes (x, and its reads of q / scale_out) are
+    // complete past this point, which precedes every global access
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if constexpr (WPR == 1 && NCH <= 8) {
         // the next row waits in shared memory (cp.async), not in registers: each lane reads back and refills only
         // its own 16-byte slots, so the refill needs no synchronisation, and the kernel fits three CTAs per SM
@@ -1010,6 +1032,10 @@ __device__ __forceinline__ void quant_rows_reg_body(const __nv_bfloat16 *__restr
                     cp_async16(&nxt[warp][j][lane], reinterpret_cast<const uint4 *>(x + nrow * K) + 32 * j + lane);
             }
             cp_async_commit();
+            // past the staged next row, pull row nrow + pf into L2 (K x 2 bytes, 16-byte aligned)
+            if (pf > 0 && lane == 0 && nrow + pf < rows)
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(x + (nrow + pf) * K),
+                             "r"(static_cast<uint32_t>(K * 2)) : "memory");
             quant_pre<PRE, NCH>(v, s1, sh, gelu, (row / rows_per_group) * K, lane);
             float amax = ROT ? rotate_chunks<NCH>(v, lane) : chunk_amax<NCH>(v);
 #pragma unroll
@@ -1063,8 +1089,8 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const __nv_bfloat16
                                                              const __nv_bfloat16 *__restrict__ sh,
                                                              const __nv_bfloat16 *__restrict__ gelu,
                                                              int8_t *__restrict__ q, float *__restrict__ scale_out,
-                                                             int64_t rows, int64_t rows_per_group) {
-    quant_rows_reg_body<PRE, NCH, WPR, ROT>(x, s1, sh, gelu, q, scale_out, rows, rows_per_group);
+                                                             int64_t rows, int64_t rows_per_group, int64_t pf) {
+    quant_rows_reg_body<PRE, NCH, WPR, ROT>(x, s1, sh, gelu, q, scale_out, rows, rows_per_group, pf);
 }
 
 // The plain pipelined case (no rotation, one warp per row, K <= 2048) with three CTAs per SM: the next row waits in
@@ -1075,8 +1101,8 @@ __global__ void __launch_bounds__(256, 3) quant_rows_plain_kernel(const __nv_bfl
                                                                   const __nv_bfloat16 *__restrict__ sh,
                                                                   const __nv_bfloat16 *__restrict__ gelu,
                                                                   int8_t *__restrict__ q, float *__restrict__ scale_out,
-                                                                  int64_t rows, int64_t rows_per_group) {
-    quant_rows_reg_body<PRE, NCH, 1, false>(x, s1, sh, gelu, q, scale_out, rows, rows_per_group);
+                                                                  int64_t rows, int64_t rows_per_group, int64_t pf) {
+    quant_rows_reg_body<PRE, NCH, 1, false>(x, s1, sh, gelu, q, scale_out, rows, rows_per_group, pf);
 }
 
 // The quantiser with the pending LayerNorm + modulate (pre 3) and no rotation, K = 512 * NV: ln_modulate_kernel's
@@ -1089,13 +1115,15 @@ __global__ void __launch_bounds__(128) quant_lnmod_kernel(const __nv_bfloat16 *_
                                                           const __nv_bfloat16 *__restrict__ s1,
                                                           const __nv_bfloat16 *__restrict__ sh,
                                                           int8_t *__restrict__ q, float *__restrict__ scale_out,
-                                                          int64_t rows, int64_t K, int64_t rows_per_group, float eps) {
+                                                          int64_t rows, int64_t K, int64_t rows_per_group, float eps,
+                                                          int pf) {
     __shared__ float red[16];
     __shared__ float amax_w[2][4];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     allow_dependents();
     int64_t row = blockIdx.x;
     if (row >= rows) return;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // a programmatic dependent, as quant_rows_reg_body
     uint2 raw[NV];
 #pragma unroll
     for (int j = 0; j < NV; ++j) raw[j] = __ldg(reinterpret_cast<const uint2 *>(x + row * K) + t + 128 * j);
@@ -1111,6 +1139,9 @@ __global__ void __launch_bounds__(128) quant_lnmod_kernel(const __nv_bfloat16 *_
 #pragma unroll
             for (int j = 0; j < NV; ++j) raw[j] = __ldg(reinterpret_cast<const uint2 *>(x + nrow * K) + t + 128 * j);
         }
+        if (pf > 0 && t == 0 && nrow + pf < rows)  // as in ln_modulate_kernel
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(x + (nrow + pf) * K),
+                         "r"(static_cast<uint32_t>(K * 2)) : "memory");
         const int64_t group = static_cast<int64_t>(static_cast<uint32_t>(row) / static_cast<uint32_t>(rows_per_group));
         if (group != cached_group) {
             cached_group = group;
@@ -1124,18 +1155,17 @@ __global__ void __launch_bounds__(128) quant_lnmod_kernel(const __nv_bfloat16 *_
         ln_stats_n<NV * 4>(v, K, mu, var, red);
         const float rstd = rsqrt_approx(__fadd_rn(var, eps));
         uint32_t ob[NV * 2];  // the modulated row as bf16 pairs
-        float amax = 0.f;
+        uint32_t am2 = 0;     // its largest |value| in each bf16 lane
+        const uint64_t neg_mu = f2pack(-mu, -mu), rstd2 = f2pack(rstd, rstd);  // as in ln_modulate_kernel
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-            const uint32_t n01 = pack2(__fmul_rn(__fsub_rn(v[4 * j], mu), rstd),
-                                       __fmul_rn(__fsub_rn(v[4 * j + 1], mu), rstd));
-            const uint32_t n23 = pack2(__fmul_rn(__fsub_rn(v[4 * j + 2], mu), rstd),
-                                       __fmul_rn(__fsub_rn(v[4 * j + 3], mu), rstd));
-            ob[2 * j] = mod_bf16x2(n01, sraw[j].x, hraw[j].x);
-            ob[2 * j + 1] = mod_bf16x2(n23, sraw[j].y, hraw[j].y);
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(bf_lo(ob[2 * j])), fabsf(bf_hi(ob[2 * j]))),
-                                     fmaxf(fabsf(bf_lo(ob[2 * j + 1])), fabsf(bf_hi(ob[2 * j + 1])))));
+            const uint64_t a = mul2(add2(f2pack(v[4 * j], v[4 * j + 1]), neg_mu), rstd2);
+            const uint64_t b = mul2(add2(f2pack(v[4 * j + 2], v[4 * j + 3]), neg_mu), rstd2);
+            ob[2 * j] = mod_bf16x2(pack2(f2lo(a), f2hi(a)), sraw[j].x, hraw[j].x);
+            ob[2 * j + 1] = mod_bf16x2(pack2(f2lo(b), f2hi(b)), sraw[j].y, hraw[j].y);
+            am2 = bf2_max(am2, bf2_max(bf2_abs(ob[2 * j]), bf2_abs(ob[2 * j + 1])));
         }
+        float amax = fmaxf(bf_lo(am2), bf_hi(am2));
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
         if (lane == 0) amax_w[parity][warp] = amax;  // two buffers: a fast warp may reach the next row first
@@ -1155,14 +1185,25 @@ __global__ void __launch_bounds__(128) quant_lnmod_kernel(const __nv_bfloat16 *_
     }
 }
 
+// L2 prefetch distance of the row-walking quantisers past their staged next row, in quarter waves
+// (WEIGHTFERRY_QUANT_PREFETCH 0 - 9, 0 = off; default 1)
+int row_prefetch() {
+    static const int w = [] {
+        const char *v = getenv("WEIGHTFERRY_QUANT_PREFETCH");
+        return (v != nullptr && v[0] >= '0' && v[0] <= '9') ? v[0] - '0' : 1;
+    }();
+    return w;
+}
+
 template <int NV>
 int launch_quant_lnmod(const void *x, const void *s1, const void *sh, int8_t *q, float *sc, int64_t rows, int64_t K,
                        int64_t rpg, float eps, cudaStream_t s) {
     const int g = persistent_grid<quant_lnmod_kernel<NV>>(128, 0, rows);
-    quant_lnmod_kernel<NV><<<g, 128, 0, s>>>(static_cast<const __nv_bfloat16 *>(x),
-                                             static_cast<const __nv_bfloat16 *>(s1),
-                                             static_cast<const __nv_bfloat16 *>(sh), q, sc, rows, K, rpg, eps);
-    return static_cast<int>(cudaGetLastError());
+    const int pf = static_cast<int>(static_cast<int64_t>(g) * row_prefetch() / 4);
+    const cudaError_t e = launch_pdl(quant_lnmod_kernel<NV>, g, 128, s, static_cast<const __nv_bfloat16 *>(x),
+                                     static_cast<const __nv_bfloat16 *>(s1), static_cast<const __nv_bfloat16 *>(sh),
+                                     q, sc, rows, K, rpg, eps, pf);
+    return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 // the register quantiser's kernel for (PRE, NCH, WPR, ROT): the pipelined plain kernel where it applies
@@ -1180,10 +1221,12 @@ int launch_quant_reg(const void *x, const void *s1, const void *sh, const void *
     // the pipelined variant walks about two rows per warp; the others one row group per CTA while they fit
     const int64_t want = (WPR == 1 && NCH <= 8) ? (groups + 1) / 2 : groups;
     const int grid = static_cast<int>(std::min<int64_t>(want, wave_ctas<kern>(256, 0)));
-    kern<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(s1),
-                              static_cast<const __nv_bfloat16 *>(sh), static_cast<const __nv_bfloat16 *>(gelu), q,
-                              sc, rows, rpg);
-    return static_cast<int>(cudaGetLastError());
+    // the pipelined kernel's L2 prefetch distance: a quarter of its warps' rows per quarter wave of row_prefetch()
+    const int64_t pf = (WPR == 1 && NCH <= 8) ? static_cast<int64_t>(grid) * 8 * row_prefetch() / 4 : 0;
+    const cudaError_t e = launch_pdl(kern, grid, 256, s, static_cast<const __nv_bfloat16 *>(x),
+                                     static_cast<const __nv_bfloat16 *>(s1), static_cast<const __nv_bfloat16 *>(sh),
+                                     static_cast<const __nv_bfloat16 *>(gelu), q, sc, rows, rpg, pf);
+    return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 // The rotated (ConvRot) register kernel for K = 256 * n up to 6144 (one warp per row), or false.
