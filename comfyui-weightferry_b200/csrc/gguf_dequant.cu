@@ -13,13 +13,14 @@
 //     current one is decoded);
 //   * a thread decodes 8 consecutive values of one block from shared memory and writes them with one 16-byte store
 //     (two for float32), so a warp writes 512 contiguous bytes per instruction;
-//   * a launch of at most two waves (a single weight) also pulls the packed bytes of each CTA's chunk after next
-//     into L2 (cp.async.bulk.prefetch.L2).
+//   * a single-tensor launch of at most two waves (one weight) also pulls the packed bytes of each CTA's chunk after
+//     next into L2 (cp.async.bulk.prefetch.L2).
 // The batched entry point walks the chunks of a table of tensors (checkpoint-wide sweep) with the same body.
 
 #include "wf_common.cuh"
 
 #include <atomic>
+#include <type_traits>
 
 #include <algorithm>
 
@@ -585,11 +586,14 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
             if constexpr (kStageDiff) stage_diff(sdiff + ((it + 1) & 1) * kChunkValues, lora_diff(p, cn), nxt.nvalues);
         }
         cp_async_commit();
-        if (ALIGNED && pf > 0 && threadIdx.x == 0 && cn + pf < n_chunks) {
-            // pull into L2 the packed bytes of the chunk pf past the next one (whole 16-byte units)
-            const ChunkRef f = chunk_of<QT, OUT>(p, cn + pf);
-            const uint32_t nb = static_cast<uint32_t>(f.nbytes) & ~15u;
-            if (nb > 0) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(f.src), "r"(nb) : "memory");
+        if constexpr (ALIGNED && std::is_same_v<P, Single>) {  // (the batched sweep runs many waves: none)
+            if (pf > 0 && threadIdx.x == 0 && cn + pf < n_chunks) {
+                // pull into L2 the packed bytes of the chunk pf past the next one (whole 16-byte units)
+                const ChunkRef f = chunk_of<QT, OUT>(p, cn + pf);
+                const uint32_t nb = static_cast<uint32_t>(f.nbytes) & ~15u;
+                if (nb > 0)
+                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(f.src), "r"(nb) : "memory");
+            }
         }
         cp_async_wait<1>();  // this thread's copies of the current chunk have landed
         __syncthreads();     // ... and every other thread's
