@@ -98,6 +98,7 @@ __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
 }
 
 __device__ __forceinline__ void mbar_drain_wait(uint32_t a, uint32_t parity) {
+    if (mbar_try(a, parity)) return;  // the usual case; a read of the global timer costs ~0.2 us
     const uint64_t t0 = global_ns();
     while (!mbar_try(a, parity) && global_ns() - t0 < kWaitLimitNs) {
     }
@@ -457,12 +458,8 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
             }
             if (!ok) {
                 // drain: every issued load lands before the CTA leaves (bounded)
-                for (int s = 0; s < STAGES; ++s) {
-                    if (!pending[s]) continue;
-                    const uint64_t t0 = global_ns();
-                    while (!mbar_try(full0 + 8 * s, issued_phase[s]) && global_ns() - t0 < kWaitLimitNs) {
-                    }
-                }
+                for (int s = 0; s < STAGES; ++s)
+                    if (pending[s]) mbar_drain_wait(full0 + 8 * s, issued_phase[s]);
             }
         }
     } else if (warp == 9) {
@@ -495,9 +492,7 @@ w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
             }
             // every MMA issued by this thread has finished before the tensor memory is released
             mma_commit(drain);
-            const uint64_t t0 = global_ns();
-            while (!mbar_try(drain, 0) && global_ns() - t0 < kWaitLimitNs) {
-            }
+            mbar_drain_wait(drain, 0);
         }
         __syncwarp();
     } else {
@@ -704,9 +699,7 @@ w8a8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_con
                 if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
             }
             mma_commit_pair(drain);
-            const uint64_t t0 = global_ns();
-            while (!mbar_try(drain, 0) && global_ns() - t0 < kWaitLimitNs) {
-            }
+            mbar_drain_wait(drain, 0);
         }
         __syncwarp();
     } else {
