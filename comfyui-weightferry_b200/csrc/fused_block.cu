@@ -1188,10 +1188,7 @@ __global__ void __launch_bounds__(128) quant_lnmod_kernel(const __nv_bfloat16 *_
 // L2 prefetch distance of the row-walking quantisers past their staged next row, in quarter waves
 // (WEIGHTFERRY_QUANT_PREFETCH 0 - 9, 0 = off; default 1)
 int row_prefetch() {
-    static const int w = [] {
-        const char *v = getenv("WEIGHTFERRY_QUANT_PREFETCH");
-        return (v != nullptr && v[0] >= '0' && v[0] <= '9') ? v[0] - '0' : 1;
-    }();
+    static const int w = env_digit("WEIGHTFERRY_QUANT_PREFETCH", 1);
     return w;
 }
 
@@ -1326,10 +1323,7 @@ namespace {
 // (WEIGHTFERRY_LN_PREFETCH 0 - 9, 0 = off; default 1. Measured on 8192 rows of 2048: 12.6 us at a quarter wave,
 // 13.1 us without)
 int ln_prefetch() {
-    static const int w = [] {
-        const char *v = getenv("WEIGHTFERRY_LN_PREFETCH");
-        return (v != nullptr && v[0] >= '0' && v[0] <= '9') ? v[0] - '0' : 1;
-    }();
+    static const int w = env_digit("WEIGHTFERRY_LN_PREFETCH", 1);
     return w;
 }
 }  // namespace
@@ -1381,10 +1375,7 @@ namespace {
 
 // WEIGHTFERRY_ROPE_V1=1 keeps the shared-memory kernel (rms_rope_kernel) for every launch
 bool rope_v2() {
-    static const bool v2 = [] {
-        const char *v = getenv("WEIGHTFERRY_ROPE_V1");
-        return !(v != nullptr && v[0] == '1');
-    }();
+    static const bool v2 = env_digit("WEIGHTFERRY_ROPE_V1", 0) != 1;
     return v2;
 }
 
@@ -1392,10 +1383,8 @@ bool rope_v2() {
 // k of (2, 4096, 16, 128): 2 rows 29.0 us, 4 rows 27.4 us)
 int rope_rows() {
     static const int r = [] {
-        const char *v = getenv("WEIGHTFERRY_ROPE_ROWS");
-        if (v != nullptr && v[0] == '2') return 2;
-        if (v != nullptr && v[0] == '8') return 8;
-        return 4;
+        const int d = env_digit("WEIGHTFERRY_ROPE_ROWS", 4);
+        return d == 2 || d == 8 ? d : 4;
     }();
     return r;
 }
@@ -1404,10 +1393,7 @@ int rope_rows() {
 // 0 = off; default 1. Measured on q and k of (2, 4096, 16, 128): 24.4 us at a quarter wave, 24.7 at a half, 26.0 at
 // one wave, 26.6 without, 28 - 30 us at one and a half waves or more: prefetched rows that wait longer in L2 lose)
 int rope_prefetch() {
-    static const int w = [] {
-        const char *v = getenv("WEIGHTFERRY_ROPE_PREFETCH");
-        return (v != nullptr && v[0] >= '0' && v[0] <= '9') ? v[0] - '0' : 1;
-    }();
+    static const int w = env_digit("WEIGHTFERRY_ROPE_PREFETCH", 1);
     return w;
 }
 

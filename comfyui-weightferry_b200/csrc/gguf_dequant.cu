@@ -613,10 +613,7 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
 // resident CTAs, as a single weight's is, off otherwise). Measured over rotating single weights (one wave): Q8_0 5120 x 5120 0.863 -> 0.886 of the copy
 // peak, Q4_K 5120 x 13824 0.861 -> 0.878; on the multi-wave 36-block Q4_K sweep it costs (0.993 -> 0.959).
 int dequant_prefetch(bool short_launch) {
-    static const int w = [] {
-        const char *v = getenv("WEIGHTFERRY_DEQUANT_PREFETCH");
-        return (v != nullptr && v[0] >= '0' && v[0] <= '9') ? v[0] - '0' : -1;
-    }();
+    static const int w = env_digit("WEIGHTFERRY_DEQUANT_PREFETCH", -1);
     return w >= 0 ? w : (short_launch ? 4 : 0);
 }
 

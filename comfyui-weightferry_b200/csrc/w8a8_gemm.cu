@@ -778,12 +778,9 @@ EncodeTiled encoder() {
     return fn;
 }
 
-// WEIGHTFERRY_W8A8_1SM=1 keeps every problem on the one-CTA kernel (the pair kernel is used for m > 128 otherwise)
+// WEIGHTFERRY_PDL=0 launches the GEMM as a plain kernel instead of a programmatic dependent
 bool use_pdl() {
-    static const bool pdl = [] {
-        const char *v = getenv("WEIGHTFERRY_PDL");
-        return !(v != nullptr && v[0] == '0');
-    }();
+    static const bool pdl = env_digit("WEIGHTFERRY_PDL", 1) != 0;
     return pdl;
 }
 
@@ -813,11 +810,9 @@ int tile_group_m() {
     return g;
 }
 
+// WEIGHTFERRY_W8A8_1SM=1 keeps every problem on the one-CTA kernel (the pair kernel is used for m > 128 otherwise)
 bool use_pair_kernel() {
-    static const bool pair = [] {
-        const char *v = getenv("WEIGHTFERRY_W8A8_1SM");
-        return !(v != nullptr && v[0] == '1');
-    }();
+    static const bool pair = env_digit("WEIGHTFERRY_W8A8_1SM", 0) != 1;
     return pair;
 }
 

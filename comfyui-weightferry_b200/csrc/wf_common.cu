@@ -1,6 +1,8 @@
 // Library-wide entry points (version, status strings) and the per-device facts the launchers size grids with.
 #include "wf_common.cuh"
 
+#include <cstdlib>
+
 #include <atomic>
 
 namespace wf {
@@ -10,6 +12,11 @@ constexpr int kMaxDevices = 64;
 std::atomic<int> g_sm[kMaxDevices];   // 0 = not queried yet
 std::atomic<int> g_ok[kMaxDevices];   // 0 = not checked, 1 = usable, -1 = not an sm_100 part
 }  // namespace
+
+int env_digit(const char *name, int dflt) {
+    const char *v = getenv(name);
+    return (v != nullptr && v[0] >= '0' && v[0] <= '9') ? v[0] - '0' : dflt;
+}
 
 int device_sm_count() {
     int dev = 0;

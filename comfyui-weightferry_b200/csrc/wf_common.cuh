@@ -139,6 +139,9 @@ __host__ __device__ constexpr int dtype_size(int d) { return d == WF_F32 ? 4 : 2
 int device_sm_count();
 // Returns WF_OK when the current device is usable (a compute capability 10.x part), else WF_ERR_DEVICE.
 int check_device();
+// The first character of environment variable `name` as a digit 0-9, else `dflt` (unset, empty or not a digit). The
+// kernels' tuning switches are read once per process through this.
+int env_digit(const char *name, int dflt);
 
 // Resident CTAs of KERN (threads per CTA, dynamic shared memory) on the whole current device: CTAs per SM times the
 // SMs. One cache per kernel (KERN is a template parameter) and device, read and written atomically, since several
