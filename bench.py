@@ -981,6 +981,92 @@ def run_prologue(torch, args, world, rank, dist):
             "quant_lnmod_us": ql_ms * 1e3, "quant_bytes": x.numel() * 3 + 8192 * 4}
 
 
+def run_block(torch, args, world, rank, dist):
+    """The fused Cosmos block drop-in against the unpatched block forward, on a Cosmos-Predict2-2B block at configs[3]'s
+    shape (x [2, 1, 64, 64, 2048], 16 heads of 128, MLP 8192, AdaLN-LoRA 256, 512 context tokens of 1024). ComfyUI is
+    absent, so the block is the stand-in of its Cosmos classes the drop-in tests use (tests/fake_comfy.py): the
+    unpatched forward is PyTorch's LayerNorm, modulation, RMSNorm, float32 RoPE and addcmul around the Linear modules
+    and SDPA; the patched one is install()'s. bf16 weights time both; int8 (ConvRot) weights time the patched forward,
+    its GEMMs this library's W8A8 path -- the two layers it leaves to ComfyUI (the cross-attention's k / v
+    projections of the context) run on the same kernels in place of comfy_kitchen's. The reference's figure for this
+    comparison: fused Anima block 22.1 vs 30.3 ms (RTX 4060)."""
+    sys.path.insert(0, os.path.join(REPO, "tests"))
+    fb = _pkg("enhancers.fused_block")  # imported before the stand-in exists: nothing installed at import
+    import fake_comfy
+    fake_comfy.FAST_INT8 = True  # the layers the drop-in leaves to ComfyUI run on kernels, as comfy_kitchen's would
+    p2 = fake_comfy.register()
+    dims = dict(x_dim=2048, ctx_dim=1024, heads=16, mlp_dim=8192, lora=True, lora_dim=256)
+    inputs = fake_comfy.block_inputs(x_dim=2048, ctx_dim=1024, B=2, T=1, H=64, W=64, S=512, lora=True,
+                                     device=f"cuda:{torch.cuda.current_device()}")
+    x, emb, ctx, rope, lora_t = inputs
+    stream = torch.cuda.current_stream()
+    n = max(args.steps, 5)
+
+    def timed(blk, parts):
+        fb.install(parts)
+        with torch.no_grad():
+            for _ in range(args.warmup):
+                blk(x, emb, ctx, rope, lora_t, None, {})
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(n):
+                out = blk(x, emb, ctx, rope, lora_t, None, {})
+            e1.record(stream)
+            torch.cuda.synchronize()
+        fb.install(())
+        return e0.elapsed_time(e1) / n, out
+
+    parts = ("mod", "qkv", "modq", "gelu", "rms", "res", "ln")
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        blk = fake_comfy.build_block(p2, "bf16", device=x.device, **dims)
+        un_ms, ref = timed(blk, ())
+        fu_ms, got = timed(blk, parts)
+        fb.stats(reset=True)
+        del blk
+        blk8 = fake_comfy.build_block(p2, "int8", device=x.device, convrot=True, **dims)
+        fb.install(parts)
+        with torch.no_grad():
+            blk8(x, emb, ctx, rope, lora_t, None, {})
+        st8 = fb.stats(reset=True)
+        fb.install(())
+        i8_ms, _ = timed(blk8, parts)
+        del blk8
+    d = (got.float() - ref.float()).abs()
+    fake_comfy.unregister()
+    return {"unpatched_ms": max_over_ranks(torch, dist, un_ms), "fused_ms": max_over_ranks(torch, dist, fu_ms),
+            "int8_fused_ms": max_over_ranks(torch, dist, i8_ms), "int8_stats": st8,
+            "rel_max_diff": float(d.max() / ref.float().abs().max()), "clk": clk.summary(), "n": n}
+
+
+def finish_block(torch, args, world, rank, dist, r):
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        tokens = 2 * 64 * 64
+        print(json.dumps({
+            "metric": "fused Cosmos block forward ms (drop-in vs unpatched)", "value": round(r["fused_ms"], 4),
+            "unit": "ms/block", "n_gpus": world, "steps": r["n"], "warmup": args.warmup,
+            "ms_per_step": round(r["fused_ms"], 4), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 (int8 line: int8 x int8 GEMMs)", "data": "synthetic (seeded)",
+            "config": {"workload": "Cosmos-Predict2-2B block (configs[3] shape): x [2, 1, 64, 64, 2048], 16 heads, MLP "
+                                   "8192, AdaLN-LoRA 256, 512 context tokens of 1024; ComfyUI's Cosmos classes as the "
+                                   "drop-in tests' stand-in",
+                       "tokens": tokens, "unpatched_bf16_ms": round(r["unpatched_ms"], 4),
+                       "fused_bf16_ms": round(r["fused_ms"], 4),
+                       "speedup_bf16": round(r["unpatched_ms"] / r["fused_ms"], 3),
+                       "fused_int8_ms": round(r["int8_fused_ms"], 4),
+                       "speedup_int8_vs_unpatched_bf16": round(r["unpatched_ms"] / r["int8_fused_ms"], 3),
+                       "int8_parts_used": r["int8_stats"],
+                       "bf16_fused_vs_unpatched_rel_max_diff": round(r["rel_max_diff"], 5),
+                       "reference_figure": "fused Anima block 22.1 vs 30.3 ms per block (x1.37), RTX 4060"},
+            "roofline": None, "cpu_baseline": None, "e2e": None, "gpu_launches": None, "clocks": r["clk"]}),
+              flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def cpu_baseline_prologue(seconds=10.0):
     """The oracle's kernel A and kernel B on the first 512 rows / tokens of configs[3], repeated for ~seconds."""
     import torch
@@ -1348,7 +1434,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="sweep",
-                    choices=["sweep", "q8", "q4k", "w8a8", "stack", "prologue", "formats", "lora", "ssd"])
+                    choices=["sweep", "q8", "q4k", "w8a8", "stack", "prologue", "formats", "lora", "ssd", "block"])
     ap.add_argument("--ssd-blocks", type=int, default=8, help="ssd: blocks in the cache file")
     ap.add_argument("--slots", type=int, default=3, help="stack: GPU slots of the streaming ring")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -1387,6 +1473,8 @@ def main():
         return finish_stack(torch, args, world, rank, dist, run_stack(torch, args, world, rank, dist))
     elif args.workload == "w8a8":
         return finish_w8a8(torch, args, world, rank, dist, run_w8a8(torch, args, world, rank, dist))
+    elif args.workload == "block":
+        return finish_block(torch, args, world, rank, dist, run_block(torch, args, world, rank, dist))
     else:
         r = run_single_weight(torch, args, world, rank, dist, args.workload)
     peak, peak_kind = measured_peaks()

@@ -934,42 +934,79 @@ __device__ __forceinline__ void quant_store(const uint4 (&v)[NCH], float sb, uin
 // d2 = (lane >> 1) & 3, d3 = (lane >> 3) & 3; stage s combines the four elements that differ only in digit s, taken
 // in digit order (a, b, c, d), into output k = their digit: ((+-a +- b) +- c) +- d with the signs of output k --
 // k = 0: (+, +, +, -), 1: (+, +, -, +), 2: (+, -, +, +), 3: (-, +, +, +) -- the reference's sums, left to right.
-__device__ __forceinline__ float neg_if(float x, bool n) { return n ? -x : x; }
-__device__ __forceinline__ float had4(float a, float b, float c, float d, int k) {
-    const float t = __fadd_rn(neg_if(a, k == 3), neg_if(b, k == 2));
-    return __fadd_rn(__fadd_rn(t, neg_if(c, k == 1)), neg_if(d, k == 0));
+
+// had4 of output k for two independent sets of four values at once (packed float32 lanes): the terms' signs as
+// factors +-1 (exact), t = fma(sa, a, sb * b), then fma(sc, c, t), fma(sd, d, t) -- each fma rounds once, so every
+// step is the reference's float addition of the (negated) term, in the same order
+__device__ __forceinline__ uint64_t had4x2(uint64_t a, uint64_t b, uint64_t c, uint64_t d, const uint64_t (&s)[4]) {
+    return fma2(s[3], d, fma2(s[2], c, fma2(s[0], a, mul2(s[1], b))));
+}
+// the sign factors of output k: term j is negated when j == 3 - k
+__device__ __forceinline__ void had4_signs(int k, uint64_t (&s)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float f = j == 3 - k ? -1.0f : 1.0f;
+        s[j] = f2pack(f, f);
+    }
 }
 
-// the chunk's 8 values of this lane, rotated and scaled by 1/16 (exact); all 32 lanes take part
+// the chunk's 8 values of this lane, rotated and scaled by 1/16 (exact); all 32 lanes take part. Values i and
+// i + 4 (digit 0 and 1 stages) or i and i + 1 (digit 2 and 3) share their signs and run as one packed pair.
 __device__ __forceinline__ void hadamard256(float (&f)[8], int lane) {
-    float o[8];
+    uint64_t s[4];
+    // digit 0: inside the lane; outputs k of the two halves (values 0-3 and 4-7) as one pair
+    uint64_t o[4];  // (output k of values 0-3, output k of values 4-7)
 #pragma unroll
-    for (int h = 0; h < 2; ++h)  // digit 0: inside the lane
-#pragma unroll
-        for (int k = 0; k < 4; ++k) o[4 * h + k] = had4(f[4 * h], f[4 * h + 1], f[4 * h + 2], f[4 * h + 3], k);
-    const int p = lane & 1;  // digit 1: the lane pair (lane ^ 1); this lane holds digit values 2p and 2p + 1
+    for (int k = 0; k < 4; ++k) {
+        had4_signs(k, s);
+        o[k] = had4x2(f2pack(f[0], f[4]), f2pack(f[1], f[5]), f2pack(f[2], f[6]), f2pack(f[3], f[7]), s);
+    }
+    // digit 1: the lane pair (lane ^ 1); this lane holds digit values 2p and 2p + 1 (its values m and 4 + m)
+    const int p = lane & 1;
+    uint64_t s_lo[4], s_hi[4];
+    had4_signs(2 * p, s_lo);
+    had4_signs(2 * p + 1, s_hi);
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
-        const float q0 = __shfl_xor_sync(0xFFFFFFFFu, o[m], 1), q1 = __shfl_xor_sync(0xFFFFFFFFu, o[4 + m], 1);
-        const float a = p ? q0 : o[m], b = p ? q1 : o[4 + m], c = p ? o[m] : q0, d = p ? o[4 + m] : q1;
-        f[m] = had4(a, b, c, d, 2 * p);
-        f[4 + m] = had4(a, b, c, d, 2 * p + 1);
+        const float om = f2lo(o[m]), o4m = f2hi(o[m]);
+        const float q0 = __shfl_xor_sync(0xFFFFFFFFu, om, 1), q1 = __shfl_xor_sync(0xFFFFFFFFu, o4m, 1);
+        const float a = p ? q0 : om, b = p ? q1 : o4m, c = p ? om : q0, d = p ? o4m : q1;
+        // outputs 2p (value m, low lane) and 2p + 1 (value 4 + m, high lane): the same operands, their own signs
+        uint64_t sp[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sp[j] = (s_lo[j] & 0xFFFFFFFFull) | (s_hi[j] & 0xFFFFFFFF00000000ull);
+        const uint64_t y = had4x2(f2pack(a, a), f2pack(b, b), f2pack(c, c), f2pack(d, d), sp);
+        f[m] = f2lo(y);
+        f[4 + m] = f2hi(y);
     }
-    const int d2 = (lane >> 1) & 3, base2 = lane & ~6;  // digit 2: lanes that differ in bits 1-2
+    // digit 2: lanes that differ in bits 1-2; output d2 of this lane's quad, values i and i + 1 as a pair
+    const int d2 = (lane >> 1) & 3, base2 = lane & ~6;
+    had4_signs(d2, s);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        float v4[4];
+    for (int i = 0; i < 8; i += 2) {
+        uint64_t v4[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v4[k] = __shfl_sync(0xFFFFFFFFu, f[i], base2 | (k << 1));
-        f[i] = had4(v4[0], v4[1], v4[2], v4[3], d2);
+        for (int k = 0; k < 4; ++k)
+            v4[k] = f2pack(__shfl_sync(0xFFFFFFFFu, f[i], base2 | (k << 1)),
+                           __shfl_sync(0xFFFFFFFFu, f[i + 1], base2 | (k << 1)));
+        const uint64_t y = had4x2(v4[0], v4[1], v4[2], v4[3], s);
+        f[i] = f2lo(y);
+        f[i + 1] = f2hi(y);
     }
-    const int d3 = (lane >> 3) & 3, base3 = lane & ~24;  // digit 3: lanes that differ in bits 3-4
+    // digit 3: lanes that differ in bits 3-4, then the exact scaling by 1/16
+    const int d3 = (lane >> 3) & 3, base3 = lane & ~24;
+    had4_signs(d3, s);
+    const uint64_t sixteenth = f2pack(0.0625f, 0.0625f);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        float v4[4];
+    for (int i = 0; i < 8; i += 2) {
+        uint64_t v4[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v4[k] = __shfl_sync(0xFFFFFFFFu, f[i], base3 | (k << 3));
-        f[i] = __fmul_rn(had4(v4[0], v4[1], v4[2], v4[3], d3), 0.0625f);
+        for (int k = 0; k < 4; ++k)
+            v4[k] = f2pack(__shfl_sync(0xFFFFFFFFu, f[i], base3 | (k << 3)),
+                           __shfl_sync(0xFFFFFFFFu, f[i + 1], base3 | (k << 3)));
+        const uint64_t y = mul2(had4x2(v4[0], v4[1], v4[2], v4[3], s), sixteenth);
+        f[i] = f2lo(y);
+        f[i + 1] = f2hi(y);
     }
 }
 
@@ -1226,22 +1263,32 @@ int launch_quant_reg(const void *x, const void *s1, const void *sh, const void *
     return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
-// The rotated (ConvRot) register kernel for K = 256 * n up to 6144 (one warp per row), or false.
+// The rotated (ConvRot) register kernel for K = 256 * n up to 3072 (one warp per row), K = 4096 / 5120 / 6144 (four
+// warps per row) or K = 2048 * n from 8192 to 32768 (eight warps per row) -- each warp's segment a whole number of
+// 256-wide groups, which the rotation keeps within a warp -- or false.
 template <int PRE>
 bool quant_rot_dispatch(int64_t K, const void *x, const void *s1, const void *sh, const void *gelu, int8_t *q,
                         float *sc, int64_t rows, int64_t rpg, cudaStream_t s, int *rc) {
-#define WF_QT(N) do { *rc = launch_quant_reg<PRE, N, 1, true>(x, s1, sh, gelu, q, sc, rows, rpg, s); return true; } while (0)
+#define WF_QT(N, W) do { *rc = launch_quant_reg<PRE, N, W, true>(x, s1, sh, gelu, q, sc, rows, rpg, s); return true; } while (0)
     if (K % 256 != 0) return false;
     switch (K / 256) {
-        case 1: WF_QT(1); case 2: WF_QT(2); case 3: WF_QT(3); case 4: WF_QT(4); case 5: WF_QT(5); case 6: WF_QT(6);
-        case 8: WF_QT(8); case 10: WF_QT(10); case 12: WF_QT(12); case 16: WF_QT(16); case 20: WF_QT(20);
-        case 24: WF_QT(24);
+        case 1: WF_QT(1, 1); case 2: WF_QT(2, 1); case 3: WF_QT(3, 1); case 4: WF_QT(4, 1); case 5: WF_QT(5, 1);
+        case 6: WF_QT(6, 1); case 8: WF_QT(8, 1); case 10: WF_QT(10, 1); case 12: WF_QT(12, 1); case 16: WF_QT(4, 4);
+        case 20: WF_QT(5, 4); case 24: WF_QT(6, 4);
+        default: break;
+    }
+    if (K % 2048 != 0) return false;
+    switch (K / 2048) {
+        case 4: WF_QT(4, 8); case 5: WF_QT(5, 8); case 6: WF_QT(6, 8); case 8: WF_QT(8, 8); case 10: WF_QT(10, 8);
+        case 12: WF_QT(12, 8); case 16: WF_QT(16, 8);
         default: return false;
     }
 #undef WF_QT
 }
 
-// The register kernel's (NCH, WPR) for K, or false: one warp per row up to K = 6144, eight from K = 8192 to 32768.
+// The register kernel's (NCH, WPR) for K, or false: one warp per row up to K = 3072, four for K = 4096 / 5120 / 6144
+// (a fifth to a fifth less time than one warp holding the whole row: fewer registers per thread, more rows in
+// flight), eight from K = 8192 to 32768.
 template <int PRE>
 bool quant_reg_dispatch(int64_t K, const void *x, const void *s1, const void *sh, const void *gelu, int8_t *q,
                         float *sc, int64_t rows, int64_t rpg, cudaStream_t s, int *rc) {
@@ -1250,7 +1297,7 @@ bool quant_reg_dispatch(int64_t K, const void *x, const void *s1, const void *sh
     switch (K / 256) {
         case 1: WF_QR(1, 1); case 2: WF_QR(2, 1); case 3: WF_QR(3, 1); case 4: WF_QR(4, 1); case 5: WF_QR(5, 1);
         case 6: WF_QR(6, 1); case 8: WF_QR(8, 1); case 10: WF_QR(10, 1); case 12: WF_QR(12, 1);
-        case 16: WF_QR(16, 1); case 20: WF_QR(20, 1); case 24: WF_QR(24, 1);
+        case 16: WF_QR(4, 4); case 20: WF_QR(5, 4); case 24: WF_QR(6, 4);
         default: break;
     }
     if (K % 2048 != 0) return false;

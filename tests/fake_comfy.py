@@ -53,10 +53,21 @@ def _quantise(x2, convrot):
     return torch.from_numpy(q), torch.from_numpy(sc)
 
 
+# Set by a benchmark: on CUDA tensors the stand-in int8 linear then runs as a kernel would -- this library's
+# quantiser and W8A8 GEMM, the place of comfy_kitchen's compiled one -- instead of the exact float64 product the tests
+# compare against.
+FAST_INT8 = False
+
+
 def kitchen_int8_linear(x, qt, bias=None):
     """bf16(((float(q(x) @ w_q^T)) * x_s) * w_s) with q(x) the per-token quantisation of _quantise (ConvRot when
     the weight says so) and the product summed exactly."""
     w_q, w_s = TensorWiseINT8Layout.get_plain_tensors(qt)
+    if FAST_INT8 and x.is_cuda:
+        import importlib
+        fi = importlib.import_module("comfyui-weightferry_b200.enhancers.fused_int8")
+        y = fi.int8_linear(x, w_q, w_s, rotate=qt._params.convrot)
+        return y + bias if bias is not None else y
     k = x.shape[-1]
     q, sc = _quantise(x.reshape(-1, k), qt._params.convrot)
     acc = q.double() @ w_q.double().t()           # exact: integer sums far below 2^53

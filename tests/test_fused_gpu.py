@@ -307,11 +307,11 @@ def test_fused_c_abi_rejections(cuda):
 
 @pytest.mark.parametrize("rotate", [0, 1])
 @pytest.mark.parametrize("pre", [0, 1, 2])
-@pytest.mark.parametrize("k", [256, 768, 1280, 2048, 5120, 6144, 8192, 20480, 1000])
+@pytest.mark.parametrize("k", [256, 768, 1280, 2048, 4096, 5120, 6144, 8192, 20480, 1000])
 def test_quant_rows_register_kernel_matches_shared_kernel(cuda, pre, k, rotate):
-    """The register-resident quantiser (16-byte aligned operands, K = 256 * n for the sizes it takes; with the
-    ConvRot Hadamard up to K = 6144) and the shared-memory one (any K % 4 == 0; reached here through an x that is only
-    8-byte aligned) give the same bits."""
+    """The register-resident quantiser (16-byte aligned operands, K = 256 * n for the sizes it takes: one warp per row
+    up to K = 3072, four for 4096 - 6144, eight from 8192, with or without the ConvRot Hadamard) and the shared-memory
+    one (any K % 4 == 0; reached here through an x that is only 8-byte aligned) give the same bits."""
     import torch
     if rotate and k % 256:
         pytest.skip("the rotation needs K % 256 == 0")
