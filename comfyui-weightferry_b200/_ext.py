@@ -115,9 +115,40 @@ def check(status, what):
 
 
 def stream_of(device):
-    """cudaStream_t of the current PyTorch stream on `device`, as an integer for ctypes."""
+    """cudaStream_t of the current PyTorch stream on `device` (a torch.device or an index), as an integer for
+    ctypes. Read through PyTorch's raw accessor where it exists: the public current_stream() costs a few
+    microseconds of Python per call, which a block's dozens of launches would pay each time."""
     import torch
-    return torch.cuda.current_stream(device).cuda_stream
+    idx = device.index if isinstance(device, torch.device) else device
+    if idx is None:
+        idx = torch.cuda.current_device()
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
+
+
+class _Same:
+    """A no-op device guard (the tensor's device is already the current one)."""
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+_SAME = _Same()
+
+
+def on_device(device):
+    """Context manager that makes `device` current for a launch: torch.cuda.device(device) when another device is
+    current, else a shared no-op (the common case costs one device query)."""
+    import torch
+    idx = device.index if isinstance(device, torch.device) else device
+    if idx is None or idx == torch.cuda.current_device():
+        return _SAME
+    return torch.cuda.device(idx)
 
 
 def dtype_code(dtype):

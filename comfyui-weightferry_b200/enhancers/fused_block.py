@@ -101,7 +101,7 @@ def gated_residual(x, gate_rows, o, rows_per_group, out=None):
             and gate_rows.shape[0] * rows_per_group >= n):
         if out is None:
             out = torch.empty_like(x)
-        with torch.cuda.device(x.device):
+        with _ext.on_device(x.device):
             rc = _ext.lib().wf_gated_residual(x.data_ptr(), gate_rows.data_ptr(), o.data_ptr(), out.data_ptr(), n, D,
                                               int(rows_per_group), _ext.stream_of(x.device))
         _ext.check(rc, "wf_gated_residual")

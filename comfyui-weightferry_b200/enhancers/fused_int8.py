@@ -157,7 +157,7 @@ def gemm(x_q, w_q, x_s, ws, out=None, acc=None):
     n = w_q.shape[0]
     if out is None:
         out = torch.empty((m, n), dtype=torch.bfloat16, device=x_q.device)
-    with torch.cuda.device(x_q.device):
+    with _ext.on_device(x_q.device):
         rc = _ext.lib().wf_w8a8_gemm(x_q.data_ptr(), w_q.data_ptr(), x_s.data_ptr(), ws.data_ptr(), out.data_ptr(),
                                      0 if acc is None else acc.data_ptr(), m, n, k, _ext.stream_of(x_q.device))
     _ext.check(rc, "wf_w8a8_gemm")
@@ -172,7 +172,7 @@ def gemm_residual(x_q, w_q, x_s, ws, resid, gate, rows_per_group, out=None):
     n = w_q.shape[0]
     if out is None:
         out = torch.empty((m, n), dtype=torch.bfloat16, device=x_q.device)
-    with torch.cuda.device(x_q.device):
+    with _ext.on_device(x_q.device):
         rc = _ext.lib().wf_w8a8_gemm_residual(x_q.data_ptr(), w_q.data_ptr(), x_s.data_ptr(), ws.data_ptr(),
                                               resid.data_ptr(), gate.data_ptr(), int(rows_per_group), out.data_ptr(),
                                               m, n, k, _ext.stream_of(x_q.device))

@@ -40,7 +40,7 @@ class _Launcher:
 
 def _mod(a, s1, h, o, n_cols, rows_per_group, **_triton_kw):
     rows = a.numel() // n_cols
-    with torch.cuda.device(a.device):
+    with _ext.on_device(a.device):
         rc = _ext.lib().wf_modulate(a.data_ptr(), s1.data_ptr(), h.data_ptr(), o.data_ptr(), rows, int(n_cols),
                                     int(rows_per_group), _stream(a))
     _ext.check(rc, "wf_modulate")
@@ -48,14 +48,14 @@ def _mod(a, s1, h, o, n_cols, rows_per_group, **_triton_kw):
 
 def _lnmod(x, s1, h, o, rows_per_group, eps, K, **_triton_kw):
     rows = x.numel() // K
-    with torch.cuda.device(x.device):
+    with _ext.on_device(x.device):
         rc = _ext.lib().wf_ln_modulate(x.data_ptr(), s1.data_ptr(), h.data_ptr(), o.data_ptr(), rows, int(K),
                                        int(rows_per_group), float(eps), _stream(x))
     _ext.check(rc, "wf_ln_modulate")
 
 
 def _rms128(x, w, o, n_rows, eps, RS=0, **_triton_kw):  # noqa: N803 -- the reference's keyword
-    with torch.cuda.device(x.device):
+    with _ext.on_device(x.device):
         rc = _ext.lib().wf_rms_norm_128(x.data_ptr(), w.data_ptr(), _ext.dtype_code(w.dtype), o.data_ptr(),
                                         int(n_rows), float(eps), _stream(x))
     _ext.check(rc, "wf_rms_norm_128")
@@ -69,7 +69,7 @@ def _quant_row(x, s, h, q, sc, rows_per_group, eps, K, PRE, ROTATE=True, **_trit
     table = s if PRE == PRE_GELU else None
     s1 = s if PRE in (PRE_MOD, PRE_LNMOD) else None
     sh = h if PRE in (PRE_MOD, PRE_LNMOD) else None
-    with torch.cuda.device(x.device):
+    with _ext.on_device(x.device):
         rc = _ext.lib().wf_quant_rows(x.data_ptr(), _p(s1), _p(sh), _p(table), q.data_ptr(), sc.data_ptr(), rows,
                                       int(K), int(rows_per_group), float(eps), int(PRE), int(bool(ROTATE)),
                                       _stream(x))

@@ -67,7 +67,7 @@ def _raw_bytes(data):
 def _launch(raw, res, n, qtype, mid, out):
     """One wf_dequant_gguf launch on the current stream of raw's device."""
     lib = _ext.lib()
-    with torch.cuda.device(raw.device):
+    with _ext.on_device(raw.device):
         rc = lib.wf_dequant_gguf(raw.data_ptr(), raw.numel(), res.data_ptr(), n, int(qtype), _DT[mid], _DT[out],
                                  _ext.stream_of(raw.device))
     _ext.check(rc, "wf_dequant_gguf")
@@ -138,7 +138,7 @@ def dequantize_many(items, qtype, mid_dtype=None, out_dtype=None):
         res = torch.empty(tuple(oshape), dtype=out, device=dev)
         tasks[i].src, tasks[i].dst, tasks[i].n_values = raw.data_ptr(), res.data_ptr(), res.numel()
         outs.append(res)
-    with torch.cuda.device(dev):
+    with _ext.on_device(dev):
         rc = _ext.lib().wf_dequant_gguf_batch(tasks, len(items), q, _DT[mid], _DT[out], _ext.stream_of(dev))
     _ext.check(rc, "wf_dequant_gguf_batch")
     return outs
@@ -228,7 +228,7 @@ def _add_loras(raw, res, loras, qtype, mid):
     lib = _ext.lib()
     mode = _factor_mode()
     n = res.numel()
-    with torch.cuda.device(dev):
+    with _ext.on_device(dev):
         for i, (up, down, sa) in enumerate(loras):
             mat1 = _factor(up, dev, mode)  # comfy's cast_to_device(v[0], device, float32)
             mat2 = _factor(down, dev, mode)

@@ -31,7 +31,7 @@ def rms_rope(x, f, w, eps):
     reference's reproduction."""
     b, L, h, d = x.shape
     out = torch.empty_like(x)
-    with torch.cuda.device(x.device):
+    with _ext.on_device(x.device):
         rc = _ext.lib().wf_rms_rope128(x.data_ptr(), f.data_ptr(), f.stride(1), f.stride(3), f.stride(4), f.stride(5),
                                        w.data_ptr(), _ext.dtype_code(w.dtype), out.data_ptr(), b, L, h, float(eps),
                                        _ext.stream_of(x.device))
@@ -46,7 +46,7 @@ def rms_rope_pair(q, k, f, q_scale, k_scale, eps):
         return rms_rope(q, f, q_scale, eps), rms_rope(k, f, k_scale, eps)
     b, L, h, d = q.shape
     qo, ko = torch.empty_like(q), torch.empty_like(k)
-    with torch.cuda.device(q.device):
+    with _ext.on_device(q.device):
         rc = _ext.lib().wf_rms_rope128_pair(q.data_ptr(), k.data_ptr(), f.data_ptr(), f.stride(1), f.stride(3),
                                             f.stride(4), f.stride(5), q_scale.data_ptr(), k_scale.data_ptr(),
                                             _ext.dtype_code(q_scale.dtype), qo.data_ptr(), ko.data_ptr(), b, L, h,
