@@ -119,6 +119,8 @@ def stream_of(device):
     ctypes. Read through PyTorch's raw accessor where it exists: the public current_stream() costs a few
     microseconds of Python per call, which a block's dozens of launches would pay each time."""
     import torch
+    if isinstance(device, str):
+        device = torch.device(device)
     idx = device.index if isinstance(device, torch.device) else device
     if idx is None:
         idx = torch.cuda.current_device()
@@ -145,6 +147,8 @@ def on_device(device):
     """Context manager that makes `device` current for a launch: torch.cuda.device(device) when another device is
     current, else a shared no-op (the common case costs one device query)."""
     import torch
+    if isinstance(device, str):
+        device = torch.device(device)
     idx = device.index if isinstance(device, torch.device) else device
     if idx is None or idx == torch.cuda.current_device():
         return _SAME
