@@ -1222,6 +1222,102 @@ __global__ void __launch_bounds__(128) quant_lnmod_kernel(const __nv_bfloat16 *_
     }
 }
 
+// The quantiser with the pending LayerNorm + modulate and the ConvRot rotation (pre 3, rotate), K = 512 * NV: the
+// row's statistics and modulation as quant_lnmod_kernel computes them (PyTorch's vectorised layout over the 128
+// threads), the modulated bf16 row then handed to the four warps through shared memory, each warp rotating whole
+// 256-value groups in registers (hadamard256, 8 values per lane; groups w, w + 4, ...), the row's absmax over the
+// rotated float values, each value quantised from its bf16 rounding -- bit for bit quant_rows_kernel<3, true>, whose
+// four shared-memory Hadamard stages and one row per CTA this replaces.
+template <int NV>
+__global__ void __launch_bounds__(128) quant_lnmod_rot_kernel(const __nv_bfloat16 *__restrict__ x,
+                                                              const __nv_bfloat16 *__restrict__ s1,
+                                                              const __nv_bfloat16 *__restrict__ sh,
+                                                              int8_t *__restrict__ q, float *__restrict__ scale_out,
+                                                              int64_t rows, int64_t K, int64_t rows_per_group,
+                                                              float eps, int pf) {
+    constexpr int G = 2 * NV;        // 256-value groups of the row
+    constexpr int NG = (G + 3) / 4;  // groups per warp (warps past the last group of a round take none)
+    __shared__ __align__(16) uint32_t srow[NV * 256];  // the modulated row as bf16 pairs
+    __shared__ float red[2][16];
+    __shared__ float amax_w[2][4];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    allow_dependents();
+    int64_t row = blockIdx.x;
+    if (row >= rows) return;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // a programmatic dependent, as quant_rows_reg_body
+    uint2 raw[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) raw[j] = __ldg(reinterpret_cast<const uint2 *>(x + row * K) + t + 128 * j);
+    int parity = 0;
+    for (; row < rows; row += gridDim.x, parity ^= 1) {
+        float v[NV * 4];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) unpack4(raw[j], v + 4 * j);
+        const int64_t nrow = row + gridDim.x;
+        if (nrow < rows) {
+#pragma unroll
+            for (int j = 0; j < NV; ++j) raw[j] = __ldg(reinterpret_cast<const uint2 *>(x + nrow * K) + t + 128 * j);
+        }
+        if (pf > 0 && t == 0 && nrow + pf < rows)  // as in ln_modulate_kernel
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(x + (nrow + pf) * K),
+                         "r"(static_cast<uint32_t>(K * 2)) : "memory");
+        const int64_t goff =
+            static_cast<int64_t>(static_cast<uint32_t>(row) / static_cast<uint32_t>(rows_per_group)) * K;
+        float mu, var;
+        ln_stats_n<NV * 4>(v, K, mu, var, red[parity]);
+        const float rstd = rsqrt_approx(__fadd_rn(var, eps));
+        const uint64_t neg_mu = f2pack(-mu, -mu), rstd2 = f2pack(rstd, rstd);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const uint2 sr = __ldg(reinterpret_cast<const uint2 *>(s1 + goff) + t + 128 * j);
+            const uint2 hr = __ldg(reinterpret_cast<const uint2 *>(sh + goff) + t + 128 * j);
+            const uint64_t a = mul2(add2(f2pack(v[4 * j], v[4 * j + 1]), neg_mu), rstd2);
+            const uint64_t b = mul2(add2(f2pack(v[4 * j + 2], v[4 * j + 3]), neg_mu), rstd2);
+            // values 4t + 512 j .. + 3 of the row: words 2t + 256 j, + 1
+            *reinterpret_cast<uint2 *>(srow + 2 * t + 256 * j) =
+                make_uint2(mod_bf16x2(pack2(f2lo(a), f2hi(a)), sr.x, hr.x),
+                           mod_bf16x2(pack2(f2lo(b), f2hi(b)), sr.y, hr.y));
+        }
+        __syncthreads();  // the modulated row is in shared memory
+        uint4 vv[NG];
+        float amax = 0.f;
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+            const int g = warp + 4 * gi;
+            if (g < G) {  // uniform over the warp: every lane takes part in the shuffles
+                vv[gi] = reinterpret_cast<const uint4 *>(srow)[32 * g + lane];  // values 256 g + 8 lane .. + 7
+                const uint32_t w[4] = {vv[gi].x, vv[gi].y, vv[gi].z, vv[gi].w};
+                float f[8];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    f[2 * k] = bf_lo(w[k]);
+                    f[2 * k + 1] = bf_hi(w[k]);
+                }
+                hadamard256(f, lane);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(f[k]));
+                vv[gi] = make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+            }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+        if (lane == 0) amax_w[parity][warp] = amax;
+        __syncthreads();  // every warp's absmax; every warp is done reading this row from shared memory
+        amax = fmaxf(fmaxf(amax_w[parity][0], amax_w[parity][1]), fmaxf(amax_w[parity][2], amax_w[parity][3]));
+        amax = fminf(amax, 3.38953139e38f);
+        const float scale = fmaxf(div_full(amax, 127.0f), 1.0e-30f);
+        if (t == 0) scale_out[row] = scale;
+        const float sb = r16(scale);
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+            const int g = warp + 4 * gi;
+            if (g < G)
+                *reinterpret_cast<uint2 *>(q + row * K + 256 * g + 8 * lane) =
+                    make_uint2(quant_quad(vv[gi].x, vv[gi].y, sb), quant_quad(vv[gi].z, vv[gi].w, sb));
+        }
+    }
+}
+
 // L2 prefetch distance of the row-walking quantisers past their staged next row, in quarter waves
 // (WEIGHTFERRY_QUANT_PREFETCH 0 - 9, 0 = off; default 1)
 int row_prefetch() {
@@ -1229,12 +1325,19 @@ int row_prefetch() {
     return w;
 }
 
-template <int NV>
+template <int NV, bool ROT>
+constexpr auto quant_lnmod_kernel_for() {
+    if constexpr (ROT) return quant_lnmod_rot_kernel<NV>;
+    else return quant_lnmod_kernel<NV>;
+}
+
+template <int NV, bool ROT = false>
 int launch_quant_lnmod(const void *x, const void *s1, const void *sh, int8_t *q, float *sc, int64_t rows, int64_t K,
                        int64_t rpg, float eps, cudaStream_t s) {
-    const int g = persistent_grid<quant_lnmod_kernel<NV>>(128, 0, rows);
+    constexpr auto kern = quant_lnmod_kernel_for<NV, ROT>();
+    const int g = persistent_grid<kern>(128, 0, rows);
     const int pf = static_cast<int>(static_cast<int64_t>(g) * row_prefetch() / 4);
-    const cudaError_t e = launch_pdl(quant_lnmod_kernel<NV>, g, 128, s, static_cast<const __nv_bfloat16 *>(x),
+    const cudaError_t e = launch_pdl(kern, g, 128, s, static_cast<const __nv_bfloat16 *>(x),
                                      static_cast<const __nv_bfloat16 *>(s1), static_cast<const __nv_bfloat16 *>(sh),
                                      q, sc, rows, K, rpg, eps, pf);
     return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
@@ -1567,6 +1670,15 @@ extern "C" WF_API int wf_quant_rows(const void *x, const void *s1, const void *s
             WF_QL(1) WF_QL(2) WF_QL(3) WF_QL(4) WF_QL(5) WF_QL(6) WF_QL(7) WF_QL(8)
             WF_QL(9) WF_QL(10) WF_QL(11) WF_QL(12) WF_QL(13) WF_QL(14) WF_QL(15) WF_QL(16)
 #undef WF_QL
+            default: break;
+        }
+    }
+    if (rotate && pre == 3 && rows <= INT32_MAX && al(q, 8)) {
+        switch (K / 512) {  // K % 512 == 0 and K <= 8192 were checked above
+#define WF_QLR(NV) case NV: return launch_quant_lnmod<NV, true>(x, s1, shift, q, scale, rows, K, rows_per_group, eps, s);
+            WF_QLR(1) WF_QLR(2) WF_QLR(3) WF_QLR(4) WF_QLR(5) WF_QLR(6) WF_QLR(7) WF_QLR(8)
+            WF_QLR(9) WF_QLR(10) WF_QLR(11) WF_QLR(12) WF_QLR(13) WF_QLR(14) WF_QLR(15) WF_QLR(16)
+#undef WF_QLR
             default: break;
         }
     }

@@ -393,3 +393,38 @@ def test_quant_rows_lnmod_equals_lnmod_then_quant(cuda, k, rpg):
     torch.cuda.synchronize()
     assert torch.equal(q3, q0)
     assert torch.equal(s3.view(torch.int32), s0.view(torch.int32))
+
+
+@pytest.mark.parametrize("k,rpg", [(2048, 4096), (512, 3), (1536, 7), (5120, 100), (8192, 7)])
+def test_quant_rows_lnmod_rotated_register_equals_shared(cuda, k, rpg):
+    """The pending LayerNorm + modulate with the ConvRot rotation (pre 3, rotate): the register kernel (8-byte aligned
+    q) gives the bits of the shared-memory kernel (reached here through a q that is only 4-byte aligned) and of kernel
+    A's rows rotated and quantised by the plain rotated quantiser."""
+    import torch
+    ext = wf("_ext")
+    L = ext.lib()
+    g = torch.Generator(device="cuda").manual_seed(3 * k + rpg)
+    rows = 301
+    groups = (rows + rpg - 1) // rpg
+    x = (torch.randn((rows, k), device="cuda", generator=g) * 2 + 0.5).to(torch.bfloat16)
+    x[5] = 1.0                                                      # a constant row: variance 0
+    s1 = (1 + 0.1 * torch.randn((groups, k), device="cuda", generator=g)).to(torch.bfloat16)
+    sh = (0.1 * torch.randn((groups, k), device="cuda", generator=g)).to(torch.bfloat16)
+    st = ext.stream_of(x.device)
+    outs = []
+    for off in (0, 4):                                              # q 8-byte aligned, then only 4-byte aligned
+        buf = torch.empty((rows * k + 8,), dtype=torch.int8, device="cuda")
+        sc = torch.empty((rows,), dtype=torch.float32, device="cuda")
+        ext.check(L.wf_quant_rows(x.data_ptr(), s1.data_ptr(), sh.data_ptr(), None, buf.data_ptr() + off,
+                                  sc.data_ptr(), rows, k, rpg, 1e-6, 3, 1, st), "quant pre 3 rotate")
+        outs.append((buf[off:off + rows * k].clone(), sc))
+    y = torch.empty_like(x)
+    ext.check(L.wf_ln_modulate(x.data_ptr(), s1.data_ptr(), sh.data_ptr(), y.data_ptr(), rows, k, rpg, 1e-6, st), "ln")
+    q0 = torch.empty((rows * k,), dtype=torch.int8, device="cuda")
+    s0 = torch.empty((rows,), dtype=torch.float32, device="cuda")
+    ext.check(L.wf_quant_rows(y.data_ptr(), None, None, None, q0.data_ptr(), s0.data_ptr(), rows, k, 1, 0.0, 0, 1, st),
+              "quant pre 0 rotate")
+    torch.cuda.synchronize()
+    for q, sc in outs[1:] + [(q0, s0)]:
+        assert torch.equal(outs[0][0], q)
+        assert torch.equal(outs[0][1].view(torch.int32), sc.view(torch.int32))
