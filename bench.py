@@ -705,6 +705,33 @@ def kernel_breakdown(torch, step, dist):
     return every
 
 
+def kernels_by_name(torch, fn, reps=5, top=14):
+    """GPU time per kernel name of `reps` calls of fn (torch.profiler's CUDA activity), in ms per call, largest
+    first: [(name, launches per call, ms per call), ...] for the `top` largest, plus the total."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+    agg = {}
+    for ev in prof.events():
+        dt = getattr(ev, "device_time_total", None)
+        if dt is None:
+            dt = getattr(ev, "cuda_time_total", 0.0)
+        if not dt or ev.device_type is None or "cuda" not in str(ev.device_type).lower():
+            continue
+        name = ev.name
+        if "memcpy" in name.lower() or "memset" in name.lower():
+            continue
+        a = agg.setdefault(name[:110], [0, 0.0])
+        a[0] += 1
+        a[1] += dt
+    rows = sorted(agg.items(), key=lambda kv: -kv[1][1])
+    out = [(name, c // reps, round(t / reps / 1e3, 4)) for name, (c, t) in rows[:top]]
+    return {"kernels": out, "total_ms": round(sum(t for _, t in agg.values()) / reps / 1e3, 4)}
+
+
 def stack_measure(torch, world, rank, dist, blocks, steps, warmup, slots=3, e2e=False, profile=False,
                   parallel="sp"):
     """a Cosmos-Predict2-14B-shaped stack of `blocks` blocks, Q8_0 weights in pinned host RAM streamed
@@ -1031,11 +1058,21 @@ def run_block(torch, args, world, rank, dist):
         st8 = fb.stats(reset=True)
         fb.install(())
         i8_ms, _ = timed(blk8, parts)
-        del blk8
+    breakdown = None
+    if args.profile:  # (outside the timed runs and the clock record)
+        breakdown = {}
+        for name, w in (("bf16", "bf16"), ("int8_convrot", "int8")):
+            b = blk8 if w == "int8" else fake_comfy.build_block(p2, "bf16", device=x.device, **dims)
+            fb.install(parts)
+            with torch.no_grad():
+                breakdown[name] = kernels_by_name(torch, lambda: b(x, emb, ctx, rope, lora_t, None, {}))
+            fb.install(())
+            del b
+    del blk8
     d = (got.float() - ref.float()).abs()
     fake_comfy.unregister()
     return {"unpatched_ms": max_over_ranks(torch, dist, un_ms), "fused_ms": max_over_ranks(torch, dist, fu_ms),
-            "int8_fused_ms": max_over_ranks(torch, dist, i8_ms), "int8_stats": st8,
+            "int8_fused_ms": max_over_ranks(torch, dist, i8_ms), "int8_stats": st8, "breakdown": breakdown,
             "rel_max_diff": float(d.max() / ref.float().abs().max()), "clk": clk.summary(), "n": n}
 
 
@@ -1059,9 +1096,85 @@ def finish_block(torch, args, world, rank, dist, r):
                        "speedup_int8_vs_unpatched_bf16": round(r["unpatched_ms"] / r["int8_fused_ms"], 3),
                        "int8_parts_used": r["int8_stats"],
                        "bf16_fused_vs_unpatched_rel_max_diff": round(r["rel_max_diff"], 5),
-                       "reference_figure": "fused Anima block 22.1 vs 30.3 ms per block (x1.37), RTX 4060"},
+                       "reference_figure": "fused Anima block 22.1 vs 30.3 ms per block (x1.37), RTX 4060",
+                       "kernel_ms_per_forward": r["breakdown"]},
             "roofline": None, "cpu_baseline": None, "e2e": None, "gpu_launches": None, "clocks": r["clk"]}),
               flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+QUANT_WIDTHS = (2048, 4096, 5120, 6144, 8192)
+QUANT_MODES = (("plain", 0, 0), ("gelu", 1, 0), ("convrot", 0, 1), ("convrot_gelu", 1, 1), ("lnmod", 3, 0),
+               ("lnmod_convrot", 3, 1))
+
+
+def run_quant(torch, args, world, rank, dist):
+    """The int8 per-token quantiser (wf_quant_rows) on 8192 rows of each width in QUANT_WIDTHS, in each mode of
+    QUANT_MODES (pre none / GELU table / pending LayerNorm + modulate, with and without the ConvRot rotation), timed
+    as a run of 8 * steps launches over 8 rotating inputs (larger than L2 from K = 2048 on) between two events."""
+    ext = _pkg("_ext")
+    fi = _pkg("enhancers.fused_int8")
+    lib = ext.lib()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = ext.stream_of(dev)
+    gelu = fi._gelu_table(dev)
+    rows, n_sets = 8192, 8
+    res = {}
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for K in QUANT_WIDTHS:
+            g = torch.Generator(device=dev)
+            g.manual_seed(20261201 + K + rank)
+            xs = [(torch.randn((rows, K), device=dev, generator=g) * 2).to(torch.bfloat16) for _ in range(n_sets)]
+            s1 = (1 + 0.1 * torch.randn((2, K), device=dev, generator=g)).to(torch.bfloat16)
+            sh = (0.1 * torch.randn((2, K), device=dev, generator=g)).to(torch.bfloat16)
+            q = torch.empty((rows, K), dtype=torch.int8, device=dev)
+            sc = torch.empty((rows,), dtype=torch.float32, device=dev)
+            for name, pre, rot in QUANT_MODES:
+                def launch(i, pre=pre, rot=rot):
+                    ext.check(lib.wf_quant_rows(xs[i % n_sets].data_ptr(), s1.data_ptr() if pre == 3 else None,
+                                                sh.data_ptr() if pre == 3 else None,
+                                                gelu.data_ptr() if pre == 1 else None, q.data_ptr(), sc.data_ptr(),
+                                                rows, K, 4096, 1e-6, pre, rot, st), "wf_quant_rows")
+                for i in range(2 * n_sets):
+                    launch(i)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                n = n_sets * max(args.steps, 3)
+                e0.record()
+                for i in range(n):
+                    launch(i)
+                e1.record()
+                torch.cuda.synchronize()
+                res[f"{K}_{name}"] = max_over_ranks(torch, dist, e0.elapsed_time(e1) * 1e3 / n)
+            del xs
+    return {"us": res, "clk": clk.summary(), "rows": rows, "launches": int(sum_over_ranks(
+        torch, dist, len(res) * (n + 2 * n_sets)))}
+
+
+def finish_quant(torch, args, world, rank, dist, r):
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        peak, kind = measured_peaks()
+        us = r["us"]
+        base = us["2048_plain"]
+        nbytes = r["rows"] * 2048 * 3 + r["rows"] * 4  # x read, int8 written, scales
+        table = {K: {name: round(us[f"{K}_{name}"], 2) for name, _, _ in QUANT_MODES} for K in QUANT_WIDTHS}
+        print(json.dumps({
+            "metric": "int8 per-token quantiser us per launch (8192 x 2048, plain)", "value": round(base, 2),
+            "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(base / 1e3, 5),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, int8 out",
+            "data": "synthetic (seeded)",
+            "config": {"workload": "wf_quant_rows on 8192 rows, every width and mode (us per launch)",
+                       "us_per_launch": table, "rows_per_modulation_group": 4096,
+                       "l2": "8 rotating inputs (128 MB to 1 GB together); no flush"},
+            "roofline": {"bound": "hbm", "achieved": round(nbytes / base / 1e3, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(nbytes / base / 1e3 / peak, 4), "traffic": None,
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})",
+                         "kernel": "quant_rows_plain_kernel<0, 8> (8192 x 2048)"},
+            "cpu_baseline": None, "e2e": None, "gpu_launches": r["launches"], "clocks": r["clk"]}), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -1434,7 +1547,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="sweep",
-                    choices=["sweep", "q8", "q4k", "w8a8", "stack", "prologue", "formats", "lora", "ssd", "block"])
+                    choices=["sweep", "q8", "q4k", "w8a8", "stack", "prologue", "formats", "lora", "ssd", "block",
+                             "quant"])
     ap.add_argument("--ssd-blocks", type=int, default=8, help="ssd: blocks in the cache file")
     ap.add_argument("--slots", type=int, default=3, help="stack: GPU slots of the streaming ring")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -1445,7 +1559,8 @@ def main():
                     help="stack over N GPUs: sp = whole blocks per rank on its token rows, weights gathered; tp = "
                          "tensor parallel")
     ap.add_argument("--profile", action="store_true",
-                    help="stack: GPU time per kind of kernel of one extra forward (torch.profiler), every rank")
+                    help="stack: GPU time per kind of kernel of one extra forward (torch.profiler), every rank; "
+                         "block: GPU time per kernel of five extra forwards")
     ap.add_argument("--blocks", type=int, default=36, help="sweep: checkpoint blocks per rank (36 = Cosmos-14B)")
     ap.add_argument("--stack-blocks", type=int, default=36,
                     help="sweep: blocks of the streamed-stack sub-record timed after the sweep (0: none)")
@@ -1475,6 +1590,8 @@ def main():
         return finish_w8a8(torch, args, world, rank, dist, run_w8a8(torch, args, world, rank, dist))
     elif args.workload == "block":
         return finish_block(torch, args, world, rank, dist, run_block(torch, args, world, rank, dist))
+    elif args.workload == "quant":
+        return finish_quant(torch, args, world, rank, dist, run_quant(torch, args, world, rank, dist))
     else:
         r = run_single_weight(torch, args, world, rank, dist, args.workload)
     peak, peak_kind = measured_peaks()
