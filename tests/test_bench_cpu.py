@@ -28,9 +28,16 @@ def test_command_line_lists_every_workload():
     out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--help"], capture_output=True, text=True,
                          timeout=120, cwd=REPO)
     assert out.returncode == 0, out.stderr
-    for w in ("sweep", "q8", "q4k", "w8a8", "stack", "prologue", "formats", "lora", "ssd"):
+    for w in ("sweep", "q8", "q4k", "w8a8", "stack", "prologue", "formats", "lora", "ssd", "block", "quant"):
         assert w in out.stdout
     assert "--impl" in out.stdout and "--ssd-blocks" in out.stdout
+
+
+def test_quant_workload_covers_every_mode_once():
+    b = _bench()
+    assert [m for m, _, _ in b.QUANT_MODES] == ["plain", "gelu", "convrot", "convrot_gelu", "lnmod", "lnmod_convrot"]
+    assert {(pre, rot) for _, pre, rot in b.QUANT_MODES} == {(0, 0), (1, 0), (0, 1), (1, 1), (3, 0), (3, 1)}
+    assert all(k % 512 == 0 and k <= 8192 for k in b.QUANT_WIDTHS)  # every mode takes every width
 
 
 def test_gguf_geometry_matches_the_library_and_the_oracle():
