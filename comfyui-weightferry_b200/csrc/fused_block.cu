@@ -1529,8 +1529,8 @@ bool rope_v2() {
     return v2;
 }
 
-// rows per half-warp in flight in rms_rope_v2_kernel (WEIGHTFERRY_ROPE_ROWS 2 / 4 / 8; measured at configs[3], q and
-// k of (2, 4096, 16, 128): 2 rows 29.0 us, 4 rows 27.4 us)
+// rows per half-warp in flight in rms_rope_v2_kernel (WEIGHTFERRY_ROPE_ROWS 2 / 4 / 8; measured on q and k of
+// (2, 4096, 16, 128) before the L2 prefetch: 2 rows 29.0 us, 4 rows 27.4 us, 8 rows 29.0 us)
 int rope_rows() {
     static const int r = [] {
         const int d = env_digit("WEIGHTFERRY_ROPE_ROWS", 4);
