@@ -512,7 +512,8 @@ def run_w8a8(torch, args, world, rank, dist):
         lib_ms = tot / 5
     except Exception:  # noqa: BLE001 -- context only
         lib_ms = None
-    sustained = w8a8_sustained(torch, lib, ext, xq, wq, xs, ws, y, stream, ops)
+    sustained = w8a8_sustained(torch, lib, ext, xq, wq, xs, ws, y, stream, ops, args.sustained_seconds) \
+        if args.sustained_seconds > 0 else {}
     e2e = None
     if not args.no_e2e:
         e2e = e2e_w8a8(torch, fi, x, wq, ws, dev, args)
@@ -530,10 +531,10 @@ def run_w8a8(torch, args, world, rank, dist):
     }
 
 
-W8A8_SUSTAINED_S = 2.0  # seconds of back-to-back launches per kernel
+W8A8_SUSTAINED_S = 2.0  # seconds of back-to-back launches per kernel (--sustained-seconds)
 
 
-def w8a8_sustained(torch, lib, ext, xq, wq, xs, ws, y, stream, ops):
+def w8a8_sustained(torch, lib, ext, xq, wq, xs, ws, y, stream, ops, seconds=W8A8_SUSTAINED_S):
     """The GEMM and cuBLASLt's `_int_mm` (int32 out, no epilogue) on the same operands, each launched back to back for
     W8A8_SUSTAINED_S seconds -- the regime of a model's forward, where the 1 kW power cap sets the clock -- with the
     clocks sampled during each run. A single launch (the step above) runs at the boost clock instead."""
@@ -558,7 +559,7 @@ def w8a8_sustained(torch, lib, ext, xq, wq, xs, ws, y, stream, ops):
                 fn()
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            n = max(1, int(W8A8_SUSTAINED_S / 100e-6))
+            n = max(1, int(seconds / 100e-6))
             with ClockSampler(torch.cuda.current_device()) as clk:
                 e0.record(stream)
                 for _ in range(n):
@@ -1562,6 +1563,8 @@ def main():
                     help="stack: GPU time per kind of kernel of one extra forward (torch.profiler), every rank; "
                          "block: GPU time per kernel of five extra forwards")
     ap.add_argument("--blocks", type=int, default=36, help="sweep: checkpoint blocks per rank (36 = Cosmos-14B)")
+    ap.add_argument("--sustained-seconds", type=float, default=W8A8_SUSTAINED_S,
+                    help="w8a8: seconds of back-to-back launches of the GEMM and of cuBLASLt (0: skip)")
     ap.add_argument("--stack-blocks", type=int, default=36,
                     help="sweep: blocks of the streamed-stack sub-record timed after the sweep (0: none)")
     ap.add_argument("--stack-steps", type=int, default=3, help="sweep: timed forwards of the stack sub-record")
@@ -1653,7 +1656,9 @@ def sustained_record(sus):
     if "tops" in ours:
         rec["roofline"] = {"bound": "tensor", "achieved": ours["tops"], "peak": round(peak, 1), "unit": "TOPS",
                            "frac": round(ours["tops"] / peak, 4), "peak_source": src}
-    rec["note"] = (f"each kernel launched back to back for {W8A8_SUSTAINED_S} s on the same operands (L2-warm), "
+    if not sus:
+        return None
+    rec["note"] = ("each kernel launched back to back for --sustained-seconds on the same operands (L2-warm), "
                    "clocks sampled meanwhile; cuBLASLt writes int32 without the rescale")
     return rec
 
